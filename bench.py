@@ -1,0 +1,466 @@
+#!/usr/bin/env python
+"""Benchmark of the Q4 decode path on B200 — prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Workload (the metric's decode tokens/s): one greedy decode step = 24 x [RMSNorm
+(1+w) -> Q4 SwiGLU MLP 2048<->6144 -> residual] -> final RMSNorm -> Q4 lm_head 248320x2048 -> argmax,
+seeded synthetic weights (N(0,0.02) via the seeded generator) and embeddings (N(0,1)), batch B
+(default 1).  At N > 1 the step is tensor-parallel (column/row-split MLP + NCCL all-reduce per
+layer, vocabulary-sharded lm_head with a max-merge of packed keys): strong scaling.
+
+`value` is tokens/s of the whole job from CUDA events around K CUDA-graph replays (weights stream
+795.7 MB per step, > 126 MB L2: every step reads HBM).  `e2e` repeats the measurement through the
+public API with the step's embeddings copied from pinned host memory and the token ids read back
+to the host every step.  `roofline` covers the kernel family with the largest share of the step;
+`gemv` is the metric's first half (config 1: one 6144x2048 Q4 GEMV, bf16 x).
+
+--impl reference times the CPU restatement of the reference's Q4 path (oracle/, OpenMP on all host
+threads) on the same workload: MLX, which holds the reference's arithmetic, is absent here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "marlin-mlx_b200"))
+
+H, I, V, L = 2048, 6144, 248320, 24
+Q4_MAT = 7_077_888               # bytes of one 2048x6144 / 6144x2048 Q4 matrix (packed + scales + biases)
+LM_BYTES = 286_064_640           # 248320x2048 Q4
+STEP_WEIGHT_BYTES = 795_672_576  # 24 x 3 x Q4_MAT + LM_BYTES
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-family and batch sweeps")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampler (nvidia-smi, 200 ms) during the timed region
+# ---------------------------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# model construction (seeded; same seeds for every N so TP shards the same model)
+# ---------------------------------------------------------------------------------------------
+def build_model(mq, tp_rank: int, tp: int):
+    import torch
+    from marlin_q4 import tp as tpmod
+    layers = []
+    for l in range(L):
+        g = mq.quantize_weight(mq.synth_bf16((I, H), 1000 + 4 * l, 0.0, 0.02))
+        u = mq.quantize_weight(mq.synth_bf16((I, H), 1001 + 4 * l, 0.0, 0.02))
+        d = mq.quantize_weight(mq.synth_bf16((H, I), 1002 + 4 * l, 0.0, 0.02))
+        nw = mq.synth_bf16((H,), 1003 + 4 * l, 0.1, 0.02)
+        layer = mq.Layer(nw, g, u, d)
+        layers.append(tpmod.shard_layer(layer, tp_rank, tp) if tp > 1 else layer)
+    lm = mq.quantize_weight(mq.synth_bf16((V, H), 2000, 0.0, 0.02))
+    off = 0
+    if tp > 1:
+        lm, off = tpmod.shard_vocab(lm, tp_rank, tp)
+    torch.cuda.empty_cache()
+    fn = mq.synth_bf16((H,), 2001, 0.1, 0.02)
+    return layers, fn, lm, off
+
+
+def time_graph(torch, fn, reps: int, warm: int = 3) -> float:
+    """Capture fn() in a CUDA graph; return ms per replay over `reps` replays (CUDA events)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(warm):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import marlin_q4 as mq
+    from marlin_q4 import tp as tpmod
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    B = args.batch
+    layers, fn, lm, off = build_model(mq, rank, world)
+    h0 = mq.synth_bf16((B, H), 3000, 0.0, 1.0)
+
+    if world > 1:
+        step = tpmod.TPDecodeStep(layers, fn, lm, off, B)
+    else:
+        step = mq.DecodeStep(layers, fn, lm, B)
+
+    # capture the step in a CUDA graph (kernels + NCCL collectives)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step(h0)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out_ids, out_best, _ = step(h0)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = B / (ms / 1e3)
+
+    # e2e: public API with host buffers (H2D of embeddings, D2H of ids every step)
+    h_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    h_host.copy_(h0.cpu())
+    ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    for _ in range(3):
+        h0.copy_(h_host, non_blocking=True)
+        graph.replay()
+        ids_host.copy_(out_ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        h0.copy_(h_host, non_blocking=True)
+        graph.replay()
+        ids_host.copy_(out_ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()  # the host reads the token every step
+    e1.record()
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    del graph
+
+    pk = peaks()
+    extras, roof, gemv = {}, None, None
+    if not args.no_extras and world == 1:
+        # kernel families, each timed alone in a CUDA graph of back-to-back launches over all 24
+        # layers' weights (340 MB / 170 MB > L2), PDL on — as they run inside the step
+        hf = torch.empty((B, H), dtype=torch.float32, device=dev).copy_(h0.float())
+        act = torch.empty((B, I), dtype=torch.float32, device=dev).normal_()
+        res = torch.empty((B, H), dtype=torch.float32, device=dev)
+        ws = mq.LmHeadWorkspace(B, dev)
+
+        def fam_gateup():
+            for Lr in layers:
+                mq.gate_up_swiglu(hf, Lr.gate_proj, Lr.up_proj, norm_weight=Lr.post_attn_norm, out=act)
+
+        def fam_down():
+            for Lr in layers:
+                mq.matmul_residual(act, Lr.down_proj, hf, out=res)
+
+        def fam_lm():
+            for _ in range(4):
+                mq.lm_head_argmax(hf, lm, norm_weight=fn, workspace=ws)
+
+        reps = max(5, args.steps // 2)
+        t_gu = time_graph(torch, fam_gateup, reps) / L
+        t_dn = time_graph(torch, fam_down, reps) / L
+        t_lm = time_graph(torch, fam_lm, reps) / 4
+        fams = {
+            "gate_up_swiglu": {"launches_per_step": L, "us": t_gu * 1e3,
+                               "bytes": 2 * Q4_MAT + B * H * 4 + B * I * 4},
+            "down_residual": {"launches_per_step": L, "us": t_dn * 1e3,
+                              "bytes": Q4_MAT + B * I * 4 + 2 * B * H * 4},
+            "lm_head_argmax": {"launches_per_step": 1, "us": t_lm * 1e3, "bytes": LM_BYTES + B * H * 4 + B * 4},
+        }
+        for f in fams.values():
+            f["gbs"] = f["bytes"] / (f["us"] * 1e-6) / 1e9
+            f["frac_hbm"] = f["gbs"] / pk["hbm_gbs"]
+            f["share_us_per_step"] = f["us"] * f["launches_per_step"]
+        dom_name = max(fams, key=lambda k: fams[k]["share_us_per_step"])
+        dom = fams[dom_name]
+        traffic = None
+        tp_path = ROOT / "profiles" / "traffic.json"
+        if tp_path.exists():
+            traffic = json.loads(tp_path.read_text()).get(dom_name)
+        roof = {"bound": "hbm", "kernel": dom_name, "achieved": round(dom["gbs"], 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(dom["frac_hbm"], 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": dom["bytes"], "launch_us": round(dom["us"], 3),
+                "peak_source": pk["source"]}
+        extras["families"] = {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
+                              for k, v in fams.items()}
+
+        # config 1 GEMV: 6144x2048, bf16 x [1, 2048], over 24 distinct weight copies (170 MB > L2)
+        xb = mq.synth_bf16((1, H), 7, 0.0, 1.0)
+
+        def gemv_stream():
+            for Lr in layers:
+                mq.qmatmul(xb, Lr.gate_proj)
+
+        t_stream = time_graph(torch, gemv_stream, reps) / L
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        iso = []
+        for _ in range(20):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            mq.qmatmul(xb, layers[0].gate_proj)
+            b.record()
+            b.synchronize()
+            iso.append(a.elapsed_time(b))
+        t_iso = statistics.median(iso)
+        gb = Q4_MAT + H * 2 + I * 2
+        gemv = {"config": "C1: x bf16 [1,2048] . Q4 W[6144,2048]^T -> bf16 [1,6144]", "bytes": gb,
+                "stream_us": round(t_stream * 1e3, 3), "stream_gbs": round(gb / (t_stream * 1e-3) / 1e9, 1),
+                "stream_frac": round(gb / (t_stream * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                "isolated_us": round(t_iso * 1e3, 3), "isolated_gbs": round(gb / (t_iso * 1e-3) / 1e9, 1),
+                "isolated_frac": round(gb / (t_iso * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                "note": "stream = back-to-back launches over 24 weight copies (PDL); isolated = one launch after "
+                        "a 256 MB L2 flush, launch latency included"}
+        # batch sweep of the full step
+        sweep = {}
+        for bb in (8, 32):
+            if bb == B:
+                continue
+            st = mq.DecodeStep(layers, fn, lm, bb)
+            hb = mq.synth_bf16((bb, H), 3001, 0.0, 1.0)
+            msb = time_graph(torch, lambda: st(hb), max(5, args.steps // 4))
+            sweep[f"batch{bb}"] = {"ms_per_step": round(msb, 4), "tokens_per_s": round(bb / (msb / 1e3), 1)}
+            del st
+        extras["batch_sweep"] = sweep
+
+    # CPU baseline: the oracle (CPU restatement) on the host cores, bounded sample, rank 0 at N=1
+    cpu = None
+    if world == 1 and rank == 0:
+        cpu = cpu_baseline_from_device(layers, fn, lm, h0, B, args.cpu_seconds)
+
+    launches = args.steps * (2 * L + 1) if world == 1 else args.steps * (3 * L + 3)
+    line = {
+        "metric": "Q4 MLP+lm_head decode tokens/s (24-layer Q4 SwiGLU MLP stack + Q4 lm_head + argmax)",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4g64 weights; f32 activations as exact bf16x3 mma planes; f32 accumulate",
+        "data": "synthetic (seeded generator: weights N(0,0.02), norms N(0.1,0.02), embeddings N(0,1))",
+        "config": {"workload": "C5 decode step: 24 x [RMSNorm(1+w) -> Q4 SwiGLU MLP 2048<->6144 -> residual] + "
+                               "final RMSNorm + Q4 lm_head 248320x2048 + argmax",
+                   "batch": B, "tp": world, "layers": L, "hidden": H, "intermediate": I, "vocab": V,
+                   "weight_bytes_per_step": STEP_WEIGHT_BYTES,
+                   "l2": "no flush: 795.7 MB of weights per step > 126 MB L2",
+                   "parallelism": f"tp{world}" if world > 1 else "single"},
+        "clocks": ck,
+        "e2e": {"value": round(B / (e2e_ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * 4,
+                "path": "public API (CUDA graph of marlin_q4_decode_step / TP step) with pinned host embeddings in "
+                        "and token ids out every step, host sync per token"},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "gemv": gemv,
+        "cpu_baseline": cpu,
+        "step_hbm": {"gbs": round(STEP_WEIGHT_BYTES / max(world, 1) / (ms * 1e-3) / 1e9, 1),
+                     "frac": round(STEP_WEIGHT_BYTES / max(world, 1) / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)},
+    }
+    if extras:
+        line["extras"] = extras
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_from_device(layers, fn, lm, h0, B, seconds):
+    """Time the oracle's decode step on the host (all OpenMP threads) for a bounded number of steps."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import q4_oracle as qo
+    import torch
+
+    def u16(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    def hq(q):
+        return qo.Q4(q.weight.cpu().numpy().view(np.uint32), u16(q.scales), u16(q.biases))
+
+    C = qo.COracle()
+    hl = [(u16(Lr.post_attn_norm), hq(Lr.gate_proj), hq(Lr.up_proj), hq(Lr.down_proj)) for Lr in layers]
+    hlm, hfn, hh0 = hq(lm), u16(fn), u16(h0)
+    C.decode_step(hh0, hl, hfn, hlm)  # warm-up (page in)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        C.decode_step(hh0, hl, hfn, hlm)
+        n += 1
+        if time.perf_counter() - t0 > seconds or n >= 50:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(B * n / dt, 3), "unit": "tokens/s", "cores": C.num_threads(), "kind": "port",
+            "sample": f"{n} full decode steps (24 layers + lm_head) at batch {B}, {dt:.1f} s",
+            "label": "CPU restatement of the reference's Q4 path (oracle/q4_oracle.c, OpenMP), not MLX"}
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm: the CPU restatement on host cores
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import q4_oracle as qo
+    C = qo.COracle()
+    B = args.batch
+    layers = []
+    for l in range(L):
+        g = C.quantize(C.synth_bf16((I, H), 1000 + 4 * l, 0.0, 0.02))
+        u = C.quantize(C.synth_bf16((I, H), 1001 + 4 * l, 0.0, 0.02))
+        d = C.quantize(C.synth_bf16((H, I), 1002 + 4 * l, 0.0, 0.02))
+        layers.append((C.synth_bf16((H,), 1003 + 4 * l, 0.1, 0.02), g, u, d))
+    lm = C.quantize(C.synth_bf16((V, H), 2000, 0.0, 0.02))
+    fn = C.synth_bf16((H,), 2001, 0.1, 0.02)
+    h0 = C.synth_bf16((B, H), 3000, 0.0, 1.0)
+    for _ in range(args.warmup):
+        C.decode_step(h0, layers, fn, lm)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        C.decode_step(h0, layers, fn, lm)
+    dt = time.perf_counter() - t0
+    ms = dt / args.steps * 1e3
+    val = B / (ms / 1e3)
+    line = {
+        "impl": "reference",
+        "metric": "Q4 MLP+lm_head decode tokens/s (24-layer Q4 SwiGLU MLP stack + Q4 lm_head + argmax)",
+        "value": round(val, 4), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (CPU)", "data": "synthetic (same seeded generator and seeds as our arm)",
+        "config": {"workload": "C5 decode step: 24 x [RMSNorm(1+w) -> Q4 SwiGLU MLP 2048<->6144 -> residual] + "
+                               "final RMSNorm + Q4 lm_head 248320x2048 + argmax", "batch": B, "tp": world},
+        "cpu_baseline": {"value": round(val, 4), "unit": "tokens/s", "cores": C.num_threads(), "kind": "port",
+                         "sample": f"{args.steps} full decode steps at batch {B} after {args.warmup} warm-up"},
+        "e2e": {"value": round(val, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "MLX v0.25.2 (the reference's arithmetic) cannot be built here; this arm is the CPU "
+                "restatement oracle/q4_oracle.c on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

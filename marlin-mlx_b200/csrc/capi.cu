@@ -1,0 +1,300 @@
+// capi.cu — the extern "C" boundary declared in include/marlin_q4.h.
+//
+// Validates every argument before any launch, maps shapes onto the kernels' envelopes, and turns
+// CUDA launch failures into MARLIN_Q4_ERR_CUDA.  Never synchronises the host (except
+// marlin_q4_device_error, which is documented as synchronous) and never allocates.
+#include "marlin_q4.h"
+
+#include "q4_gemv.cuh"
+#include "q4_misc.cuh"
+
+#include <algorithm>
+#include <cstdint>
+
+namespace marlin {
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+bool g_pdl = true;
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return MARLIN_Q4_OK;
+    t_last_cuda_error = (int)e;
+    cudaGetLastError();  // clear the sticky-free launch error so later calls start clean
+    return MARLIN_Q4_ERR_CUDA;
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline bool valid_dtype(int32_t d) { return d == MARLIN_Q4_BF16 || d == MARLIN_Q4_F32; }
+inline size_t dtype_size(int32_t d) { return d == MARLIN_Q4_BF16 ? 2 : 4; }
+inline size_t align16(size_t v) { return (v + 255) / 256 * 256; }
+
+int check_tensor(const marlin_q4_tensor* t) {
+    if (!t || !t->weight || !t->scales || !t->biases) return MARLIN_Q4_ERR_ARG;
+    if (t->n <= 0 || t->k <= 0) return MARLIN_Q4_ERR_ARG;
+    if (t->group_size != 64 || t->bits != 4 || t->k % 64 != 0) return MARLIN_Q4_ERR_SHAPE;
+    if (t->k > (1 << 20) || t->n > (int64_t)1 << 31) return MARLIN_Q4_ERR_UNSUPPORTED;
+    if (!aligned(t->weight, 16) || !aligned(t->scales, 16) || !aligned(t->biases, 16)) return MARLIN_Q4_ERR_ALIGN;
+    return MARLIN_Q4_OK;
+}
+
+int check_act(const void* x, int32_t dtype) {
+    if (!x) return MARLIN_Q4_ERR_ARG;
+    if (!valid_dtype(dtype)) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(x, dtype_size(dtype))) return MARLIN_Q4_ERR_ALIGN;
+    return MARLIN_Q4_OK;
+}
+
+Q4Mat view(const marlin_q4_tensor* t) { return Q4Mat{t->weight, t->scales, t->biases, t->n, t->k}; }
+
+// rows per GEMV pass for an activation dtype (m * planes <= 32)
+int64_t rows_per_pass(int32_t act_dtype, bool normed) {
+    return (normed || act_dtype == MARLIN_Q4_F32) ? 10 : 32;
+}
+
+// y[m, n] (y_dtype) for x[m, k]; rows processed in passes of at most rows_per_pass
+int gemv_passes(const void* x, int32_t x_dtype, int64_t m, const uint16_t* norm_w, float eps, const Q4Mat& w0,
+                const Q4Mat& w1, int epi, void* y, int32_t y_dtype, int64_t ldy, const void* resid,
+                int32_t resid_dtype, int64_t ldr, cudaStream_t stream) {
+    const int64_t rp = rows_per_pass(x_dtype, norm_w != nullptr);
+    for (int64_t r0 = 0; r0 < m; r0 += rp) {
+        GemvLaunch L{};
+        L.x = static_cast<const uint8_t*>(x) + r0 * w0.k * dtype_size(x_dtype);
+        L.x_dtype = x_dtype;
+        L.m = std::min(rp, m - r0);
+        L.norm_w = norm_w;
+        L.eps = eps;
+        L.w0 = w0;
+        L.w1 = w1;
+        L.y = static_cast<uint8_t*>(y) + r0 * ldy * dtype_size(y_dtype);
+        L.y_dtype = y_dtype;
+        L.ldy = ldy;
+        L.resid = resid ? static_cast<const uint8_t*>(resid) + r0 * ldr * dtype_size(resid_dtype) : nullptr;
+        L.resid_dtype = resid_dtype;
+        L.ldr = ldr;
+        L.epi = epi;
+        L.pdl = g_pdl;
+        const int rc = cuda_status(launch_q4_gemv(L, stream));
+        if (rc) return rc;
+    }
+    return MARLIN_Q4_OK;
+}
+
+}  // namespace
+}  // namespace marlin
+
+using namespace marlin;
+
+extern "C" {
+
+const char* marlin_q4_version(void) { return "marlin-q4-b200 0.1 (sm_100a)"; }
+
+const char* marlin_q4_status_string(int status) {
+    switch (status) {
+        case MARLIN_Q4_OK: return "ok";
+        case MARLIN_Q4_ERR_ARG: return "invalid argument";
+        case MARLIN_Q4_ERR_SHAPE: return "invalid shape (k % 64, group_size 64, bits 4, matching dims)";
+        case MARLIN_Q4_ERR_ALIGN: return "misaligned pointer";
+        case MARLIN_Q4_ERR_UNSUPPORTED: return "unsupported size";
+        case MARLIN_Q4_ERR_CUDA: return "CUDA launch failed";
+        case MARLIN_Q4_ERR_WORKSPACE: return "workspace missing, too small or misaligned";
+        default: return "unknown status";
+    }
+}
+
+int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
+
+int marlin_q4_device_error(int clear) {
+    const int v = gemv_device_error(clear != 0);
+    if (v < 0) return cuda_status(cudaGetLastError());
+    return v;
+}
+
+void marlin_q4_set_pdl(int enable) { g_pdl = enable != 0; }
+
+int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_size, int32_t bits, uint32_t* wq,
+                       uint16_t* scales, uint16_t* biases, void* stream) {
+    if (!w || !wq || !scales || !biases || n <= 0 || k <= 0) return MARLIN_Q4_ERR_ARG;
+    if (group_size != 64 || bits != 4 || k % 64 != 0) return MARLIN_Q4_ERR_SHAPE;
+    if (!aligned(w, 16) || !aligned(wq, 4) || !aligned(scales, 2) || !aligned(biases, 2)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_quantize(w, n, k, wq, scales, biases, static_cast<cudaStream_t>(stream)));
+}
+
+int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, void* y, void* stream) {
+    int rc = check_tensor(w);
+    if (rc) return rc;
+    if ((rc = check_act(x, x_dtype))) return rc;
+    if ((rc = check_act(y, x_dtype))) return rc;
+    if (m <= 0) return MARLIN_Q4_ERR_ARG;
+    const Q4Mat v = view(w);
+    return gemv_passes(x, x_dtype, m, nullptr, 0.f, v, v, kEpiStore, y, x_dtype, w->n, nullptr, 0, 0,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int marlin_q4_rms_norm(const void* x, int32_t x_dtype, const uint16_t* weight, int64_t m, int64_t h, float eps,
+                       float* out, void* stream) {
+    int rc = check_act(x, x_dtype);
+    if (rc) return rc;
+    if (!weight || !out || m <= 0 || h <= 0) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(out, 4) || !aligned(weight, 2)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_rms_norm(x, x_dtype, weight, m, h, eps, out, static_cast<cudaStream_t>(stream)));
+}
+
+int marlin_q4_gate_up_swiglu(const void* x, int32_t x_dtype, int64_t m, const uint16_t* norm_weight, float eps,
+                             const marlin_q4_tensor* gate, const marlin_q4_tensor* up, void* act, void* stream) {
+    int rc;
+    if ((rc = check_tensor(gate)) || (rc = check_tensor(up))) return rc;
+    if ((rc = check_act(x, x_dtype))) return rc;
+    if (gate->n != up->n || gate->k != up->k) return MARLIN_Q4_ERR_SHAPE;
+    if (m <= 0) return MARLIN_Q4_ERR_ARG;
+    const int32_t act_dtype = norm_weight ? MARLIN_Q4_F32 : x_dtype;
+    if ((rc = check_act(act, act_dtype))) return rc;
+    return gemv_passes(x, x_dtype, m, norm_weight, eps, view(gate), view(up), kEpiSwiglu, act, act_dtype, gate->n,
+                       nullptr, 0, 0, static_cast<cudaStream_t>(stream));
+}
+
+int marlin_q4_matmul_residual(const void* act, int32_t act_dtype, int64_t m, const marlin_q4_tensor* w,
+                              const void* resid, int32_t resid_dtype, float* y, void* stream) {
+    int rc;
+    if ((rc = check_tensor(w))) return rc;
+    if ((rc = check_act(act, act_dtype)) || (rc = check_act(resid, resid_dtype))) return rc;
+    if ((rc = check_act(y, MARLIN_Q4_F32))) return rc;
+    if (m <= 0) return MARLIN_Q4_ERR_ARG;
+    const Q4Mat v = view(w);
+    return gemv_passes(act, act_dtype, m, nullptr, 0.f, v, v, kEpiResid, y, MARLIN_Q4_F32, w->n, resid, resid_dtype,
+                       w->n, static_cast<cudaStream_t>(stream));
+}
+
+size_t marlin_q4_mlp_workspace_size(int64_t m, int64_t intermediate, int32_t x_dtype) {
+    if (m <= 0 || intermediate <= 0 || !valid_dtype(x_dtype)) return 0;
+    return align16((size_t)m * intermediate * dtype_size(x_dtype));
+}
+
+int marlin_q4_mlp(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* gate,
+                  const marlin_q4_tensor* up, const marlin_q4_tensor* down, void* y, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_tensor(gate)) || (rc = check_tensor(up)) || (rc = check_tensor(down))) return rc;
+    if ((rc = check_act(x, x_dtype)) || (rc = check_act(y, x_dtype))) return rc;
+    if (m <= 0) return MARLIN_Q4_ERR_ARG;
+    if (gate->n != up->n || gate->k != up->k || down->k != gate->n || down->n != gate->k) return MARLIN_Q4_ERR_SHAPE;
+    if (!workspace || !aligned(workspace, 16) || workspace_bytes < marlin_q4_mlp_workspace_size(m, gate->n, x_dtype))
+        return MARLIN_Q4_ERR_WORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = gemv_passes(x, x_dtype, m, nullptr, 0.f, view(gate), view(up), kEpiSwiglu, workspace, x_dtype,
+                          gate->n, nullptr, 0, 0, st)))
+        return rc;
+    const Q4Mat d = view(down);
+    return gemv_passes(workspace, x_dtype, m, nullptr, 0.f, d, d, kEpiStore, y, x_dtype, down->n, nullptr, 0, 0, st);
+}
+
+int marlin_q4_residual_add(const void* h, int32_t h_dtype, const float* y, int64_t count, float* out, void* stream) {
+    int rc;
+    if ((rc = check_act(h, h_dtype))) return rc;
+    if (!y || !out || count <= 0) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(y, 4) || !aligned(out, 4)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_residual_add(h, h_dtype, y, count, out, static_cast<cudaStream_t>(stream)));
+}
+
+size_t marlin_q4_lm_head_workspace_size(int64_t m) {
+    if (m <= 0) return 0;
+    return align16((size_t)m * 8 + 16);
+}
+
+int marlin_q4_lm_head_argmax(const void* hidden, int32_t dtype, int64_t m, const uint16_t* norm_weight, float eps,
+                             const marlin_q4_tensor* lm, int64_t vocab_offset, int32_t* ids, float* best,
+                             uint64_t* keys_out, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_tensor(lm))) return rc;
+    if ((rc = check_act(hidden, dtype))) return rc;
+    if (m <= 0 || vocab_offset < 0 || (!ids && !best && !keys_out)) return MARLIN_Q4_ERR_ARG;
+    if (vocab_offset + lm->n > 0xffffffffLL) return MARLIN_Q4_ERR_UNSUPPORTED;
+    if (!workspace || !aligned(workspace, 16) || workspace_bytes < marlin_q4_lm_head_workspace_size(m))
+        return MARLIN_Q4_ERR_WORKSPACE;
+    if ((ids && !aligned(ids, 4)) || (best && !aligned(best, 4)) || (keys_out && !aligned(keys_out, 8)))
+        return MARLIN_Q4_ERR_ALIGN;
+    unsigned long long* keys = static_cast<unsigned long long*>(workspace);
+    unsigned int* counter = reinterpret_cast<unsigned int*>(keys + m);
+    const int64_t rp = rows_per_pass(dtype, norm_weight != nullptr);
+    for (int64_t r0 = 0; r0 < m; r0 += rp) {
+        LmHeadLaunch L{};
+        L.x = static_cast<const uint8_t*>(hidden) + r0 * lm->k * dtype_size(dtype);
+        L.x_dtype = dtype;
+        L.m = std::min(rp, m - r0);
+        L.norm_w = norm_weight;
+        L.eps = eps;
+        L.w = view(lm);
+        L.vocab_offset = vocab_offset;
+        L.keys = keys + r0;
+        L.counter = counter;
+        L.keys_out = keys_out ? reinterpret_cast<unsigned long long*>(keys_out) + r0 : nullptr;
+        L.ids = ids ? ids + r0 : nullptr;
+        L.best = best ? best + r0 : nullptr;
+        L.pdl = g_pdl;
+        if ((rc = cuda_status(launch_q4_lm_head_argmax(L, static_cast<cudaStream_t>(stream))))) return rc;
+    }
+    return MARLIN_Q4_OK;
+}
+
+int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* best, void* stream) {
+    if (!keys || m <= 0 || (!ids && !best)) return MARLIN_Q4_ERR_ARG;
+    return cuda_status(launch_decode_keys(reinterpret_cast<const unsigned long long*>(keys), m, ids, best,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate) {
+    if (m <= 0 || hidden <= 0 || intermediate <= 0) return 0;
+    return align16((size_t)m * hidden * 4) + align16((size_t)m * intermediate * 4) + marlin_q4_lm_head_workspace_size(m);
+}
+
+int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
+                          const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
+                          const marlin_q4_tensor* lm, int32_t* ids, float* best, float* h_out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    int rc;
+    if (!h0 || m <= 0 || hidden <= 0 || n_layers < 1 || !layers || !final_norm || !ids)
+        return MARLIN_Q4_ERR_ARG;
+    if ((rc = check_tensor(lm))) return rc;
+    if (lm->k != hidden) return MARLIN_Q4_ERR_SHAPE;
+    int64_t inter = 1;
+    for (int32_t l = 0; l < n_layers; ++l) {
+        const marlin_q4_layer& L = layers[l];
+        if (!L.post_attn_norm) return MARLIN_Q4_ERR_ARG;
+        if ((rc = check_tensor(&L.gate_proj)) || (rc = check_tensor(&L.up_proj)) || (rc = check_tensor(&L.down_proj)))
+            return rc;
+        if (L.gate_proj.k != hidden || L.up_proj.k != hidden || L.up_proj.n != L.gate_proj.n ||
+            L.down_proj.k != L.gate_proj.n || L.down_proj.n != hidden)
+            return MARLIN_Q4_ERR_SHAPE;
+        inter = std::max<int64_t>(inter, L.gate_proj.n);
+    }
+    if (!workspace || !aligned(workspace, 16) ||
+        workspace_bytes < marlin_q4_decode_step_workspace_size(m, hidden, inter))
+        return MARLIN_Q4_ERR_WORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* h = reinterpret_cast<float*>(ws);
+    float* act = reinterpret_cast<float*>(ws + align16((size_t)m * hidden * 4));
+    void* lmws = ws + align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
+    if (h_out) h = h_out;
+    const void* cur = h0;
+    int32_t cur_dtype = MARLIN_Q4_BF16;
+    for (int32_t l = 0; l < n_layers; ++l) {
+        const marlin_q4_layer& L = layers[l];
+        if ((rc = marlin_q4_gate_up_swiglu(cur, cur_dtype, m, L.post_attn_norm, eps, &L.gate_proj, &L.up_proj, act,
+                                           stream)))
+            return rc;
+        if ((rc = marlin_q4_matmul_residual(act, MARLIN_Q4_F32, m, &L.down_proj, cur, cur_dtype, h, stream))) return rc;
+        cur = h;
+        cur_dtype = MARLIN_Q4_F32;
+    }
+    return marlin_q4_lm_head_argmax(cur, cur_dtype, m, final_norm, eps, lm, 0, ids, best, nullptr, lmws,
+                                    marlin_q4_lm_head_workspace_size(m), st);
+}
+
+int marlin_q4_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float sigma, void* stream) {
+    if (!out || n <= 0) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(out, 2)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_synth_bf16(out, n, seed, mean, sigma, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,156 @@
+// common.cuh — device helpers shared by the Q4 kernels (sm_100a).
+//
+// Inline PTX wrappers for: mbarriers with bounded waits, 1-D TMA bulk copies (cp.async.bulk, no
+// multicast), programmatic dependent launch (griddepcontrol), and the bf16 m16n8k16 mma used by
+// the decode GEMV.  Every wait loop here is bounded: on timeout it records an error code in
+// g_marlin_device_error and returns false so the kernel can exit; nothing traps.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace marlin {
+
+// Device-side error word: 0 = ok.  Written only on a wait timeout or an internal consistency
+// failure.  Each translation unit that waits on device-side conditions has its own copy (the
+// library is compiled without relocatable device code) and a host accessor that
+// marlin_q4_device_error() combines.
+static __device__ int g_marlin_device_error = 0;
+
+enum DeviceError : int {
+    kDevErrNone = 0,
+    kDevErrMbarTimeout = 1,
+    kDevErrTmemAlloc = 2,
+};
+
+__device__ __forceinline__ void record_device_error(int code) {
+    atomicCAS(&g_marlin_device_error, 0, code);
+}
+
+// ---- bf16 helpers ------------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+// round-to-nearest-even binary32 -> bf16 bits (finite inputs; NaN made quiet)
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (u >> 16) | 0x40u;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return u >> 16;
+}
+__device__ __forceinline__ float bf16_round(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+// ---- shared-memory address / mbarrier ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  try_wait itself suspends for a hardware-defined time; the
+// loop adds a nanosleep back-off and gives up after ~2^22 polls (well over a second), recording
+// kDevErrMbarTimeout.  Returns true when the phase completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (it > 64) __nanosleep(256);
+    }
+    record_device_error(kDevErrMbarTimeout);
+    return false;
+}
+
+// ---- TMA 1-D bulk copy global -> shared (no multicast) -----------------------------------------
+// dst and src 16-byte aligned, bytes a multiple of 16; completion counted on `bar` (complete_tx).
+__device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// L2 prefetch of a contiguous range (16-byte aligned, multiple of 16 bytes).
+__device__ __forceinline__ void tma_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- shared loads -------------------------------------------------------------------------------
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_u32(p)));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(const void* p) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+    return v;
+}
+
+// ---- mma.sync m16n8k16 bf16 x bf16 -> f32 ------------------------------------------------------
+// A row-major 16x16 (a0: row g cols 2t..2t+1, a1: row g+8, a2: row g cols 2t+8.., a3: row g+8 ..),
+// B col-major 16x8 (b0: k 2t..2t+1 col g, b1: k 2t+8..), D 16x8 (d0,d1: row g cols 2t,2t+1;
+// d2,d3: row g+8), g = lane/4, t = lane%4.
+__device__ __forceinline__ void mma_bf16_16816(float d[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Q4 nibble pairs -> bf16x2 holding 1 + q/16 (exact).  For a packed word w (nibble j = element j
+// in bits [4j,4j+4)), pair j in {0..3} holds (element j, element j+4) in the (low, high) halves.
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+    return r;
+}
+__device__ __forceinline__ void q4_pairs(uint32_t w, uint32_t p[4]) {
+    const uint32_t M = 0x00780078u, C = 0x3F803F80u;
+    p[0] = lop3_and_or(w << 3, M, C);
+    p[1] = lop3_and_or(w >> 1, M, C);
+    p[2] = lop3_and_or(w >> 5, M, C);
+    p[3] = lop3_and_or(w >> 9, M, C);
+}
+
+}  // namespace marlin

@@ -1,0 +1,77 @@
+// q4_gemv.cuh — host-visible declarations of the Q4 decode kernels' launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace marlin {
+
+enum ActDtype : int { kBF16 = 0, kF32 = 1 };
+
+// Device view of a QuantizedTensor (MLX layout).
+struct Q4Mat {
+    const uint32_t* w;  // [n, k/8]
+    const uint16_t* s;  // bf16 [n, k/64]
+    const uint16_t* b;  // bf16 [n, k/64]
+    int64_t n;
+    int64_t k;
+};
+
+enum Epilogue : int {
+    kEpiStore = 0,   // y[m, row] = out                      (y dtype = out_dtype)
+    kEpiSwiglu = 1,  // y[m, f] = (sigmoid(g)*g)*u of the gate (w0) and up (w1) rows f
+    kEpiResid = 2,   // y[m, row] = resid[m, row] + out       (residual add, binary32)
+};
+
+struct GemvLaunch {
+    const void* x;  // [m, k] activations (x_dtype)
+    int x_dtype;
+    int64_t m;
+    const uint16_t* norm_w;  // optional RMSNorm (1+w) applied to x first (k == hidden); null = none
+    float eps;
+    Q4Mat w0;  // main weight (gate for kEpiSwiglu)
+    Q4Mat w1;  // up weight (kEpiSwiglu only)
+    void* y;
+    int y_dtype;
+    int64_t ldy;         // row stride of y in elements
+    const void* resid;   // kEpiResid input, [m, ldr]
+    int resid_dtype;
+    int64_t ldr;
+    int epi;
+    bool pdl;  // launch with programmatic stream serialization
+};
+
+// Number of activation rows the tensor-core GEMV handles in one pass: m * planes <= 32, with
+// planes = 1 for bf16 activations and 3 for binary32 (exact bf16 hi/mid/lo split).
+int gemv_max_rows(int act_dtype);
+
+// Launches the decode GEMV family (one CTA per row block, weights fetched before the PDL wait).
+// Returns cudaSuccess or the launch error.  Arguments are validated by the caller.
+cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream);
+
+struct LmHeadLaunch {
+    const void* x;  // [m, k] hidden state (x_dtype)
+    int x_dtype;
+    int64_t m;
+    const uint16_t* norm_w;  // optional final RMSNorm
+    float eps;
+    Q4Mat w;                 // [vocab_shard, k]
+    int64_t vocab_offset;    // global index of row 0 of this shard
+    unsigned long long* keys;  // [m] packed (value, index) keys; must be zero on entry, left zero
+    unsigned int* counter;     // completion counter; must be zero on entry, left zero
+    unsigned long long* keys_out;  // optional [m]: final keys (for a cross-shard merge)
+    int32_t* ids;            // optional [m]: argmax ids (vocab_offset applied)
+    float* best;             // optional [m]: winning logit
+    bool pdl;
+};
+
+cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream);
+
+// Device error word of this translation unit (0 ok, >0 a DeviceError code, -1 CUDA failure).
+int gemv_device_error(bool clear);
+
+// Decode packed keys [m] into ids/best (used after a cross-GPU max-merge of keys).
+cudaError_t launch_decode_keys(const unsigned long long* keys, int64_t m, int32_t* ids, float* best,
+                               cudaStream_t stream);
+
+}  // namespace marlin

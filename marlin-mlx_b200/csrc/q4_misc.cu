@@ -1,0 +1,197 @@
+// q4_misc.cu — Q4 quantize/pack, standalone RMSNorm, and the seeded synthetic-input generator.
+#include "common.cuh"
+#include "q4_misc.cuh"
+
+namespace marlin {
+namespace {
+
+// ------------------------------------------------------------------------------------------------
+// quantize: mx::quantize(w, group_size=64, bits=4) as called at src/model/weights.cpp:46 and :183.
+// One warp covers 4 consecutive groups (groups are contiguous in row-major [n, k] since k % 64 == 0):
+// 8 lanes per group, each lane loads 8 bf16 (16 B) and emits one packed u32 word.  Per group, in
+// IEEE binary32 with no contraction:
+//   max = max(0, w..), min = min(w..), s = max((max - min)/15, 1e-7)
+//   side = |min| > |max|; s = side ? s : -s; edge = side ? min : max
+//   q0 = round(edge/s); q0 != 0 ? (s = edge/q0, b = edge) : (b = 0)
+//   q = min(max(round((w - b)/s), 0), 15);  round = ties away from zero
+// scales/biases are stored as bf16 (round to nearest even).
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) quantize_kernel(const uint16_t* __restrict__ w, int64_t ngroups,
+                                                       uint32_t* __restrict__ wq, uint16_t* __restrict__ scales,
+                                                       uint16_t* __restrict__ biases) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t gi = warp_global * 4 + (lane >> 3);
+    const int j = lane & 7;
+    const bool valid = gi < ngroups;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (valid) raw = __ldg(reinterpret_cast<const uint4*>(w + gi * 64 + j * 8));
+    float v[8];
+    const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = bf16_bits_to_f32(rw[i] & 0xffffu);
+        v[2 * i + 1] = bf16_bits_to_f32(rw[i] >> 16);
+    }
+    float wmin = INFINITY, wmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        wmin = fminf(wmin, v[i]);
+        wmax = fmaxf(wmax, v[i]);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        wmin = fminf(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+        wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    }
+    float scale = fmaxf(__fdiv_rn(__fsub_rn(wmax, wmin), 15.0f), 1e-7f);
+    const bool side = fabsf(wmin) > fabsf(wmax);
+    scale = side ? scale : -scale;
+    const float edge = side ? wmin : wmax;
+    const float q0 = roundf(__fdiv_rn(edge, scale));
+    float bias = 0.0f;
+    if (q0 != 0.0f) {
+        scale = __fdiv_rn(edge, q0);
+        bias = edge;
+    }
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float c = roundf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
+        c = fminf(fmaxf(c, 0.0f), 15.0f);
+        word |= (uint32_t)c << (4 * i);
+    }
+    if (valid) {
+        wq[gi * 8 + j] = word;
+        if (j == 0) {
+            scales[gi] = (uint16_t)f32_to_bf16_bits(scale);
+            biases[gi] = (uint16_t)f32_to_bf16_bits(bias);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// RMSNorm (src/model/marlin.cpp:12-16) as MLX's C++ API evaluates it; one CTA per row.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rms_norm_kernel(const void* __restrict__ x, int dtype,
+                                                       const uint16_t* __restrict__ wn, int64_t H, float eps,
+                                                       float* __restrict__ out) {
+    __shared__ float scr[32];
+    __shared__ float rf;
+    const int64_t m = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    auto ld = [&](int64_t k) -> float {
+        if (dtype == kDtypeBF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(x)[m * H + k]);
+        return static_cast<const float*>(x)[m * H + k];
+    };
+    float part = 0.f;
+    for (int64_t k = tid; k < H; k += blockDim.x) {
+        const float v = ld(k);
+        float sq = __fmul_rn(v, v);
+        if (dtype == kDtypeBF16) sq = bf16_round(sq);
+        part = __fadd_rn(part, sq);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+    if (lane == 0) scr[warp] = part;
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.f;
+        for (int w = 0; w < (int)(blockDim.x / 32); ++w) sum = __fadd_rn(sum, scr[w]);
+        float var;
+        if (dtype == kDtypeBF16)
+            var = bf16_round(__fmul_rn(bf16_round(sum), bf16_round((float)(1.0 / (double)H))));
+        else
+            var = __fmul_rn(sum, (float)(1.0 / (double)H));
+        rf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    }
+    __syncthreads();
+    const float r = rf;
+    for (int64_t k = tid; k < H; k += blockDim.x)
+        out[m * H + k] = __fmul_rn(__fmul_rn(ld(k), r), __fadd_rn(1.0f, bf16_bits_to_f32(wn[k])));
+}
+
+// ------------------------------------------------------------------------------------------------
+// Seeded generator: element i = bf16_rn(mean + sigma * (S - 393210)/65536), S = sum of twelve 16-bit
+// lanes of three splitmix64 outputs.  Integer arithmetic plus one binary32 product and one sum
+// (no contraction), so the host restatement reproduces it bit for bit.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z ^= z >> 30;
+    z *= 0xbf58476d1ce4e5b9ull;
+    z ^= z >> 27;
+    z *= 0x94d049bb133111ebull;
+    z ^= z >> 31;
+    return z;
+}
+
+__global__ void synth_kernel(uint16_t* __restrict__ out, int64_t n, uint64_t seed, float mean, float sigma_scaled) {
+    const uint64_t base = mix64(seed ^ 0x5851f42d4c957f2dull);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t s = 0;
+#pragma unroll
+        for (uint64_t r = 0; r < 3; ++r) {
+            const uint64_t h = mix64(base + (3ull * (uint64_t)i + r) * 0x9e3779b97f4a7c15ull);
+            s += (int64_t)((h & 0xffffu) + ((h >> 16) & 0xffffu) + ((h >> 32) & 0xffffu) + (h >> 48));
+        }
+        const float z = (float)(s - 393210);
+        const float v = __fadd_rn(__fmul_rn(z, sigma_scaled), mean);
+        out[i] = (uint16_t)f32_to_bf16_bits(v);
+    }
+}
+
+__global__ void residual_add_kernel(const void* __restrict__ h, int dtype, const float* __restrict__ y,
+                                    int64_t n, float* __restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float hv = dtype == kDtypeBF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(h)[i])
+                                             : static_cast<const float*>(h)[i];
+        out[i] = __fadd_rn(hv, y[i]);
+    }
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(const uint16_t* w, int64_t n, int64_t k, uint32_t* wq, uint16_t* scales,
+                            uint16_t* biases, cudaStream_t stream) {
+    const int64_t ngroups = n * (k / 64);
+    if (ngroups <= 0) return cudaSuccess;
+    const int64_t warps = (ngroups + 3) / 4;
+    const int64_t blocks = (warps * 32 + 255) / 256;
+    quantize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(w, ngroups, wq, scales, biases);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(const void* x, int dtype, const uint16_t* w, int64_t m, int64_t h, float eps,
+                            float* out, cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    rms_norm_kernel<<<(unsigned)m, 256, 0, stream>>>(x, dtype, w, h, eps, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_residual_add(const void* h, int dtype, const float* y, int64_t n, float* out,
+                                cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+    residual_add_kernel<<<(unsigned)blocks, 256, 0, stream>>>(h, dtype, y, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float sigma, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 16);
+    synth_kernel<<<(unsigned)blocks, 256, 0, stream>>>(out, n, seed, mean, sigma * (1.0f / 65536.0f));
+    return cudaGetLastError();
+}
+
+}  // namespace marlin

@@ -1,0 +1,13 @@
+"""marlin_q4 — B200 (sm_100a) Q4 path of marlin-mlx: Python front end over libmarlin_q4.so.
+
+The product is the CUDA library (marlin-mlx_b200/csrc, C ABI in include/marlin_q4.h); this
+package binds it for torch tensors (tests, benchmarks, the tensor-parallel driver).
+"""
+from ._lib import LIB_PATH, MarlinQ4Error, load  # noqa: F401
+from .ops import (DecodeStep, Layer, LmHeadWorkspace, QuantizedTensor, decode_keys, device_error,  # noqa: F401
+                  gate_up_swiglu, lm_head_argmax, matmul_residual, mlp_forward, qmatmul, quantize_weight,
+                  residual_add, rms_norm, set_pdl, synth_bf16)
+
+__all__ = ["QuantizedTensor", "quantize_weight", "qmatmul", "rms_norm", "gate_up_swiglu", "matmul_residual",
+           "mlp_forward", "residual_add", "lm_head_argmax", "LmHeadWorkspace", "decode_keys", "Layer",
+           "DecodeStep", "synth_bf16", "device_error", "set_pdl", "load", "LIB_PATH", "MarlinQ4Error"]

@@ -1,0 +1,254 @@
+"""Torch-tensor front end over the C ABI, mirroring the reference's operator surface.
+
+Names follow marlin-mlx: ``QuantizedTensor`` (src/core/types.h:75-82), ``quantize_weight``
+(src/model/weights.cpp:45-56), ``qmatmul`` (src/model/marlin.cpp:18-25), ``rms_norm`` (:12-16),
+``mlp_forward`` (:31-35), ``lm_head`` + greedy ``sample_token`` (:161-169, sampler.cpp:9-16).
+Tensors are CUDA tensors; every op launches on torch's current stream and goes through
+libmarlin_q4.so — there is no PyTorch or CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, Q4Layer, Q4Tensor, check
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.float32:
+        return F32
+    raise TypeError(f"activation dtype must be bfloat16 or float32, got {t.dtype}")
+
+
+def _cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+@dataclass
+class QuantizedTensor:
+    """MLX Q4 operand: weight uint32 [n, k/8] (held as int32 bits), scales/biases bf16 [n, k/64]."""
+    weight: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    group_size: int = 64
+    bits: int = 4
+    quantized: bool = True
+
+    @property
+    def n(self) -> int:
+        return self.weight.shape[0]
+
+    @property
+    def k(self) -> int:
+        return self.weight.shape[1] * 8
+
+    def c(self) -> Q4Tensor:
+        return Q4Tensor(self.weight.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(), self.n, self.k,
+                        self.group_size, self.bits)
+
+    def shard_rows(self, r0: int, r1: int) -> "QuantizedTensor":
+        """Rows [r0, r1) (output features) — a column-parallel / vocabulary shard."""
+        return QuantizedTensor(self.weight[r0:r1].contiguous(), self.scales[r0:r1].contiguous(),
+                               self.biases[r0:r1].contiguous())
+
+    def shard_k(self, k0: int, k1: int) -> "QuantizedTensor":
+        """Input features [k0, k1) (must be 64-aligned) — a row-parallel shard."""
+        assert k0 % 64 == 0 and k1 % 64 == 0
+        return QuantizedTensor(self.weight[:, k0 // 8:k1 // 8].contiguous(),
+                               self.scales[:, k0 // 64:k1 // 64].contiguous(),
+                               self.biases[:, k0 // 64:k1 // 64].contiguous())
+
+
+def quantize_weight(w: torch.Tensor, bits: int = 4, group_size: int = 64) -> QuantizedTensor:
+    """mx::quantize(w, group_size, bits) (src/model/weights.cpp:45-56)."""
+    _cuda(w, "w")
+    if w.dtype != torch.bfloat16 or w.dim() != 2:
+        raise TypeError("w must be a 2-D bfloat16 tensor")
+    n, k = w.shape
+    wq = torch.empty((n, max(k // 8, 1)), dtype=torch.int32, device=w.device)
+    s = torch.empty((n, max(k // 64, 1)), dtype=torch.bfloat16, device=w.device)
+    b = torch.empty_like(s)
+    check(_lib.load().marlin_q4_quantize(w.data_ptr(), n, k, group_size, bits, wq.data_ptr(), s.data_ptr(),
+                                         b.data_ptr(), _stream()), "marlin_q4_quantize")
+    return QuantizedTensor(wq, s, b, group_size, bits)
+
+
+def qmatmul(x: torch.Tensor, w: QuantizedTensor) -> torch.Tensor:
+    """mx::quantized_matmul(x, w, scales, biases, transpose=true, 64, 4): [.., k] -> [.., n]."""
+    _cuda(x, "x")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    y = torch.empty((x2.shape[0], w.n), dtype=x.dtype, device=x.device)
+    tw = w.c()
+    check(_lib.load().marlin_q4_matmul(x2.data_ptr(), _dtype_code(x), x2.shape[0], ctypes.byref(tw), y.data_ptr(),
+                                       _stream()), "marlin_q4_matmul")
+    return y.reshape(*lead, w.n)
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """rms_norm (src/model/marlin.cpp:12-16) with a float eps: binary32 output."""
+    _cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    out = torch.empty(x2.shape, dtype=torch.float32, device=x.device)
+    check(_lib.load().marlin_q4_rms_norm(x2.data_ptr(), _dtype_code(x), weight.data_ptr(), x2.shape[0],
+                                         x2.shape[1], eps, out.data_ptr(), _stream()), "marlin_q4_rms_norm")
+    return out.reshape(x.shape)
+
+
+def gate_up_swiglu(x: torch.Tensor, gate: QuantizedTensor, up: QuantizedTensor,
+                   norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    act_dtype = torch.float32 if norm_weight is not None else x.dtype
+    if out is None:
+        out = torch.empty((x2.shape[0], gate.n), dtype=act_dtype, device=x.device)
+    tg, tu = gate.c(), up.c()
+    check(_lib.load().marlin_q4_gate_up_swiglu(
+        x2.data_ptr(), _dtype_code(x), x2.shape[0], norm_weight.data_ptr() if norm_weight is not None else None, eps,
+        ctypes.byref(tg), ctypes.byref(tu), out.data_ptr(), _stream()), "marlin_q4_gate_up_swiglu")
+    return out
+
+
+def matmul_residual(act: torch.Tensor, w: QuantizedTensor, resid: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    m = act.reshape(-1, act.shape[-1]).shape[0]
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=act.device)
+    tw = w.c()
+    check(_lib.load().marlin_q4_matmul_residual(act.data_ptr(), _dtype_code(act), m, ctypes.byref(tw),
+                                                resid.data_ptr(), _dtype_code(resid), out.data_ptr(), _stream()),
+          "marlin_q4_matmul_residual")
+    return out
+
+
+def mlp_forward(x: torch.Tensor, gate: QuantizedTensor, up: QuantizedTensor, down: QuantizedTensor) -> torch.Tensor:
+    """mlp_forward (src/model/marlin.cpp:31-35): down(swiglu(gate x, up x)), output in x's dtype."""
+    _cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    m, dt = x2.shape[0], _dtype_code(x)
+    lib = _lib.load()
+    ws_bytes = lib.marlin_q4_mlp_workspace_size(m, gate.n, dt)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    y = torch.empty((m, down.n), dtype=x.dtype, device=x.device)
+    tg, tu, td = gate.c(), up.c(), down.c()
+    check(lib.marlin_q4_mlp(x2.data_ptr(), dt, m, ctypes.byref(tg), ctypes.byref(tu), ctypes.byref(td),
+                            y.data_ptr(), ws.data_ptr(), ws_bytes, _stream()), "marlin_q4_mlp")
+    return y.reshape(*x.shape[:-1], down.n)
+
+
+def residual_add(h: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(h.shape, dtype=torch.float32, device=h.device)
+    check(_lib.load().marlin_q4_residual_add(h.data_ptr(), _dtype_code(h), y.data_ptr(), h.numel(), out.data_ptr(),
+                                             _stream()), "marlin_q4_residual_add")
+    return out
+
+
+class LmHeadWorkspace:
+    """Zero-initialised keys + counter the fused lm_head/argmax needs (left zeroed by every call)."""
+
+    def __init__(self, m: int, device):
+        nbytes = _lib.load().marlin_q4_lm_head_workspace_size(m)
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.m = m
+
+
+def lm_head_argmax(hidden: torch.Tensor, lm: QuantizedTensor, norm_weight: torch.Tensor | None = None,
+                   eps: float = 1e-6, vocab_offset: int = 0, workspace: LmHeadWorkspace | None = None,
+                   want_keys: bool = False):
+    """lm_head (src/model/marlin.cpp:161-169) + greedy argmax (sampler.cpp:14-16), fused.
+
+    Returns (ids int32 [m], best float32 [m]) or, with want_keys, the packed int64 keys [m]."""
+    _cuda(hidden, "hidden")
+    h2 = hidden.reshape(-1, hidden.shape[-1])
+    m = h2.shape[0]
+    if workspace is None or workspace.m < m:
+        workspace = LmHeadWorkspace(m, hidden.device)
+    ids = torch.empty(m, dtype=torch.int32, device=hidden.device)
+    best = torch.empty(m, dtype=torch.float32, device=hidden.device)
+    keys = torch.empty(m, dtype=torch.int64, device=hidden.device) if want_keys else None
+    tl = lm.c()
+    check(_lib.load().marlin_q4_lm_head_argmax(
+        h2.data_ptr(), _dtype_code(hidden), m, norm_weight.data_ptr() if norm_weight is not None else None, eps,
+        ctypes.byref(tl), vocab_offset, ids.data_ptr(), best.data_ptr(), keys.data_ptr() if keys is not None else None,
+        workspace.buf.data_ptr(), workspace.buf.numel(), _stream()), "marlin_q4_lm_head_argmax")
+    if want_keys:
+        return keys
+    return ids, best
+
+
+def decode_keys(keys: torch.Tensor):
+    m = keys.numel()
+    ids = torch.empty(m, dtype=torch.int32, device=keys.device)
+    best = torch.empty(m, dtype=torch.float32, device=keys.device)
+    check(_lib.load().marlin_q4_decode_keys(keys.data_ptr(), m, ids.data_ptr(), best.data_ptr(), _stream()),
+          "marlin_q4_decode_keys")
+    return ids, best
+
+
+@dataclass
+class Layer:
+    post_attn_norm: torch.Tensor
+    gate_proj: QuantizedTensor
+    up_proj: QuantizedTensor
+    down_proj: QuantizedTensor
+
+    def c(self) -> Q4Layer:
+        return Q4Layer(self.post_attn_norm.data_ptr(), self.gate_proj.c(), self.up_proj.c(), self.down_proj.c())
+
+
+class DecodeStep:
+    """One greedy decode step over the Q4 path (marlin_q4_decode_step), with persistent workspace."""
+
+    def __init__(self, layers: list[Layer], final_norm: torch.Tensor, lm: QuantizedTensor, m: int,
+                 eps: float = 1e-6):
+        self.layers, self.final_norm, self.lm, self.m, self.eps = layers, final_norm, lm, m, eps
+        dev = final_norm.device
+        self.hidden = lm.k
+        inter = max(L.gate_proj.n for L in layers)
+        lib = _lib.load()
+        self.ws_bytes = lib.marlin_q4_decode_step_workspace_size(m, self.hidden, inter)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.c_layers = (Q4Layer * len(layers))(*[L.c() for L in layers])
+        self.c_lm = lm.c()
+        self.ids = torch.empty(m, dtype=torch.int32, device=dev)
+        self.best = torch.empty(m, dtype=torch.float32, device=dev)
+        self.h = torch.empty((m, self.hidden), dtype=torch.float32, device=dev)
+
+    def __call__(self, h0: torch.Tensor):
+        assert h0.dtype == torch.bfloat16 and h0.shape == (self.m, self.hidden)
+        check(_lib.load().marlin_q4_decode_step(
+            h0.data_ptr(), self.m, self.hidden, len(self.layers), self.c_layers, self.final_norm.data_ptr(), self.eps,
+            ctypes.byref(self.c_lm), self.ids.data_ptr(), self.best.data_ptr(), self.h.data_ptr(), self.ws.data_ptr(),
+            self.ws_bytes, _stream()), "marlin_q4_decode_step")
+        return self.ids, self.best, self.h
+
+
+def synth_bf16(shape, seed: int, mean: float = 0.0, sigma: float = 1.0, device="cuda") -> torch.Tensor:
+    """Seeded synthetic bf16 tensor (bit-identical to the CPU generator for the same seed)."""
+    out = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    check(_lib.load().marlin_q4_synth_bf16(out.data_ptr(), out.numel(), seed, mean, sigma, _stream()),
+          "marlin_q4_synth_bf16")
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    return _lib.load().marlin_q4_device_error(1 if clear else 0)
+
+
+def set_pdl(enable: bool) -> None:
+    _lib.load().marlin_q4_set_pdl(1 if enable else 0)
