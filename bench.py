@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-family and batch sweeps")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg (profiling runs)")
     return ap.parse_args()
 
 
@@ -341,7 +342,7 @@ def run_ours(args):
 
     # CPU baseline: the oracle (CPU restatement) on the host cores, bounded sample, rank 0 at N=1
     cpu = None
-    if world == 1 and rank == 0:
+    if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_baseline_from_device(layers, fn, lm, h0, B, args.cpu_seconds)
 
     launches = args.steps * (2 * L + 1) if world == 1 else args.steps * (3 * L + 3)

@@ -45,6 +45,15 @@ int check_act(const void* x, int32_t dtype) {
     return MARLIN_Q4_OK;
 }
 
+// activations read by the GEMV kernels with 16-byte vector loads
+int check_act16(const void* x, int32_t dtype) {
+    int rc = check_act(x, dtype);
+    if (rc) return rc;
+    return aligned(x, 16) ? MARLIN_Q4_OK : MARLIN_Q4_ERR_ALIGN;
+}
+
+int check_norm(const uint16_t* w) { return (!w || aligned(w, 16)) ? MARLIN_Q4_OK : MARLIN_Q4_ERR_ALIGN; }
+
 Q4Mat view(const marlin_q4_tensor* t) { return Q4Mat{t->weight, t->scales, t->biases, t->n, t->k}; }
 
 // rows per GEMV pass for an activation dtype (m * planes <= 32)
@@ -123,7 +132,7 @@ int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_si
 int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, void* y, void* stream) {
     int rc = check_tensor(w);
     if (rc) return rc;
-    if ((rc = check_act(x, x_dtype))) return rc;
+    if ((rc = check_act16(x, x_dtype))) return rc;
     if ((rc = check_act(y, x_dtype))) return rc;
     if (m <= 0) return MARLIN_Q4_ERR_ARG;
     const Q4Mat v = view(w);
@@ -144,7 +153,7 @@ int marlin_q4_gate_up_swiglu(const void* x, int32_t x_dtype, int64_t m, const ui
                              const marlin_q4_tensor* gate, const marlin_q4_tensor* up, void* act, void* stream) {
     int rc;
     if ((rc = check_tensor(gate)) || (rc = check_tensor(up))) return rc;
-    if ((rc = check_act(x, x_dtype))) return rc;
+    if ((rc = check_act16(x, x_dtype)) || (rc = check_norm(norm_weight))) return rc;
     if (gate->n != up->n || gate->k != up->k) return MARLIN_Q4_ERR_SHAPE;
     if (m <= 0) return MARLIN_Q4_ERR_ARG;
     const int32_t act_dtype = norm_weight ? MARLIN_Q4_F32 : x_dtype;
@@ -157,7 +166,7 @@ int marlin_q4_matmul_residual(const void* act, int32_t act_dtype, int64_t m, con
                               const void* resid, int32_t resid_dtype, float* y, void* stream) {
     int rc;
     if ((rc = check_tensor(w))) return rc;
-    if ((rc = check_act(act, act_dtype)) || (rc = check_act(resid, resid_dtype))) return rc;
+    if ((rc = check_act16(act, act_dtype)) || (rc = check_act(resid, resid_dtype))) return rc;
     if ((rc = check_act(y, MARLIN_Q4_F32))) return rc;
     if (m <= 0) return MARLIN_Q4_ERR_ARG;
     const Q4Mat v = view(w);
@@ -175,7 +184,7 @@ int marlin_q4_mlp(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_ten
                   size_t workspace_bytes, void* stream) {
     int rc;
     if ((rc = check_tensor(gate)) || (rc = check_tensor(up)) || (rc = check_tensor(down))) return rc;
-    if ((rc = check_act(x, x_dtype)) || (rc = check_act(y, x_dtype))) return rc;
+    if ((rc = check_act16(x, x_dtype)) || (rc = check_act(y, x_dtype))) return rc;
     if (m <= 0) return MARLIN_Q4_ERR_ARG;
     if (gate->n != up->n || gate->k != up->k || down->k != gate->n || down->n != gate->k) return MARLIN_Q4_ERR_SHAPE;
     if (!workspace || !aligned(workspace, 16) || workspace_bytes < marlin_q4_mlp_workspace_size(m, gate->n, x_dtype))
@@ -206,16 +215,16 @@ int marlin_q4_lm_head_argmax(const void* hidden, int32_t dtype, int64_t m, const
                              uint64_t* keys_out, void* workspace, size_t workspace_bytes, void* stream) {
     int rc;
     if ((rc = check_tensor(lm))) return rc;
-    if ((rc = check_act(hidden, dtype))) return rc;
+    if ((rc = check_act16(hidden, dtype)) || (rc = check_norm(norm_weight))) return rc;
     if (m <= 0 || vocab_offset < 0 || (!ids && !best && !keys_out)) return MARLIN_Q4_ERR_ARG;
-    if (vocab_offset + lm->n > 0xffffffffLL) return MARLIN_Q4_ERR_UNSUPPORTED;
+    if (vocab_offset + lm->n > 0xffffffffLL || lm->k > 64 * 64) return MARLIN_Q4_ERR_UNSUPPORTED;
     if (!workspace || !aligned(workspace, 16) || workspace_bytes < marlin_q4_lm_head_workspace_size(m))
         return MARLIN_Q4_ERR_WORKSPACE;
     if ((ids && !aligned(ids, 4)) || (best && !aligned(best, 4)) || (keys_out && !aligned(keys_out, 8)))
         return MARLIN_Q4_ERR_ALIGN;
     unsigned long long* keys = static_cast<unsigned long long*>(workspace);
     unsigned int* counter = reinterpret_cast<unsigned int*>(keys + m);
-    const int64_t rp = rows_per_pass(dtype, norm_weight != nullptr);
+    const int64_t rp = lm_head_max_rows(dtype, norm_weight != nullptr);
     for (int64_t r0 = 0; r0 < m; r0 += rp) {
         LmHeadLaunch L{};
         L.x = static_cast<const uint8_t*>(hidden) + r0 * lm->k * dtype_size(dtype);
@@ -254,6 +263,7 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     int rc;
     if (!h0 || m <= 0 || hidden <= 0 || n_layers < 1 || !layers || !final_norm || !ids)
         return MARLIN_Q4_ERR_ARG;
+    if (!aligned(h0, 16) || !aligned(final_norm, 16) || (h_out && !aligned(h_out, 16))) return MARLIN_Q4_ERR_ALIGN;
     if ((rc = check_tensor(lm))) return rc;
     if (lm->k != hidden) return MARLIN_Q4_ERR_SHAPE;
     int64_t inter = 1;

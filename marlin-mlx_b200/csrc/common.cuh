@@ -78,14 +78,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase.  try_wait itself suspends for a hardware-defined time; the
-// loop adds a nanosleep back-off and gives up after ~2^22 polls (well over a second), recording
-// kDevErrMbarTimeout.  Returns true when the phase completed.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on an mbarrier phase.  try_wait suspends the thread for a hardware-defined time
+// while the phase is pending; the loop gives up after 2 s of wall time (global timer) or 2^28
+// polls, records kDevErrMbarTimeout and returns false.  Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    for (uint32_t it = 0; it < (1u << 22); ++it) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1; it < (1u << 28); ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (it > 64) __nanosleep(256);
+        if ((it & 255u) == 0 && globaltimer_ns() - t0 > 2000000000ull) break;
     }
     record_device_error(kDevErrMbarTimeout);
     return false;
@@ -98,6 +105,20 @@ __device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// TMA tiled 2-D load (no multicast): box at element coordinates (x, y) of the tensor map into
+// shared memory; x * element size must be a multiple of 16 bytes.  Out-of-range elements are
+// zero-filled and still counted in the transaction bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t x, int32_t y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
 // L2 prefetch of a contiguous range (16-byte aligned, multiple of 16 bytes).

@@ -4,36 +4,42 @@
 // marlin-mlx (src/model/marlin.cpp:18-25 qmatmul, :31-35 mlp_forward, :161-169 lm_head) and the
 // greedy mx::argmax that follows the lm_head (src/sampling/sampler.cpp:14-16).
 //
-// Data path (per CTA):
-//   * Weights stream HBM -> shared memory by 1-D TMA bulk copies (cp.async.bulk, one per packed row
-//     into a padded row so the fragment loads are bank-conflict free, one for each tile's scales
-//     and biases).  They are issued BEFORE griddepcontrol.wait: a kernel launched with
-//     programmatic stream serialization fetches its weights while the previous kernel finishes.
-//   * Activations (optionally RMSNorm'ed on the fly) are split into bf16 planes (1 plane for bf16
-//     activations, 3 exact hi/mid/lo planes for binary32) and stored pre-permuted in shared memory
-//     in mma.sync A-fragment order, together with per-(plane row, group) sums.
-//   * Nibbles become bf16 (1 + q/16) with one LOP3 per pair (exact); mma.sync m16n8k16 (bf16 in,
-//     fp32 accumulate) with the weights as the B operand (8 weight rows per n8 tile) produces, per
-//     64-group, D = sum x*(1+q/16).  The group result is folded as
+// Data path:
+//   * Weights stream HBM -> shared memory by 1-D TMA bulk copies (cp.async.bulk; one per packed row
+//     into a padded row so the fragment loads are bank-conflict free, one each for a block's scales
+//     and biases).  The decode kernels issue them BEFORE griddepcontrol.wait: launched with
+//     programmatic stream serialization, a kernel fetches its weights while its predecessor runs.
+//   * Activations (optionally RMSNorm'ed on the fly) become bf16 planes — 1 for bf16 activations,
+//     3 exact hi/mid/lo planes for binary32 — stored pre-permuted in mma.sync A-fragment order,
+//     with per-(plane row, 64-group) sums.
+//   * K is split across the warps of a CTA: each warp loads a group's A fragments once and reuses
+//     them for all the CTA's 8-row weight tiles.  Nibbles become bf16 (1 + q/16) with one LOP3 per
+//     pair (exact); mma.sync m16n8k16 (bf16 in, fp32 accumulate; weights as the B operand, 8 rows
+//     per n8 tile) gives per group D = sum x*(1+q/16), folded as
 //        y += 16*s*D + (b - 16*s)*sum(x)  ==  s*sum(x*q) + b*sum(x)
-//     so the per-group scale/bias stay in fp32 exactly as the reference's dequant formula says.
-//   * K is split across the CTA's warps; partials meet in shared memory for the epilogue
-//     (store / SwiGLU of gate+up rows / residual add).
+//     so the per-group scale/bias stay binary32 as in the reference's dequant formula.  Partials
+//     meet in shared memory for the epilogue (store / SwiGLU of gate+up rows / residual add).
 //
-// The lm_head kernel streams the vocabulary with a per-warp TMA ring and reduces the argmax on the
-// fly: packed (ordered value << 32 | ~index) keys, one atomicMax per CTA and row, the last CTA
-// decoding and re-zeroing the keys.  Logits are never written to memory.
+// Why mma.sync and not tcgen05 here: at M <= 32 the kernel is HBM-bound at 0.5625 B/weight; a
+// tcgen05 operand must sit in shared memory in bf16, i.e. 2 B/weight written plus 2 B/weight read
+// per weight, which exceeds shared-memory bandwidth at HBM rate.  Register-level dequant feeding
+// mma.sync keeps the dequantized weights out of shared memory.
+//
+// The lm_head kernel is persistent: a producer warp streams 32-row vocabulary blocks through a
+// TMA ring, 8 consumer warps split K, and the argmax is reduced on the fly with packed
+// (ordered value << 32 | ~index) keys, one atomicMax per CTA and row, the last CTA decoding and
+// re-zeroing the keys.  Logits are never written to memory.
 #include "common.cuh"
 #include "q4_gemv.cuh"
+
+#include <cuda.h>
 
 #include <algorithm>
 
 namespace marlin {
-
 namespace {
 
 constexpr int kGroup = 64;
-constexpr int kMaxThreads = 256;
 
 // ------------------------------------------------------------------------------------------------
 // shared-memory geometry
@@ -60,207 +66,340 @@ __device__ __forceinline__ float load_act(const void* x, int dtype, int64_t i) {
     return static_cast<const float*>(x)[i];
 }
 
-// position of element e (0..15) of a 16-element slot in mma A-fragment order
-// (slot order: 0,4,1,5,2,6,3,7,8,12,9,13,10,14,11,15)
-__device__ __forceinline__ int frag_pos(int e) { return (e & 8) | ((e & 3) << 1) | ((e >> 2) & 1); }
-
 struct XGeom {
     uint8_t* xp;  // planes: row r = plane*M + m, stride XRS bytes, GC groups of 128 B
     float* xs;    // [M_eff][GC] plane sums per group
     float* rf;    // [M] RMSNorm factors
-    float* scr;   // >= 32 floats reduction scratch
+    float* ssq;   // [M * K/8] per-unit sums of squares (norm only)
     int M, P, M_eff, XRS, GC;
 };
 
-// RMSNorm factors r_m = 1/sqrt(mean(x^2) + eps) as MLX's C++ API evaluates
-// x * rsqrt(mean(square(x)) + eps) * (1.0f + w)  (src/model/marlin.cpp:12-16):
-// bf16 x: square and mean in bf16 (binary32 accumulation, one bf16 rounding of the sum);
-// binary32 x: all binary32.  The `+ eps` and everything after it is binary32.
-__device__ void compute_norm_factors(const void* x, int dtype, int M, int K, float eps, const XGeom& g) {
-    const int nt = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int m = 0; m < M; ++m) {
-        float part = 0.f;
-        for (int k = tid; k < K; k += nt) {
-            float v = load_act(x, dtype, (int64_t)m * K + k);
-            float sq = __fmul_rn(v, v);
-            if (dtype == kBF16) sq = bf16_round(sq);
-            part = __fadd_rn(part, sq);
-        }
+// Eight consecutive activations starting at element i (i % 8 == 0), as binary32.
+__device__ __forceinline__ void load8(const void* x, int dtype, int64_t i, float v[8]) {
+    if (dtype == kBF16) {
+        const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + i);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-        for (int o = 16; o; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
-        if (lane == 0) g.scr[warp] = part;
-        __syncthreads();
-        if (tid == 0) {
-            float sum = 0.f;
-            for (int w = 0; w < nt / 32; ++w) sum = __fadd_rn(sum, g.scr[w]);
+        for (int j = 0; j < 4; ++j) {
+            v[2 * j] = bf16_bits_to_f32(w[j] & 0xffffu);
+            v[2 * j + 1] = bf16_bits_to_f32(w[j] >> 16);
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + i);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + i + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+// Sum of squares of one 8-element unit as MLX's C++ rms_norm evaluates mean(square(x))
+// (src/model/marlin.cpp:13): bf16 x squares round to bf16; binary32 x stays binary32.
+__device__ __forceinline__ float unit_ssq(const float v[8], int dtype) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float sq = __fmul_rn(v[j], v[j]);
+        if (dtype == kBF16) sq = bf16_round(sq);
+        s = __fadd_rn(s, sq);
+    }
+    return s;
+}
+
+// Row factors r_m = 1/sqrt(mean + eps) from the per-unit sums in g.ssq (fixed order: units
+// lane-strided, then a shuffle tree).  bf16 x: the sum and the mean round to bf16; the `+ eps`
+// (a C++ float, src/core/config.h:20) and everything after it is binary32.  Ends with a barrier.
+__device__ void finish_norm_factors(int dtype, int M, int K, float eps, const XGeom& g) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int upr = K / 8;
+    for (int m = warp; m < M; m += nw) {
+        float s = 0.f;
+        for (int u = lane; u < upr; u += 32) s = __fadd_rn(s, g.ssq[m * upr + u]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == 0) {
             float var;
             if (dtype == kBF16)
-                var = bf16_round(__fmul_rn(bf16_round(sum), bf16_round((float)(1.0 / (double)K))));
+                var = bf16_round(__fmul_rn(bf16_round(s), bf16_round((float)(1.0 / (double)K))));
             else
-                var = __fmul_rn(sum, (float)(1.0 / (double)K));
+                var = __fmul_rn(s, (float)(1.0 / (double)K));
             g.rf[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
         }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) { return lo | (hi << 16); }
+
+// Emit one 8-element unit (row m, unit ul of the staged chunk): optional RMSNorm, split into
+// planes, one 16-byte store per plane at slot positions 8*(ul & 1) + {0,2,4,6,1,3,5,7}, and the
+// plane sums of the unit's 64-group (the 8 units of a group are 8 consecutive lanes: a 3-step
+// shuffle tree).  Every lane of the warp must call it (ok = false contributes nothing).
+__device__ __forceinline__ void emit_unit(float (&v)[8], uint4 nwv, int m, int ul, bool ok, bool normed,
+                                          const XGeom& g) {
+    const int lane = threadIdx.x & 31, P = g.P;
+    float ps[3] = {0.f, 0.f, 0.f};
+    if (ok) {
+        if (normed) {
+            const float r = g.rf[m];
+            const uint32_t w4[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float wj = bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+                v[j] = __fmul_rn(__fmul_rn(v[j], r), __fadd_rn(1.0f, wj));
+            }
+        }
+        uint32_t h[3][8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            h[0][j] = f32_to_bf16_bits(v[j]);
+            if (P == 3) {
+                const float r1 = __fsub_rn(v[j], bf16_bits_to_f32(h[0][j]));
+                h[1][j] = f32_to_bf16_bits(r1);
+                h[2][j] = f32_to_bf16_bits(__fsub_rn(r1, bf16_bits_to_f32(h[1][j])));
+            }
+        }
+        const int gl = ul >> 3, e0 = (ul & 7) * 8;
+        const uint32_t off = gl * 128 + (e0 >> 4) * 32 + ((e0 >> 3) & 1) * 16;
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+            if (p < P) {
+                uint4 st;
+                st.x = pack_bf16x2(h[p][0], h[p][4]);
+                st.y = pack_bf16x2(h[p][1], h[p][5]);
+                st.z = pack_bf16x2(h[p][2], h[p][6]);
+                st.w = pack_bf16x2(h[p][3], h[p][7]);
+                *reinterpret_cast<uint4*>(g.xp + (uint32_t)(p * g.M + m) * g.XRS + off) = st;
+                float s = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s += bf16_bits_to_f32(h[p][j]);
+                ps[p] = s;
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        if (p < P) {
+            float s = ps[p];
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            if (ok && (lane & 7) == 0) g.xs[(p * g.M + m) * g.GC + (ul >> 3)] = s;
+        }
+    }
+}
+
+// Stage activation groups [gc0, gc0 + ngc) of x[M, K] into g (RMSNorm factors must already be in
+// g.rf when norm_w is set).  Loads of a pass are all issued before use.  Ends with __syncthreads.
+__device__ void stage_chunk(const void* x, int dtype, int K, const uint16_t* norm_w, int gc0, int ngc,
+                            const XGeom& g) {
+    const int nt = blockDim.x, lane = threadIdx.x & 31;
+    const int upr = ngc * 8, total = g.M * upr;
+    const int k0c = gc0 * kGroup;
+    constexpr int U = 2;
+    for (int base = (int)threadIdx.x - lane; base < total; base += nt * U) {  // warp-uniform trip count
+        float v[U][8];
+        uint4 nwv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + lane + u * nt;
+            if (idx < total) {
+                const int m = idx / upr, k = k0c + (idx % upr) * 8;
+                load8(x, dtype, (int64_t)m * K + k, v[u]);
+                if (norm_w) nwv[u] = *reinterpret_cast<const uint4*>(norm_w + k);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + lane + u * nt;
+            const bool ok = idx < total;
+            emit_unit(v[u], nwv[u], ok ? idx / upr : 0, ok ? idx % upr : 0, ok, norm_w != nullptr, g);
+        }
+    }
+    __syncthreads();
+}
+
+// Per-unit sums of squares of the whole x[M, K] into g.ssq, then the row factors.
+__device__ void norm_factors_only(const void* x, int dtype, int K, float eps, const XGeom& g) {
+    const int nt = blockDim.x, upr = K / 8, total = g.M * upr;
+    for (int base = (int)threadIdx.x; base < total; base += nt * 2) {
+        float v[2][8];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = base + u * nt;
+            if (idx < total) load8(x, dtype, (int64_t)(idx / upr) * K + (idx % upr) * 8, v[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = base + u * nt;
+            if (idx < total) g.ssq[idx] = unit_ssq(v[u], dtype);
+        }
+    }
+    __syncthreads();
+    finish_norm_factors(dtype, g.M, K, eps, g);
+}
+
+// Whole-K staging.  When the activations fit in two 8-element units per thread: one pass (load,
+// sums of squares, row factors, planes — one global round trip).  Otherwise norm factors in one
+// pass and planes in a second (an L1 hit).  Ends with __syncthreads.
+__device__ void stage_all(const void* x, int dtype, int K, const uint16_t* norm_w, float eps, const XGeom& g) {
+    const int nt = blockDim.x;
+    const int upr = K / 8, total = g.M * upr;
+    if (total > 2 * nt) {
+        if (norm_w) norm_factors_only(x, dtype, K, eps, g);
+        stage_chunk(x, dtype, K, norm_w, 0, K / kGroup, g);
+        return;
+    }
+    float v[2][8];
+    uint4 nwv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int idx = (int)threadIdx.x + u * nt;
+        if (idx < total) {
+            const int k = (idx % upr) * 8;
+            load8(x, dtype, (int64_t)(idx / upr) * K + k, v[u]);
+            if (norm_w) nwv[u] = *reinterpret_cast<const uint4*>(norm_w + k);
+        }
+    }
+    if (norm_w) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = (int)threadIdx.x + u * nt;
+            if (idx < total) g.ssq[idx] = unit_ssq(v[u], dtype);
+        }
         __syncthreads();
+        finish_norm_factors(dtype, g.M, K, eps, g);
     }
-}
-
-// Stage groups [gc0, gc0 + ngc) of the activations into planes + sums.  Ends with __syncthreads.
-__device__ void stage_x_chunk(const void* x, int dtype, int K, const uint16_t* norm_w, int gc0, int ngc,
-                              const XGeom& g) {
-    const int nt = blockDim.x, tid = threadIdx.x;
-    const int kc0 = gc0 * kGroup, kcn = ngc * kGroup;
-    const int total = g.M * kcn;
-    for (int idx = tid; idx < total; idx += nt) {
-        const int m = idx / kcn, kl = idx - m * kcn, k = kc0 + kl;
-        const int gl = kl >> 6, e = kl & 63, t = e >> 4, pos = frag_pos(e & 15);
-        const uint32_t off = gl * 128 + t * 32 + pos * 2;
-        float v = load_act(x, dtype, (int64_t)m * K + k);
-        if (norm_w) v = __fmul_rn(__fmul_rn(v, g.rf[m]), __fadd_rn(1.0f, bf16_bits_to_f32(norm_w[k])));
-        if (g.P == 1) {
-            uint16_t h = (dtype == kBF16 && !norm_w) ? static_cast<const uint16_t*>(x)[(int64_t)m * K + k]
-                                                      : (uint16_t)f32_to_bf16_bits(v);
-            *reinterpret_cast<uint16_t*>(g.xp + (uint32_t)m * g.XRS + off) = h;
-        } else {
-            uint32_t h0 = f32_to_bf16_bits(v);
-            float r1 = __fsub_rn(v, bf16_bits_to_f32(h0));
-            uint32_t h1 = f32_to_bf16_bits(r1);
-            float r2 = __fsub_rn(r1, bf16_bits_to_f32(h1));
-            uint32_t h2 = f32_to_bf16_bits(r2);
-            *reinterpret_cast<uint16_t*>(g.xp + (uint32_t)m * g.XRS + off) = (uint16_t)h0;
-            *reinterpret_cast<uint16_t*>(g.xp + (uint32_t)(g.M + m) * g.XRS + off) = (uint16_t)h1;
-            *reinterpret_cast<uint16_t*>(g.xp + (uint32_t)(2 * g.M + m) * g.XRS + off) = (uint16_t)h2;
-        }
-    }
-    __syncthreads();
-    for (int idx = tid; idx < g.M_eff * ngc; idx += nt) {
-        const int r = idx / ngc, gl = idx - r * ngc;
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(g.xp + (uint32_t)r * g.XRS + gl * 128);
-        float s = 0.f;
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-            uint32_t v = p[j];
-            s += bf16_bits_to_f32(v & 0xffffu) + bf16_bits_to_f32(v >> 16);
-        }
-        g.xs[r * g.GC + gl] = s;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int idx = (int)threadIdx.x + u * nt;  // idx % 32 == lane: groups are lane-aligned
+        const bool ok = idx < total;
+        emit_unit(v[u], nwv[u], ok ? idx / upr : 0, ok ? idx % upr : 0, ok, norm_w != nullptr, g);
     }
     __syncthreads();
 }
 
 // ------------------------------------------------------------------------------------------------
-// per-warp tensor-core group loop
+// tensor-core group step
 // ------------------------------------------------------------------------------------------------
-// Scale table entry (group, row): (16*s, b - 16*s), built once per tile and K range.
-__device__ __forceinline__ void build_sb_table(const uint16_t* s_tile, const uint16_t* b_tile, int G,
-                                               int g0, int g1, float2* table) {
-    const int lane = threadIdx.x & 31;
-    const int cnt = (g1 - g0) * 8;
-    for (int e = lane; e < cnt; e += 32) {
-        const int gg = g0 + (e >> 3), n = e & 7;
-        const float s = bf16_bits_to_f32(s_tile[n * G + gg]);
-        const float b = bf16_bits_to_f32(b_tile[n * G + gg]);
-        const float s16 = s * 16.0f;
-        table[gg * 8 + n] = make_float2(s16, b - s16);
-    }
-}
-
-// acc[nb][mt][0..3]: rows (mt*16+g, mt*16+g+8) x weight rows (2t, 2t+1) of tile nb.
-// Groups [g0, g1) of the weights; the staged activation chunk starts at group gx0.
-template <int NB, int MT, bool HALF>
-__device__ __forceinline__ void mma_groups(const uint8_t* const (&wt)[NB], int RS,
-                                           const float2* const (&sbt)[NB], const uint8_t* xp, int XRS,
-                                           const float* xs, int GC, int M_eff, int g0, int g1, int gx0,
-                                           float (&acc)[NB][MT][4]) {
+template <int MT, bool HALF>
+__device__ __forceinline__ void load_a(const uint8_t* xp, int XRS, const float* xs, int GC, int M_eff, int gl,
+                                       uint32_t (&A)[MT][2][8], float (&X)[MT][2]) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-#pragma unroll 1
-    for (int gg = g0; gg < g1; ++gg) {
-        const int gl = gg - gx0;
-        uint32_t A[MT][2][8];
-        float X[MT][2];
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
+    for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = mt * 16 + h * 8 + g;
-                if ((HALF && h == 1) || r >= M_eff) {
+        for (int h = 0; h < 2; ++h) {
+            const int r = mt * 16 + h * 8 + g;
+            if ((HALF && h == 1) || r >= M_eff) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) A[mt][h][j] = 0u;
-                    X[mt][h] = 0.f;
-                } else {
-                    const uint8_t* p = xp + (uint32_t)r * XRS + gl * 128 + t * 32;
-                    const uint4 lo = lds128(p), hi = lds128(p + 16);
-                    A[mt][h][0] = lo.x; A[mt][h][1] = lo.y; A[mt][h][2] = lo.z; A[mt][h][3] = lo.w;
-                    A[mt][h][4] = hi.x; A[mt][h][5] = hi.y; A[mt][h][6] = hi.z; A[mt][h][7] = hi.w;
-                    X[mt][h] = xs[r * GC + gl];
-                }
-            }
-        }
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-            const uint2 wv = lds64(wt[nb] + g * RS + gg * 32 + t * 8);
-            uint32_t p0[4], p1[4];
-            q4_pairs(wv.x, p0);
-            q4_pairs(wv.y, p1);
-            const float4 sb = *reinterpret_cast<const float4*>(sbt[nb] + gg * 8 + 2 * t);
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                float d[4] = {0.f, 0.f, 0.f, 0.f};
-                mma_bf16_16816(d, A[mt][0][0], A[mt][1][0], A[mt][0][1], A[mt][1][1], p0[0], p0[1]);
-                mma_bf16_16816(d, A[mt][0][2], A[mt][1][2], A[mt][0][3], A[mt][1][3], p0[2], p0[3]);
-                mma_bf16_16816(d, A[mt][0][4], A[mt][1][4], A[mt][0][5], A[mt][1][5], p1[0], p1[1]);
-                mma_bf16_16816(d, A[mt][0][6], A[mt][1][6], A[mt][0][7], A[mt][1][7], p1[2], p1[3]);
-                acc[nb][mt][0] = fmaf(sb.x, d[0], fmaf(sb.y, X[mt][0], acc[nb][mt][0]));
-                acc[nb][mt][1] = fmaf(sb.z, d[1], fmaf(sb.w, X[mt][0], acc[nb][mt][1]));
-                if (!HALF) {
-                    acc[nb][mt][2] = fmaf(sb.x, d[2], fmaf(sb.y, X[mt][1], acc[nb][mt][2]));
-                    acc[nb][mt][3] = fmaf(sb.z, d[3], fmaf(sb.w, X[mt][1], acc[nb][mt][3]));
-                }
+                for (int j = 0; j < 8; ++j) A[mt][h][j] = 0u;
+                X[mt][h] = 0.f;
+            } else {
+                const uint8_t* p = xp + (uint32_t)r * XRS + gl * 128 + t * 32;
+                const uint4 lo = lds128(p), hi = lds128(p + 16);
+                A[mt][h][0] = lo.x; A[mt][h][1] = lo.y; A[mt][h][2] = lo.z; A[mt][h][3] = lo.w;
+                A[mt][h][4] = hi.x; A[mt][h][5] = hi.y; A[mt][h][6] = hi.z; A[mt][h][7] = hi.w;
+                X[mt][h] = xs[r * GC + gl];
             }
         }
     }
 }
 
-// Issue the TMA copies of one 8-row weight tile (rows [row0, row0+8) of W) into `tile`.
-// Returns the byte count (for expect_tx).  Scales/biases of a partial tile are not copied here.
-__device__ __forceinline__ uint32_t tile_bytes_expected(const Q4Mat& W, int64_t row0) {
-    const int64_t rows = (int64_t)min((long long)8, max((long long)0, (long long)(W.n - row0)));
+// One 64-group of one 8-row tile: D = x . (1 + q/16) as two independent 2-step mma chains
+// (steps 0-1 and 2-3), folded into acc with the group's (16 s, b - 16 s) for rows (2t, 2t+1).
+template <int MT, bool HALF>
+__device__ __forceinline__ void group_mma(const uint32_t (&A)[MT][2][8], const float (&X)[MT][2], uint2 wv,
+                                          float4 sb, float (&acc)[MT][4]) {
+    uint32_t p0[4], p1[4];
+    q4_pairs(wv.x, p0);
+    q4_pairs(wv.y, p1);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_bf16_16816(d0, A[mt][0][0], A[mt][1][0], A[mt][0][1], A[mt][1][1], p0[0], p0[1]);
+        mma_bf16_16816(d1, A[mt][0][4], A[mt][1][4], A[mt][0][5], A[mt][1][5], p1[0], p1[1]);
+        mma_bf16_16816(d0, A[mt][0][2], A[mt][1][2], A[mt][0][3], A[mt][1][3], p0[2], p0[3]);
+        mma_bf16_16816(d1, A[mt][0][6], A[mt][1][6], A[mt][0][7], A[mt][1][7], p1[2], p1[3]);
+        acc[mt][0] = fmaf(sb.x, d0[0] + d1[0], fmaf(sb.y, X[mt][0], acc[mt][0]));
+        acc[mt][1] = fmaf(sb.z, d0[1] + d1[1], fmaf(sb.w, X[mt][0], acc[mt][1]));
+        if (!HALF) {
+            acc[mt][2] = fmaf(sb.x, d0[2] + d1[2], fmaf(sb.y, X[mt][1], acc[mt][2]));
+            acc[mt][3] = fmaf(sb.z, d0[3] + d1[3], fmaf(sb.w, X[mt][1], acc[mt][3]));
+        }
+    }
+}
+
+// Scale-table entry of one (row, group): (16*s, b - 16*s).
+__device__ __forceinline__ float2 sb_entry(float s, float b) {
+    const float s16 = s * 16.0f;
+    return make_float2(s16, b - s16);
+}
+
+// ------------------------------------------------------------------------------------------------
+// TMA issue helpers
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ int64_t rows_in(const Q4Mat& W, int64_t row0, int64_t R) {
+    return (int64_t)min((long long)R, max((long long)0, (long long)(W.n - row0)));
+}
+// Bytes the copies of an R-row block (rows [row0, row0 + R) of W) deliver: packed rows always,
+// scales/biases only for a full block (a partial block's are read with plain loads).
+__device__ __forceinline__ uint32_t block_bytes(const Q4Mat& W, int64_t row0, int R) {
+    const int64_t rows = rows_in(W, row0, R);
     const int G = (int)(W.k / kGroup);
     uint32_t bytes = (uint32_t)(rows * (W.k / 2));
-    if (rows == 8) bytes += 2u * 8u * G * 2u;
+    if (rows == R) bytes += 2u * (uint32_t)R * G * 2u;
     return bytes;
 }
-__device__ __forceinline__ void issue_tile(const Q4Mat& W, int64_t row0, uint8_t* tile, int RS, uint64_t* bar) {
-    const int64_t rows = (int64_t)min((long long)8, max((long long)0, (long long)(W.n - row0)));
+// Copies into: packed rows at dst + r*RS, scales at sdst [R][G], biases at sdst + R*G*2 bytes.
+__device__ __forceinline__ void issue_block(const Q4Mat& W, int64_t row0, int R, uint8_t* dst, int RS,
+                                            uint8_t* sdst, uint64_t* bar) {
+    const int64_t rows = rows_in(W, row0, R);
     const int G = (int)(W.k / kGroup);
     const uint32_t rb = (uint32_t)(W.k / 2);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(W.w) + row0 * (int64_t)rb;
-    for (int r = 0; r < rows; ++r) tma_bulk_g2s(tile + r * RS, src + (int64_t)r * rb, rb, bar);
-    if (rows == 8) {
-        uint8_t* sdst = tile + 8 * RS;
-        tma_bulk_g2s(sdst, W.s + row0 * G, 8u * G * 2u, bar);
-        tma_bulk_g2s(sdst + 8 * G * 2, W.b + row0 * G, 8u * G * 2u, bar);
-    }
-}
-// Scales/biases of a partial tile, loaded by one warp with plain loads.
-__device__ __forceinline__ void load_partial_scales(const Q4Mat& W, int64_t row0, uint8_t* tile, int RS) {
-    const int64_t rows = (int64_t)min((long long)8, max((long long)0, (long long)(W.n - row0)));
-    if (rows == 8) return;
-    const int G = (int)(W.k / kGroup);
-    uint16_t* sd = reinterpret_cast<uint16_t*>(tile + 8 * RS);
-    uint16_t* bd = sd + 8 * G;
-    for (int e = threadIdx.x & 31; e < 8 * G; e += 32) {
-        const int r = e / G;
-        const bool ok = r < rows;
-        sd[e] = ok ? W.s[row0 * G + e] : (uint16_t)0;
-        bd[e] = ok ? W.b[row0 * G + e] : (uint16_t)0;
+    for (int r = 0; r < rows; ++r) tma_bulk_g2s(dst + r * RS, src + (int64_t)r * rb, rb, bar);
+    if (rows == R) {
+        tma_bulk_g2s(sdst, W.s + row0 * G, (uint32_t)R * G * 2u, bar);
+        tma_bulk_g2s(sdst + R * G * 2, W.b + row0 * G, (uint32_t)R * G * 2u, bar);
     }
 }
 
 // ------------------------------------------------------------------------------------------------
-// unit kernel: one CTA = NWR warp rows x NB tiles x 8 weight rows, K split over NWK warps
+// weight block layouts in shared memory
 // ------------------------------------------------------------------------------------------------
+// Row copies (any K): each packed row is one 1-D bulk copy into a row padded to RS bytes; tile
+// column n of the mma is physical row n.  Used when a block has fewer than 32 rows (boxes would be
+// under 4 KB) — with K >= 4096 the rows are >= 2 KB, which keeps the copy engine efficient.
+//
+// Swizzled boxes (2-D tensor map, 128-byte swizzle): a block of BR rows arrives as ceil(K/256)
+// boxes of [BR rows x 128 B] (4 KB at BR = 32), box c holding words [32c, 32c+32) of every row; the
+// hardware XORs the 16-byte unit index of row r with r & 7.  Tile column n maps to physical row
+// perm(n) = 2(n&3) + (n>>2), so a half-warp's four rows are {0,2,4,6} (or {1,3,5,7}) and the
+// XORed units of one 64-group are all distinct: conflict-free 8-byte fragment loads.
+__device__ __forceinline__ int col_to_row(int n) { return 2 * (n & 3) + (n >> 2); }
+
+// Address of the 8 packed bytes thread (g, t4) feeds the mma for tile row block `r8` (multiple of
+// 8), group gg.
+template <bool SWZ>
+__device__ __forceinline__ const uint8_t* frag_addr(const uint8_t* blk, int BR, int RS, int r8, int g, int t4, int gg) {
+    if (SWZ) {
+        const int pr = col_to_row(g);
+        const int j = (2 * (gg & 3) + (t4 >> 1)) ^ pr;
+        return blk + (gg >> 2) * (BR * 128) + (r8 + pr) * 128 + j * 16 + (t4 & 1) * 8;
+    }
+    return blk + (r8 + g) * RS + gg * 32 + t4 * 8;
+}
+
+// ------------------------------------------------------------------------------------------------
+// decode GEMV (one CTA per row block, weights fetched before the PDL wait)
+// ------------------------------------------------------------------------------------------------
+// A CTA owns NT 8-row tiles (kEpiSwiglu: NT/2 gate tiles and the NT/2 up tiles of the same
+// features) and splits K over its NWK warps: the CTA stages the activations, then every warp runs
+// its K range over all NT tiles, loading each group's A fragments once.
 struct UnitArgs {
+    CUtensorMap tm0, tm1;  // SWZ layout: tensor maps of w0 / w1 packed words [n][k/8]
     GemvLaunch L;
-    int P, M_eff, G, NWR, NWK, GC, RS, XRS;
+    int P, M_eff, G, NWK, GC, RS, XRS, BR, nchunk;
     uint32_t tbytes, off_tiles, off_sb, off_xp, off_xs, off_red, off_scr, off_bar;
 };
 
@@ -275,134 +414,158 @@ __device__ __forceinline__ float swiglu_apply(float gv, float uv, int dtype) {
     return (sg * gv) * uv;
 }
 
-template <int NB, int MT, bool HALF, int EPI>
-__global__ void __launch_bounds__(kMaxThreads) q4_unit_kernel(const __grid_constant__ UnitArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+template <int NT, int MT, bool HALF, int EPI, bool SWZ>
+__global__ void __launch_bounds__(256, 2) q4_unit_kernel(const __grid_constant__ UnitArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const GemvLaunch& L = a.L;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int NWR = a.NWR, NWK = a.NWK, G = a.G;
-    const int wr = warp % NWR, wk = warp / NWR;
+    const int tid = threadIdx.x, wk = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int NWK = a.NWK, G = a.G;
+    constexpr int HT = EPI == kEpiSwiglu ? NT / 2 : NT;  // output tiles (= tiles per matrix)
+    constexpr int NMAT = EPI == kEpiSwiglu ? 2 : 1;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + a.off_bar);
-    uint8_t* tiles = smem + a.off_tiles;
-    float2* sbt_all = reinterpret_cast<float2*>(smem + a.off_sb);
-    float* red = reinterpret_cast<float*>(smem + a.off_red);
+    uint8_t* wbase = smem + a.off_tiles;
+    float2* sbt = reinterpret_cast<float2*>(smem + a.off_sb);  // [NT][G][8 columns]
+    float* red = reinterpret_cast<float*>(smem + a.off_red);   // [NWK][NT][M_eff][8 columns]
     XGeom xg{smem + a.off_xp, reinterpret_cast<float*>(smem + a.off_xs),
              reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
              (int)L.m, a.P, a.M_eff, a.XRS, a.GC};
 
-    // weight rows of tile (r, nb)
-    const int64_t unit_rows = (int64_t)NWR * 8 * (EPI == kEpiSwiglu ? 1 : NB);
-    const int64_t base = (int64_t)blockIdx.x * unit_rows;
-    auto tile_row0 = [&](int r, int nb) -> int64_t {
-        return EPI == kEpiSwiglu ? base + r * 8 : base + (int64_t)(r * NB + nb) * 8;
-    };
-    auto tile_mat = [&](int nb) -> const Q4Mat& { return (EPI == kEpiSwiglu && nb == 1) ? L.w1 : L.w0; };
+    const int64_t base = (int64_t)blockIdx.x * HT * 8;
+    auto mat_of = [&](int t) -> int { return (EPI == kEpiSwiglu && t >= HT) ? 1 : 0; };
+    auto tile_mat = [&](int t) -> const Q4Mat& { return mat_of(t) ? L.w1 : L.w0; };
+    auto tile_row0 = [&](int t) -> int64_t { return base + (int64_t)(t % HT) * 8; };
+    // SWZ: one block per matrix (packed boxes, then scales [BR][G], biases [BR][G]);
+    // row copies: one tile per t (packed rows, scales [8][G], biases [8][G]).
+    auto blk_of = [&](int t) -> uint8_t* { return SWZ ? wbase + mat_of(t) * a.tbytes : wbase + t * a.tbytes; };
+    const int BR = SWZ ? a.BR : 8;
+    const uint32_t packed = SWZ ? (uint32_t)a.nchunk * a.BR * 128 : 8u * a.RS;
 
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
         uint32_t bytes = 0;
-        for (int r = 0; r < NWR; ++r)
-            for (int nb = 0; nb < NB; ++nb) bytes += tile_bytes_expected(tile_mat(nb), tile_row0(r, nb));
-        mbar_arrive_expect_tx(bar, bytes);
-        for (int r = 0; r < NWR; ++r)
-            for (int nb = 0; nb < NB; ++nb)
-                issue_tile(tile_mat(nb), tile_row0(r, nb), tiles + (r * NB + nb) * a.tbytes, a.RS, bar);
+        if (SWZ) {
+            for (int m = 0; m < NMAT; ++m) {
+                bytes += packed;
+                if (rows_in(m ? L.w1 : L.w0, base, BR) == BR) bytes += 2u * BR * G * 2u;
+            }
+            mbar_arrive_expect_tx(bar, bytes);
+            for (int m = 0; m < NMAT; ++m) {
+                const Q4Mat& W = m ? L.w1 : L.w0;
+                const CUtensorMap* tm = m ? &a.tm1 : &a.tm0;
+                uint8_t* blk = wbase + m * a.tbytes;
+                for (int c = 0; c < a.nchunk; ++c) tma_load_2d(blk + c * BR * 128, tm, c * 32, (int32_t)base, bar);
+                if (rows_in(W, base, BR) == BR) {
+                    tma_bulk_g2s(blk + packed, W.s + base * G, (uint32_t)BR * G * 2u, bar);
+                    tma_bulk_g2s(blk + packed + BR * G * 2, W.b + base * G, (uint32_t)BR * G * 2u, bar);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) bytes += block_bytes(tile_mat(t), tile_row0(t), 8);
+            mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                uint8_t* tb = wbase + t * a.tbytes;
+                issue_block(tile_mat(t), tile_row0(t), 8, tb, a.RS, tb + packed, bar);
+            }
+        }
     }
     // Everything above is independent of the previous kernel; activations below are not.
     pdl_wait();
     pdl_launch_dependents();
 
-    if (L.norm_w) compute_norm_factors(L.x, L.x_dtype, (int)L.m, (int)L.w0.k, L.eps, xg);
-
-    // this warp's tiles and group range
+    const int K = (int)L.w0.k;
     const int g0 = wk * G / NWK, g1 = (wk + 1) * G / NWK;
-    const uint8_t* wt[NB];
-    const float2* sbt[NB];
-    float2* sbt_w[NB];
+    float acc[NT][MT][4];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-        uint8_t* tb = tiles + (wr * NB + nb) * a.tbytes;
-        wt[nb] = tb;
-        sbt_w[nb] = sbt_all + (size_t)(wr * NB + nb) * G * 8;
-        sbt[nb] = sbt_w[nb];
-    }
-    float acc[NB][MT][4];
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[nb][mt][j] = 0.f;
+            for (int j = 0; j < 4; ++j) acc[t][mt][j] = 0.f;
 
-    bool weights_ready = false;
+    const bool chunked = a.GC < G;
+    if (!chunked) stage_all(L.x, L.x_dtype, K, L.norm_w, L.eps, xg);
+    else if (L.norm_w) norm_factors_only(L.x, L.x_dtype, K, L.eps, xg);
+
+    // weights: uniform across the CTA — a (recorded) timeout ends the whole CTA
+    if (!__syncthreads_and(mbar_wait(bar, 0) ? 1 : 0)) return;
+    // scale table for this warp's groups of every tile, indexed by mma column
+    // (partial blocks read their scales from global)
+    {
+        const int ng = g1 - g0, cnt = ng * 8 * NT;
+        for (int e = lane; e < cnt; e += 32) {
+            const int t = e / (ng * 8), rem = e - t * ng * 8, gg = g0 + (rem >> 3), n = rem & 7;
+            const Q4Mat& W = tile_mat(t);
+            const int pr = SWZ ? 8 * (t % HT) + col_to_row(n) : n;  // row within the smem block
+            const int64_t row = (SWZ ? base : tile_row0(t)) + pr;
+            float s = 0.f, b = 0.f;
+            if (rows_in(W, SWZ ? base : tile_row0(t), BR) == BR) {
+                const uint16_t* sp = reinterpret_cast<const uint16_t*>(blk_of(t) + packed);
+                s = bf16_bits_to_f32(sp[pr * G + gg]);
+                b = bf16_bits_to_f32(sp[BR * G + pr * G + gg]);
+            } else if (row < W.n) {
+                s = bf16_bits_to_f32(W.s[row * G + gg]);
+                b = bf16_bits_to_f32(W.b[row * G + gg]);
+            }
+            sbt[(t * G + gg) * 8 + n] = sb_entry(s, b);
+        }
+    }
+    __syncwarp();
+
     for (int gc0 = 0; gc0 < G; gc0 += a.GC) {
         const int ngc = min(a.GC, G - gc0);
-        stage_x_chunk(L.x, L.x_dtype, (int)L.w0.k, L.norm_w, gc0, ngc, xg);
-        if (!weights_ready) {
-            // uniform across the CTA: a timeout (recorded on the device) ends the whole CTA
-            if (!__syncthreads_and(mbar_wait(bar, 0) ? 1 : 0)) return;
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
-                if (wk == 0) load_partial_scales(tile_mat(nb), tile_row0(wr, nb), const_cast<uint8_t*>(wt[nb]), a.RS);
-            }
-            __syncthreads();
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb) {
-                const uint16_t* st = reinterpret_cast<const uint16_t*>(wt[nb] + 8 * a.RS);
-                build_sb_table(st, st + 8 * G, G, g0, g1, sbt_w[nb]);
-            }
-            __syncwarp();
-            weights_ready = true;
-        }
+        if (chunked) stage_chunk(L.x, L.x_dtype, K, L.norm_w, gc0, ngc, xg);
         const int lo = max(g0, gc0), hi = min(g1, gc0 + ngc);
-        if (lo < hi) mma_groups<NB, MT, HALF>(wt, a.RS, sbt, xg.xp, a.XRS, xg.xs, a.GC, a.M_eff, lo, hi, gc0, acc);
-        __syncthreads();  // chunk buffer reuse
+#pragma unroll 1
+        for (int gg = lo; gg < hi; ++gg) {
+            uint32_t A[MT][2][8];
+            float X[MT][2];
+            load_a<MT, HALF>(xg.xp, a.XRS, xg.xs, a.GC, a.M_eff, gg - gc0, A, X);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const uint2 wv = lds64(frag_addr<SWZ>(blk_of(t), BR, a.RS, SWZ ? 8 * (t % HT) : 0, g, t4, gg));
+                const float4 sb = *reinterpret_cast<const float4*>(sbt + (t * G + gg) * 8 + 2 * t4);
+                group_mma<MT, HALF>(A, X, wv, sb, acc[t]);
+            }
+        }
+        if (chunked) __syncthreads();  // chunk buffer reuse
     }
 
-    // partials -> shared memory: red[((wk*NWR + wr)*NB + nb)*M_eff*8 + r*8 + n]
-    {
-        const int g = lane >> 2, t = lane & 3;
+    // partials -> red[((wk*NT + t)*M_eff + r)*8 + column]
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                for (int h = 0; h < (HALF ? 1 : 2); ++h) {
-                    const int r = mt * 16 + h * 8 + g;
-                    if (r < a.M_eff) {
-                        float* dst = red + ((size_t)((wk * NWR + wr) * NB + nb) * a.M_eff + r) * 8 + 2 * t;
-                        *reinterpret_cast<float2*>(dst) = make_float2(acc[nb][mt][2 * h], acc[nb][mt][2 * h + 1]);
-                    }
-                }
-    }
+            for (int h = 0; h < (HALF ? 1 : 2); ++h) {
+                const int r = mt * 16 + h * 8 + g;
+                if (r < a.M_eff)
+                    *reinterpret_cast<float2*>(red + ((size_t)(wk * NT + t) * a.M_eff + r) * 8 + 2 * t4) =
+                        make_float2(acc[t][mt][2 * h], acc[t][mt][2 * h + 1]);
+            }
     __syncthreads();
 
-    // epilogue
     const int M = (int)L.m, P = a.P;
-    const int NBO = EPI == kEpiSwiglu ? 1 : NB;
-    const int total = NWR * NBO * M * 8;
-    auto gather = [&](int r_, int nb, int m, int n) -> float {
+    auto gather = [&](int t, int m, int n) -> float {
         float v = 0.f;
         for (int w = 0; w < NWK; ++w)
-            for (int p = 0; p < P; ++p)
-                v += red[((size_t)((w * NWR + r_) * NB + nb) * a.M_eff + (p * M + m)) * 8 + n];
+            for (int p = 0; p < P; ++p) v += red[((size_t)(w * NT + t) * a.M_eff + (p * M + m)) * 8 + n];
         return v;
     };
+    const int total = HT * M * 8;
     for (int o = tid; o < total; o += blockDim.x) {
-        const int n = o & 7;
-        int rest = o >> 3;
-        const int m = rest % M;
-        rest /= M;
-        const int nbo = rest % NBO, r_ = rest / NBO;
-        const int64_t row = tile_row0(r_, nbo) + n;
+        const int n = o & 7, rest = o >> 3, m = rest % M, t = rest / M;
+        const int64_t row = tile_row0(t) + (SWZ ? col_to_row(n) : n);
         if (row >= L.w0.n) continue;
         const int64_t yi = (int64_t)m * L.ldy + row;
         float v;
         if (EPI == kEpiSwiglu) {
-            v = swiglu_apply(gather(r_, 0, m, n), gather(r_, 1, m, n), L.y_dtype);
+            v = swiglu_apply(gather(t, m, n), gather(t + HT, m, n), L.y_dtype);
         } else {
-            v = gather(r_, nbo, m, n);
+            v = gather(t, m, n);
             if (EPI == kEpiResid) v = load_act(L.resid, L.resid_dtype, (int64_t)m * L.ldr + row) + v;
         }
         if (L.y_dtype == kBF16)
@@ -413,13 +576,20 @@ __global__ void __launch_bounds__(kMaxThreads) q4_unit_kernel(const __grid_const
 }
 
 // ------------------------------------------------------------------------------------------------
-// lm_head + argmax: persistent CTAs, per-warp TMA ring over 8-row vocabulary tiles
+// lm_head + argmax: persistent CTAs, producer warp + 8 consumer warps, 32-row blocks
 // ------------------------------------------------------------------------------------------------
+constexpr int kLmRows = 32;      // rows per block (4 tiles): 4 KB boxes
+constexpr int kLmTiles = 4;
+constexpr int kLmConsumers = 8;  // consumer warps (split K)
+constexpr int kLmThreads = 32 * (kLmConsumers + 1);
+constexpr int kLmMaxGroupsPerWarp = 8;
+
 struct LmArgs {
+    CUtensorMap tm;  // packed words [n][k/8], box [32 words][32 rows], 128-byte swizzle
     LmHeadLaunch L;
-    int P, M_eff, G, RS, XRS, D, nwarps;
-    int64_t ntiles;
-    uint32_t tbytes, off_ring, off_sb, off_xp, off_xs, off_scr, off_bar, off_out, off_keys;
+    int P, M_eff, G, XRS, S, nchunk;
+    int64_t nblocks;
+    uint32_t sbytes, packed, off_ring, off_sb, off_xp, off_xs, off_scr, off_bar, off_red, off_keys;
 };
 
 __device__ __forceinline__ unsigned long long pack_key(float v, int64_t idx) {
@@ -434,101 +604,162 @@ __device__ __forceinline__ void unpack_key(unsigned long long k, int32_t* id, fl
     *id = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
 }
 
+// Barrier among the 8 consumer warps (named barrier 1); returns the AND of `pred` over them.
+__device__ __forceinline__ bool consumers_and(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "n"(32 * kLmConsumers)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void lm_issue(const LmArgs& a, int64_t blk, uint8_t* st, uint64_t* bar) {
+    const int64_t row0 = blk * kLmRows;
+    const bool fullblk = rows_in(a.L.w, row0, kLmRows) == kLmRows;
+    const int G = a.G;
+    mbar_arrive_expect_tx(bar, a.packed + (fullblk ? 2u * kLmRows * G * 2u : 0u));
+    for (int c = 0; c < a.nchunk; ++c) tma_load_2d(st + c * kLmRows * 128, &a.tm, c * 32, (int32_t)row0, bar);
+    if (fullblk) {
+        tma_bulk_g2s(st + a.packed, a.L.w.s + row0 * G, (uint32_t)kLmRows * G * 2u, bar);
+        tma_bulk_g2s(st + a.packed + kLmRows * G * 2, a.L.w.b + row0 * G, (uint32_t)kLmRows * G * 2u, bar);
+    }
+}
+
 template <int MT, bool HALF>
-__global__ void __launch_bounds__(kMaxThreads) q4_lm_head_kernel(const __grid_constant__ LmArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kLmThreads, 1) q4_lm_head_kernel(const __grid_constant__ LmArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const LmHeadLaunch& L = a.L;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int D = a.D, G = a.G;
-    const int64_t TW = (int64_t)gridDim.x * a.nwarps;
-    const int64_t gw = (int64_t)blockIdx.x * a.nwarps + warp;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bar) + warp * D;
-    uint8_t* ring = smem + a.off_ring + (size_t)warp * D * a.tbytes;
-    float2* table = reinterpret_cast<float2*>(smem + a.off_sb) + (size_t)warp * G * 8;
-    float* wout = reinterpret_cast<float*>(smem + a.off_out) + (size_t)warp * a.M_eff * 8;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int G = a.G, S = a.S;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+    uint64_t* empty = full + S;
+    uint8_t* ring = smem + a.off_ring;
+    float* red = reinterpret_cast<float*>(smem + a.off_red);  // [2][8][M_eff][32 columns]
     unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);
     XGeom xg{smem + a.off_xp, reinterpret_cast<float*>(smem + a.off_xs),
              reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
              (int)L.m, a.P, a.M_eff, a.XRS, G};
+    const bool producer = warp == kLmConsumers;
 
-    if (lane == 0) {
-        for (int s = 0; s < D; ++s) mbar_init(&bars[s], 1);
+    if (tid == 0) {
+        prefetch_tmap(&a.tm);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kLmConsumers);
+        }
         fence_mbar_init();
-        for (int s = 0; s < D; ++s) {
-            const int64_t tile = gw + (int64_t)s * TW;
-            if (tile < a.ntiles) {
-                mbar_arrive_expect_tx(&bars[s], tile_bytes_expected(L.w, tile * 8));
-                issue_tile(L.w, tile * 8, ring + (size_t)s * a.tbytes, a.RS, &bars[s]);
-            }
+    }
+    __syncthreads();
+    if (producer && lane == 0) {
+        for (int s = 0; s < S; ++s) {
+            const int64_t blk = blockIdx.x + (int64_t)s * gridDim.x;
+            if (blk >= a.nblocks) break;
+            lm_issue(a, blk, ring + (size_t)s * a.sbytes, &full[s]);
         }
     }
     pdl_wait();
     pdl_launch_dependents();
-    if (L.norm_w) compute_norm_factors(L.x, L.x_dtype, (int)L.m, (int)L.w.k, L.eps, xg);
-    stage_x_chunk(L.x, L.x_dtype, (int)L.w.k, L.norm_w, 0, G, xg);
+    stage_all(L.x, L.x_dtype, (int)L.w.k, L.norm_w, L.eps, xg);
 
     const int M = (int)L.m, P = a.P;
-    // lane owns output column n = lane & 7 and rows m = (lane >> 3) + 4j
-    constexpr int kSlots = 8;  // M <= 32
+    constexpr int kSlots = 4;  // a lane owns rows m = (lane >> 2) + 8j, j < 4 (M <= 32)
     unsigned long long best[kSlots];
 #pragma unroll
     for (int j = 0; j < kSlots; ++j) best[j] = 0ull;
 
-    bool ok = true;
-    for (int64_t i = 0;; ++i) {
-        const int64_t tile = gw + i * TW;
-        if (tile >= a.ntiles) break;
-        const int s = (int)(i % D);
-        const uint32_t parity = (uint32_t)((i / D) & 1);
-        uint8_t* st = ring + (size_t)s * a.tbytes;
-        // warp-uniform: on a (recorded) timeout the warp stops streaming
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], parity) ? 1 : 0)) { ok = false; break; }
-        load_partial_scales(L.w, tile * 8, st, a.RS);
-        __syncwarp();
-        {
-            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + 8 * a.RS);
-            build_sb_table(sp, sp + 8 * G, G, 0, G, table);
-        }
-        __syncwarp();
-        float acc[1][MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[0][mt][j] = 0.f;
-        const uint8_t* wt[1] = {st};
-        const float2* sbt[1] = {table};
-        mma_groups<1, MT, HALF>(wt, a.RS, sbt, xg.xp, a.XRS, xg.xs, G, a.M_eff, 0, G, 0, acc);
-        __syncwarp();
+    if (producer) {
         if (lane == 0) {
-            const int64_t nt = tile + (int64_t)D * TW;
-            if (nt < a.ntiles) {
-                mbar_arrive_expect_tx(&bars[s], tile_bytes_expected(L.w, nt * 8));
-                issue_tile(L.w, nt * 8, st, a.RS, &bars[s]);
+            for (int64_t i = S;; ++i) {
+                const int64_t blk = blockIdx.x + i * gridDim.x;
+                if (blk >= a.nblocks) break;
+                const int s = (int)(i % S);
+                if (!mbar_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1))) break;
+                lm_issue(a, blk, ring + (size_t)s * a.sbytes, &full[s]);
             }
         }
-        {
-            const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                for (int h = 0; h < (HALF ? 1 : 2); ++h) {
-                    const int r = mt * 16 + h * 8 + g;
-                    if (r < a.M_eff)
-                        *reinterpret_cast<float2*>(wout + r * 8 + 2 * t) =
-                            make_float2(acc[0][mt][2 * h], acc[0][mt][2 * h + 1]);
+    } else {
+        const int wk = warp;
+        const int g0 = wk * G / kLmConsumers, g1 = (wk + 1) * G / kLmConsumers, ng = g1 - g0;
+        float2* table = reinterpret_cast<float2*>(smem + a.off_sb) + (size_t)wk * kLmMaxGroupsPerWarp * kLmRows;
+        for (int64_t i = 0;; ++i) {
+            const int64_t blk = blockIdx.x + i * gridDim.x;
+            if (blk >= a.nblocks) break;
+            const int s = (int)(i % S);
+            const uint8_t* st = ring + (size_t)s * a.sbytes;
+            // uniform over the consumers: on a (recorded) timeout all of them stop together
+            if (!consumers_and(mbar_wait(&full[s], (uint32_t)((i / S) & 1)))) break;
+            const int64_t row0 = blk * kLmRows;
+            const bool fullblk = rows_in(L.w, row0, kLmRows) == kLmRows;
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + a.packed);
+            // table[gl][column c]: the (16 s, b - 16 s) of physical row (c & ~7) + perm(c & 7)
+            for (int e = lane; e < kLmMaxGroupsPerWarp * kLmRows; e += 32) {
+                const int c = (e >> 2) & (kLmRows - 1), gl = (e & 3) + (e >> 7) * 4;
+                if (gl >= ng) continue;
+                const int gg = g0 + gl;
+                const int pr = (c & ~7) + col_to_row(c & 7);
+                float s_ = 0.f, b_ = 0.f;
+                if (fullblk) {
+                    s_ = bf16_bits_to_f32(sp[pr * G + gg]);
+                    b_ = bf16_bits_to_f32(sp[kLmRows * G + pr * G + gg]);
+                } else if (row0 + pr < L.w.n) {
+                    s_ = bf16_bits_to_f32(L.w.s[(row0 + pr) * G + gg]);
+                    b_ = bf16_bits_to_f32(L.w.b[(row0 + pr) * G + gg]);
                 }
-        }
-        __syncwarp();
-        {
-            const int n = lane & 7;
-            const int64_t row = tile * 8 + n;
+                table[gl * kLmRows + c] = sb_entry(s_, b_);
+            }
+            __syncwarp();
+            float acc[kLmTiles][MT][4];
+#pragma unroll
+            for (int t = 0; t < kLmTiles; ++t)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[t][mt][j] = 0.f;
+#pragma unroll 1
+            for (int gl = 0; gl < ng; ++gl) {
+                const int gg = g0 + gl;
+                uint32_t A[MT][2][8];
+                float X[MT][2];
+                load_a<MT, HALF>(xg.xp, a.XRS, xg.xs, G, a.M_eff, gg, A, X);
+#pragma unroll
+                for (int t = 0; t < kLmTiles; ++t) {
+                    const uint2 wv = lds64(frag_addr<true>(st, kLmRows, 0, t * 8, g, t4, gg));
+                    const float4 sb = *reinterpret_cast<const float4*>(table + gl * kLmRows + t * 8 + 2 * t4);
+                    group_mma<MT, HALF>(A, X, wv, sb, acc[t]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads stage s
+            float* rb = red + (size_t)(i & 1) * kLmConsumers * a.M_eff * kLmRows;
+#pragma unroll
+            for (int t = 0; t < kLmTiles; ++t)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int h = 0; h < (HALF ? 1 : 2); ++h) {
+                        const int r = mt * 16 + h * 8 + g;
+                        if (r < a.M_eff)
+                            *reinterpret_cast<float2*>(rb + ((size_t)wk * a.M_eff + r) * kLmRows + t * 8 + 2 * t4) =
+                                make_float2(acc[t][mt][2 * h], acc[t][mt][2 * h + 1]);
+                    }
+            consumers_and(true);  // the block's partials are visible to all consumers
+            // warp wk finishes columns [4wk, 4wk+4): lane -> column 4wk + (lane & 3), m = (lane >> 2) + 8j
+            const int c = 4 * wk + (lane & 3);
+            const int64_t row = row0 + (c & ~7) + col_to_row(c & 7);
             if (row < L.w.n) {
 #pragma unroll
                 for (int j = 0; j < kSlots; ++j) {
-                    const int m = (lane >> 3) + 4 * j;
+                    const int m = (lane >> 2) + 8 * j;
                     if (m < M) {
                         float v = 0.f;
-                        for (int p = 0; p < P; ++p) v += wout[(p * M + m) * 8 + n];
+                        for (int w = 0; w < kLmConsumers; ++w)
+                            for (int p = 0; p < P; ++p) v += rb[((size_t)w * a.M_eff + p * M + m) * kLmRows + c];
                         if (L.x_dtype == kBF16 && !L.norm_w) v = bf16_round(v);
                         const unsigned long long k = pack_key(v, L.vocab_offset + row);
                         best[j] = k > best[j] ? k : best[j];
@@ -536,30 +767,28 @@ __global__ void __launch_bounds__(kMaxThreads) q4_lm_head_kernel(const __grid_co
                 }
             }
         }
-        __syncwarp();
-    }
-    (void)ok;
-    // reduce over the 8 lanes sharing m, then over warps, then across CTAs
-#pragma unroll
-    for (int j = 0; j < kSlots; ++j) {
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-            unsigned long long other = __shfl_xor_sync(0xffffffffu, best[j], o);
-            best[j] = other > best[j] ? other : best[j];
-        }
-    }
-    if ((lane & 7) == 0) {
+        // reduce over the 4 lanes sharing m, then over warps
 #pragma unroll
         for (int j = 0; j < kSlots; ++j) {
-            const int m = (lane >> 3) + 4 * j;
-            if (m < M) ckeys[warp * M + m] = best[j];
+#pragma unroll
+            for (int o = 1; o < 4; o <<= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, best[j], o);
+                best[j] = other > best[j] ? other : best[j];
+            }
+        }
+        if ((lane & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) {
+                const int m = (lane >> 2) + 8 * j;
+                if (m < M) ckeys[wk * M + m] = best[j];
+            }
         }
     }
     __syncthreads();
     __shared__ bool is_last;
     if (tid < M) {
         unsigned long long k = 0ull;
-        for (int w = 0; w < a.nwarps; ++w) k = ckeys[w * M + tid] > k ? ckeys[w * M + tid] : k;
+        for (int w = 0; w < kLmConsumers; ++w) k = ckeys[w * M + tid] > k ? ckeys[w * M + tid] : k;
         if (k) atomicMax(&L.keys[tid], k);
     }
     __threadfence();
@@ -609,7 +838,40 @@ int num_sms() {
     return n;
 }
 
-constexpr uint32_t kSmemLimit = 226 * 1024;  // dynamic; leaves room for static shared memory
+constexpr uint32_t kSmemLimit = 225 * 1024;     // dynamic, incl. 1 KB alignment slack; leaves room for static
+constexpr uint32_t kSmemTwoPerSm = 111 * 1024;  // two CTAs per SM (228 KB per SM, 1 KB reserved each)
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Packed words of W as a 2-D tensor [n rows][k/8 words], box [32 words][box_rows rows], 128-byte
+// swizzle, zero fill out of range.
+bool encode_packed_map(CUtensorMap* m, const Q4Mat& W, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(W.k / 8), (cuuint64_t)W.n};
+    const cuuint64_t strides[1] = {(cuuint64_t)(W.k / 2)};
+    const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(W.w), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <typename KernelT, typename ArgT>
 cudaError_t launch_kernel(KernelT kernel, const ArgT& args, int grid, int threads, uint32_t smem, bool pdl,
@@ -629,16 +891,60 @@ cudaError_t launch_kernel(KernelT kernel, const ArgT& args, int grid, int thread
     return cudaLaunchKernelEx(&cfg, kernel, args);
 }
 
-template <int NB, int EPI>
+template <int NT, int EPI, bool SWZ>
 cudaError_t dispatch_unit(const UnitArgs& a, int grid, int threads, uint32_t smem, bool pdl, cudaStream_t st) {
-    if (a.M_eff <= 8) return launch_kernel(q4_unit_kernel<NB, 1, true, EPI>, a, grid, threads, smem, pdl, st);
-    if (a.M_eff <= 16) return launch_kernel(q4_unit_kernel<NB, 1, false, EPI>, a, grid, threads, smem, pdl, st);
-    return launch_kernel(q4_unit_kernel<NB, 2, false, EPI>, a, grid, threads, smem, pdl, st);
+    if (a.M_eff <= 8) return launch_kernel(q4_unit_kernel<NT, 1, true, EPI, SWZ>, a, grid, threads, smem, pdl, st);
+    if (a.M_eff <= 16) return launch_kernel(q4_unit_kernel<NT, 1, false, EPI, SWZ>, a, grid, threads, smem, pdl, st);
+    return launch_kernel(q4_unit_kernel<NT, 2, false, EPI, SWZ>, a, grid, threads, smem, pdl, st);
+}
+
+// Shared-memory plan of the unit kernel; 0 if it does not fit.
+uint32_t plan_unit(UnitArgs& a, int NT, int nmat, bool swz, int64_t M, bool norm, int K) {
+    const int HT = NT / nmat;
+    if (swz) {
+        a.BR = HT * 8;
+        a.nchunk = (K / 8 + 31) / 32;
+        a.tbytes = align_up((uint32_t)a.nchunk * a.BR * 128 + 2u * a.BR * a.G * 2u, 1024);
+    } else {
+        a.BR = 8;
+        a.nchunk = 0;
+        a.tbytes = tile_bytes(K);
+    }
+    uint32_t off = 0;
+    a.off_tiles = off;
+    off += (swz ? nmat : NT) * a.tbytes;
+    a.off_bar = off;
+    off += 128;
+    a.off_scr = off;
+    off += align_up((64 + (norm ? (uint32_t)M * (K / 8) : 0u)) * 4, 128);
+    a.off_sb = off;
+    off += align_up((uint32_t)NT * a.G * 8 * 8, 128);
+    a.off_red = off;
+    off += align_up((uint32_t)a.NWK * NT * a.M_eff * 8 * 4, 128);
+    const uint32_t fixed = off + 1024;  // + alignment slack of the dynamic window
+    // whole-K activations when they fit under the two-CTAs-per-SM budget, else K chunks
+    const uint32_t whole = align_up((uint32_t)a.M_eff * (a.G * 128 + 16), 128) + align_up((uint32_t)a.M_eff * a.G * 4, 128);
+    int GC = a.G;
+    if (fixed + whole > kSmemTwoPerSm) {
+        const uint32_t budget = std::max<uint32_t>(kSmemTwoPerSm, fixed + 16384);
+        const uint32_t per_group = (uint32_t)a.M_eff * (128 + 4);
+        GC = (int)((budget - fixed - (uint32_t)a.M_eff * 16 - 256) / per_group);
+        GC = std::max(1, std::min(GC, a.G));
+    }
+    a.GC = GC;
+    a.XRS = GC * 128 + 16;
+    a.off_xp = off;
+    off += align_up((uint32_t)a.M_eff * a.XRS, 128);
+    a.off_xs = off;
+    off += align_up((uint32_t)a.M_eff * GC * 4, 128);
+    off += 1024;  // alignment slack
+    return off <= kSmemLimit ? off : 0;
 }
 
 }  // namespace
 
 int gemv_max_rows(int act_dtype) { return act_dtype == kBF16 ? 32 : 10; }
+int lm_head_max_rows(int act_dtype, bool normed) { return (normed || act_dtype == kF32) ? 5 : 16; }
 
 cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
     UnitArgs a{};
@@ -647,57 +953,53 @@ cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
     a.G = K / kGroup;
     a.P = (L.norm_w || L.x_dtype == kF32) ? 3 : 1;
     a.M_eff = (int)L.m * a.P;
-    const int epi = L.epi;
-    int NB, NWR;
-    if (epi == kEpiSwiglu) {
-        NB = 2;
-        NWR = 2;
-    } else {
-        NB = (L.w0.n >= 2LL * 16 * num_sms()) ? 2 : 1;
-        NWR = 1;
-    }
-    int NWK = std::max(1, std::min(epi == kEpiSwiglu ? 4 : 8, a.G / 8));
-    a.NWR = NWR;
-    a.NWK = NWK;
     a.RS = packed_row_stride(K);
-    a.tbytes = tile_bytes(K);
-    const uint32_t ntiles = NWR * NB;
-    // shared-memory budget: weights + scale tables + reduction fixed, activation chunk takes the rest
-    uint32_t off = 0;
-    a.off_bar = off;
-    off += 128;
-    a.off_scr = off;
-    off += align_up((64 + (uint32_t)L.m) * 4, 128);
-    a.off_tiles = off;
-    off += ntiles * a.tbytes;
-    a.off_sb = off;
-    off += align_up(ntiles * a.G * 8 * 8, 128);
-    a.off_red = off;
-    off += align_up((uint32_t)NWK * ntiles * a.M_eff * 8 * 4, 128);
-    const uint32_t fixed = off;
-    const uint32_t budget = std::min<uint32_t>(kSmemLimit, std::max<uint32_t>(fixed + 16384, 110 * 1024));
-    const uint32_t per_group = (uint32_t)a.M_eff * (128 + 4);
-    int GC = (int)((budget - fixed - (uint32_t)a.M_eff * 16 - 256) / per_group);
-    GC = std::max(1, std::min(GC, a.G));
-    a.GC = GC;
-    a.XRS = GC * 128 + 16;
-    a.off_xp = off;
-    off += align_up((uint32_t)a.M_eff * a.XRS, 128);
-    a.off_xs = off;
-    off += align_up((uint32_t)a.M_eff * GC * 4, 128);
-    const uint32_t smem = off;
-    if (smem > kSmemLimit) return cudaErrorInvalidConfiguration;
-    const int64_t unit_rows = (int64_t)NWR * 8 * (epi == kEpiSwiglu ? 1 : NB);
-    const int grid = (int)((L.w0.n + unit_rows - 1) / unit_rows);
-    if (grid <= 0) return cudaSuccess;
-    const int threads = 32 * NWR * NWK;
-    if (epi == kEpiSwiglu) return dispatch_unit<2, kEpiSwiglu>(a, grid, threads, smem, L.pdl, stream);
-    if (epi == kEpiResid) {
-        return NB == 2 ? dispatch_unit<2, kEpiResid>(a, grid, threads, smem, L.pdl, stream)
-                       : dispatch_unit<1, kEpiResid>(a, grid, threads, smem, L.pdl, stream);
+    a.NWK = std::max(1, std::min(8, a.G / 4));
+    const int epi = L.epi;
+    const int nmat = epi == kEpiSwiglu ? 2 : 1;
+    const int64_t want = (int64_t)num_sms() * 5 / 4;  // CTAs wanted: about one wave
+    // tiles per CTA: as many as keep >= ~1.25 CTAs per SM
+    int NT = nmat;
+    for (int c : {8, 4, 2}) {
+        if (c < nmat || (epi != kEpiSwiglu && c > 4)) continue;
+        const int64_t ctas = (L.w0.n + (c / nmat) * 8 - 1) / ((c / nmat) * 8);
+        if (ctas >= want && (a.M_eff <= 8 || c <= 4)) {
+            NT = c;
+            break;
+        }
     }
-    return NB == 2 ? dispatch_unit<2, kEpiStore>(a, grid, threads, smem, L.pdl, stream)
-                   : dispatch_unit<1, kEpiStore>(a, grid, threads, smem, L.pdl, stream);
+    uint32_t smem = 0;
+    bool swz = false;
+    for (; NT >= nmat; NT /= 2) {
+        swz = (NT / nmat) * 8 >= 32 && encode_fn() != nullptr;
+        smem = plan_unit(a, NT, nmat, swz, L.m, L.norm_w != nullptr, K);
+        if (smem) break;
+    }
+    if (!smem) return cudaErrorInvalidConfiguration;
+    if (swz) {
+        if (!encode_packed_map(&a.tm0, L.w0, a.BR)) return cudaErrorInvalidValue;
+        if (nmat == 2 && !encode_packed_map(&a.tm1, L.w1, a.BR)) return cudaErrorInvalidValue;
+    }
+    const int64_t rows_per_cta = (NT / nmat) * 8;
+    const int grid = (int)((L.w0.n + rows_per_cta - 1) / rows_per_cta);
+    if (grid <= 0) return cudaSuccess;
+    const int threads = 32 * a.NWK;
+    if (epi == kEpiSwiglu) {
+        if (NT == 8) return dispatch_unit<8, kEpiSwiglu, true>(a, grid, threads, smem, L.pdl, stream);
+        if (NT == 4) return swz ? dispatch_unit<4, kEpiSwiglu, true>(a, grid, threads, smem, L.pdl, stream)
+                                : dispatch_unit<4, kEpiSwiglu, false>(a, grid, threads, smem, L.pdl, stream);
+        return dispatch_unit<2, kEpiSwiglu, false>(a, grid, threads, smem, L.pdl, stream);
+    }
+    if (epi == kEpiResid) {
+        if (NT == 4) return swz ? dispatch_unit<4, kEpiResid, true>(a, grid, threads, smem, L.pdl, stream)
+                                : dispatch_unit<4, kEpiResid, false>(a, grid, threads, smem, L.pdl, stream);
+        if (NT == 2) return dispatch_unit<2, kEpiResid, false>(a, grid, threads, smem, L.pdl, stream);
+        return dispatch_unit<1, kEpiResid, false>(a, grid, threads, smem, L.pdl, stream);
+    }
+    if (NT == 4) return swz ? dispatch_unit<4, kEpiStore, true>(a, grid, threads, smem, L.pdl, stream)
+                            : dispatch_unit<4, kEpiStore, false>(a, grid, threads, smem, L.pdl, stream);
+    if (NT == 2) return dispatch_unit<2, kEpiStore, false>(a, grid, threads, smem, L.pdl, stream);
+    return dispatch_unit<1, kEpiStore, false>(a, grid, threads, smem, L.pdl, stream);
 }
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream) {
@@ -705,43 +1007,41 @@ cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream)
     a.L = L;
     const int K = (int)L.w.k;
     a.G = K / kGroup;
+    if (a.G > kLmMaxGroupsPerWarp * kLmConsumers) return cudaErrorInvalidValue;
     a.P = (L.norm_w || L.x_dtype == kF32) ? 3 : 1;
     a.M_eff = (int)L.m * a.P;
-    a.RS = packed_row_stride(K);
-    a.tbytes = tile_bytes(K);
+    if (a.M_eff > 32 || L.m > 32) return cudaErrorInvalidValue;
+    if (!encode_packed_map(&a.tm, L.w, kLmRows)) return cudaErrorInvalidValue;
+    a.nchunk = (K / 8 + 31) / 32;
     a.XRS = a.G * 128 + 16;
-    a.ntiles = (L.w.n + 7) / 8;
-    const int nwarps = 8;
-    a.nwarps = nwarps;
+    a.nblocks = (L.w.n + kLmRows - 1) / kLmRows;
+    a.packed = (uint32_t)a.nchunk * kLmRows * 128;
+    a.sbytes = align_up(a.packed + 2u * kLmRows * a.G * 2u, 1024);
     uint32_t off = 0;
     a.off_bar = off;
-    off += align_up(nwarps * 4 * 8, 128);
+    off += 256;
     a.off_scr = off;
-    off += align_up((64 + (uint32_t)L.m) * 4, 128);
+    off += align_up((64 + (L.norm_w ? (uint32_t)L.m * (K / 8) : 0u)) * 4, 128);
     a.off_keys = off;
-    off += align_up(nwarps * (uint32_t)L.m * 8, 128);
-    a.off_out = off;
-    off += align_up(nwarps * (uint32_t)a.M_eff * 8 * 4, 128);
+    off += align_up(kLmConsumers * (uint32_t)L.m * 8, 128);
+    a.off_red = off;
+    off += align_up(2u * kLmConsumers * a.M_eff * kLmRows * 4, 128);
     a.off_sb = off;
-    off += align_up(nwarps * (uint32_t)a.G * 8 * 8, 128);
+    off += align_up((uint32_t)kLmConsumers * kLmMaxGroupsPerWarp * kLmRows * 8, 128);
     a.off_xp = off;
     off += align_up((uint32_t)a.M_eff * a.XRS, 128);
     a.off_xs = off;
     off += align_up((uint32_t)a.M_eff * a.G * 4, 128);
+    off = align_up(off, 1024);  // 128-byte-swizzled TMA boxes need 1024-byte-aligned destinations
     a.off_ring = off;
-    const uint32_t avail = kSmemLimit > off ? kSmemLimit - off : 0;
-    int D = (int)(avail / (nwarps * a.tbytes));
-    D = std::min(D, 4);
-    if (D < 1) return cudaErrorInvalidConfiguration;
-    a.D = D;
-    off += (uint32_t)nwarps * D * a.tbytes;
-    const uint32_t smem = off;
-    const int64_t want = (a.ntiles + nwarps - 1) / nwarps;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), want));
-    const int threads = 32 * nwarps;
-    if (a.M_eff <= 8) return launch_kernel(q4_lm_head_kernel<1, true>, a, grid, threads, smem, L.pdl, stream);
-    if (a.M_eff <= 16) return launch_kernel(q4_lm_head_kernel<1, false>, a, grid, threads, smem, L.pdl, stream);
-    return launch_kernel(q4_lm_head_kernel<2, false>, a, grid, threads, smem, L.pdl, stream);
+    const uint32_t avail = kSmemLimit > off + 1024 ? kSmemLimit - off - 1024 : 0;
+    a.S = std::min<int>(12, (int)(avail / a.sbytes));  // 2*S mbarriers fit the 256-byte slot
+    if (a.S < 2) return cudaErrorInvalidConfiguration;
+    const uint32_t smem = off + (uint32_t)a.S * a.sbytes + 1024;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), a.nblocks));
+    if (a.M_eff <= 8) return launch_kernel(q4_lm_head_kernel<1, true>, a, grid, kLmThreads, smem, L.pdl, stream);
+    if (a.M_eff <= 16) return launch_kernel(q4_lm_head_kernel<1, false>, a, grid, kLmThreads, smem, L.pdl, stream);
+    return launch_kernel(q4_lm_head_kernel<2, false>, a, grid, kLmThreads, smem, L.pdl, stream);
 }
 
 int gemv_device_error(bool clear) {

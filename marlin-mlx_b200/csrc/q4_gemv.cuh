@@ -41,9 +41,10 @@ struct GemvLaunch {
     bool pdl;  // launch with programmatic stream serialization
 };
 
-// Number of activation rows the tensor-core GEMV handles in one pass: m * planes <= 32, with
-// planes = 1 for bf16 activations and 3 for binary32 (exact bf16 hi/mid/lo split).
+// Activation rows per pass: the GEMV handles m * planes <= 32 (planes = 1 for bf16, 3 for binary32
+// or RMSNorm'ed input: exact bf16 hi/mid/lo split); the lm_head kernel m * planes <= 16.
 int gemv_max_rows(int act_dtype);
+int lm_head_max_rows(int act_dtype, bool normed);
 
 // Launches the decode GEMV family (one CTA per row block, weights fetched before the PDL wait).
 // Returns cudaSuccess or the launch error.  Arguments are validated by the caller.

@@ -1,0 +1,66 @@
+"""Standalone driver of the decode kernels, for profilers (ncu) and quick timing.
+
+    python -m marlin_q4.prof [--m 1] [--reps 3] [--time]
+
+Builds one decode layer (gate/up/down Q4 [6144,2048]/[2048,6144]) and the Q4 lm_head
+[248320, 2048] from the seeded generator, then launches, in this order, `reps` times each:
+gate_up_swiglu (RMSNorm fused), matmul_residual (down + residual), lm_head_argmax (final norm
+fused), and qmatmul (config 1: bf16 x [1, 2048] . W[6144, 2048]^T).  About 1.6 GB on the device.
+With --time, prints each family's CUDA-event time per launch (back-to-back launches, no graph).
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+import marlin_q4 as mq
+
+H, I, V = 2048, 6144, 248320
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--time", action="store_true")
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    g = mq.quantize_weight(mq.synth_bf16((I, H), 1000, 0.0, 0.02))
+    u = mq.quantize_weight(mq.synth_bf16((I, H), 1001, 0.0, 0.02))
+    d = mq.quantize_weight(mq.synth_bf16((H, I), 1002, 0.0, 0.02))
+    nw = mq.synth_bf16((H,), 1003, 0.1, 0.02)
+    lm = mq.quantize_weight(mq.synth_bf16((V, H), 2000, 0.0, 0.02))
+    torch.cuda.empty_cache()
+    fn = mq.synth_bf16((H,), 2001, 0.1, 0.02)
+    h = mq.synth_bf16((a.m, H), 3000, 0.0, 1.0).float()
+    act = torch.empty((a.m, I), dtype=torch.float32, device="cuda")
+    res = torch.empty((a.m, H), dtype=torch.float32, device="cuda")
+    xb = mq.synth_bf16((1, H), 7, 0.0, 1.0)
+    ws = mq.LmHeadWorkspace(a.m, "cuda")
+    fams = {
+        "gate_up_swiglu": lambda: mq.gate_up_swiglu(h, g, u, norm_weight=nw, out=act),
+        "down_residual": lambda: mq.matmul_residual(act, d, h, out=res),
+        "lm_head_argmax": lambda: mq.lm_head_argmax(h, lm, norm_weight=fn, workspace=ws),
+        "qmatmul_c1": lambda: mq.qmatmul(xb, g),
+    }
+    for name, f in fams.items():
+        if a.time:
+            f()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.reps):
+                f()
+            e1.record()
+            e1.synchronize()
+            print(f"{name}: {e0.elapsed_time(e1) / a.reps * 1e3:.2f} us/launch")
+        else:
+            for _ in range(a.reps):
+                f()
+    torch.cuda.synchronize()
+    assert mq.device_error() == 0
+
+
+if __name__ == "__main__":
+    main()

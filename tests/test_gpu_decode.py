@@ -27,7 +27,7 @@ def model():
     return layers, host_layers, lm, host_q4(lm), fn, u16(fn)
 
 
-@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("m", [1, 3, 12])
 def test_decode_step_matches_oracle(oracle, model, m):
     layers, hl, lm, hlm, fn, hfn = model
     step = mq.DecodeStep(layers, fn, lm, m)

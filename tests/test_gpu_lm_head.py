@@ -22,7 +22,7 @@ def lm():
     return q, host_q4(q), norm, u16(norm)
 
 
-@pytest.mark.parametrize("m", [1, 2, 5, 8])
+@pytest.mark.parametrize("m", [1, 2, 5, 8, 10, 13])
 def test_lm_head_argmax_after_final_norm(oracle, lm, m):
     """Config 3: hidden bf16 ~N(0,1) -> RMSNorm(1+w) (binary32, as the reference's C++ evaluates it)
     -> Q4 lm_head -> argmax."""
@@ -36,11 +36,12 @@ def test_lm_head_argmax_after_final_norm(oracle, lm, m):
     assert mq.device_error() == 0
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_lm_head_argmax_plain(oracle, lm, dtype):
+@pytest.mark.parametrize("dtype,m", [(torch.bfloat16, 4), (torch.float32, 4), (torch.bfloat16, 32),
+                                     (torch.float32, 10), (torch.bfloat16, 33)])
+def test_lm_head_argmax_plain(oracle, lm, dtype, m):
     """No norm: bf16 hidden compares bf16-rounded logits (ties -> first index); f32 compares f32."""
     q, hq = lm[0], lm[1]
-    h = act((4, H), 30, dtype)
+    h = act((m, H), 30 + m, dtype)
     ids, best = mq.lm_head_argmax(h, q)
     rids, rbest = oracle.lm_head_argmax(host_act(h), hq)
     assert np.array_equal(ids.cpu().numpy(), rids)
