@@ -72,6 +72,9 @@ int marlin_q4_device_error(int clear);
 /* Programmatic dependent launch (kernels prefetch weights while their predecessor finishes).
  * Enabled by default; enable = 0 launches every kernel with plain stream ordering. */
 void marlin_q4_set_pdl(int enable);
+/* Decode kernels on the 5th-generation tensor cores (tcgen05 + TMEM; k % 512 == 0, m * planes <= 32)
+ * where they apply (default), or on the warp-level mma.sync kernels everywhere (enable = 0). */
+void marlin_q4_set_tcgen05(int enable);
 
 /* ---- quantize --------------------------------------------------------------------------------
  * Replaces mx::quantize(w, group_size, bits) at src/model/weights.cpp:46 (quantize_weight,

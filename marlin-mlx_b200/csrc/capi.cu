@@ -121,6 +121,8 @@ int marlin_q4_device_error(int clear) {
 
 void marlin_q4_set_pdl(int enable) { g_pdl = enable != 0; }
 
+void marlin_q4_set_tcgen05(int enable) { set_tcgen05(enable != 0); }
+
 int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_size, int32_t bits, uint32_t* wq,
                        uint16_t* scales, uint16_t* biases, void* stream) {
     if (!w || !wq || !scales || !biases || n <= 0 || k <= 0) return MARLIN_Q4_ERR_ARG;
@@ -224,7 +226,7 @@ int marlin_q4_lm_head_argmax(const void* hidden, int32_t dtype, int64_t m, const
         return MARLIN_Q4_ERR_ALIGN;
     unsigned long long* keys = static_cast<unsigned long long*>(workspace);
     unsigned int* counter = reinterpret_cast<unsigned int*>(keys + m);
-    const int64_t rp = lm_head_max_rows(dtype, norm_weight != nullptr);
+    const int64_t rp = lm_head_max_rows(dtype, norm_weight != nullptr, lm->k);
     for (int64_t r0 = 0; r0 < m; r0 += rp) {
         LmHeadLaunch L{};
         L.x = static_cast<const uint8_t*>(hidden) + r0 * lm->k * dtype_size(dtype);

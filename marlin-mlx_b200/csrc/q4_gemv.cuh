@@ -44,7 +44,9 @@ struct GemvLaunch {
 // Activation rows per pass: the GEMV handles m * planes <= 32 (planes = 1 for bf16, 3 for binary32
 // or RMSNorm'ed input: exact bf16 hi/mid/lo split); the lm_head kernel m * planes <= 16.
 int gemv_max_rows(int act_dtype);
-int lm_head_max_rows(int act_dtype, bool normed);
+int lm_head_max_rows(int act_dtype, bool normed, int64_t k);
+// Use the tcgen05 (TMEM) kernels where they apply (default) or the mma.sync kernels only.
+void set_tcgen05(bool enable);
 
 // Launches the decode GEMV family (one CTA per row block, weights fetched before the PDL wait).
 // Returns cudaSuccess or the launch error.  Arguments are validated by the caller.

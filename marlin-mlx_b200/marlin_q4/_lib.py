@@ -39,6 +39,7 @@ SIGNATURES = {
     "marlin_q4_last_cuda_error": (ctypes.c_int, []),
     "marlin_q4_device_error": (ctypes.c_int, [ctypes.c_int]),
     "marlin_q4_set_pdl": (None, [ctypes.c_int]),
+    "marlin_q4_set_tcgen05": (None, [ctypes.c_int]),
     "marlin_q4_quantize": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     "marlin_q4_matmul": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),
     "marlin_q4_rms_norm": (ctypes.c_int, [_vp, _i32, _vp, _i64, _i64, _f32, _vp, _vp]),

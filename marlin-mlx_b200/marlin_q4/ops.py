@@ -252,3 +252,8 @@ def device_error(clear: bool = True) -> int:
 
 def set_pdl(enable: bool) -> None:
     _lib.load().marlin_q4_set_pdl(1 if enable else 0)
+
+
+def set_tcgen05(enable: bool) -> None:
+    """Select the tcgen05/TMEM decode kernels (default) or the mma.sync kernels for every shape."""
+    _lib.load().marlin_q4_set_tcgen05(1 if enable else 0)
