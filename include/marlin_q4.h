@@ -135,6 +135,23 @@ int marlin_q4_lm_head_argmax(const void* hidden, int32_t dtype, int64_t m, const
                              float* best, uint64_t* keys_out, void* workspace, size_t workspace_bytes,
                              void* stream);
 size_t marlin_q4_lm_head_workspace_size(int64_t m);
+
+/* marlin_q4_lm_head_argmax without a workspace argument.  No counterpart in the reference: it
+ * exists for callers that cannot allocate or own device scratch for this call, such as a binding
+ * that replaces MarlinModel::lm_head + sample_token (src/model/marlin.cpp:161-169,
+ * src/sampling/sampler.cpp:14-16), whose call shape carries no buffer, or a runtime that must not
+ * call cudaMalloc (a device-wide synchronisation) inside its decode loop.  Same arguments and
+ * results as marlin_q4_lm_head_argmax otherwise.
+ * The keys live in one library-owned device array per device (zeroed at module load, left zeroed
+ * by every call); nothing is allocated.  m > MARLIN_Q4_LM_HEAD_STATIC_MAX_ROWS returns
+ * MARLIN_Q4_ERR_UNSUPPORTED.  All calls on one device share that array: calls that can overlap in
+ * time (different streams, unordered host threads) race and return wrong ids, so keep them on one
+ * stream.  The first call on each device looks the array up (cudaGetSymbolAddress) and must be made
+ * outside stream capture. */
+#define MARLIN_Q4_LM_HEAD_STATIC_MAX_ROWS 64
+int marlin_q4_lm_head_argmax_static(const void* hidden, int32_t dtype, int64_t m, const uint16_t* norm_weight,
+                                    float eps, const marlin_q4_tensor* lm, int64_t vocab_offset, int32_t* ids,
+                                    float* best, uint64_t* keys_out, void* stream);
 /* ids/best from packed keys (after a cross-shard max-merge of keys_out). */
 int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* best, void* stream);
 

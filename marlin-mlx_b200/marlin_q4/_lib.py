@@ -51,6 +51,8 @@ SIGNATURES = {
     "marlin_q4_lm_head_argmax": (ctypes.c_int, [_vp, _i32, _i64, _vp, _f32, _PT, _i64, _vp, _vp, _vp,
                                                 _vp, _sz, _vp]),
     "marlin_q4_lm_head_workspace_size": (_sz, [_i64]),
+    "marlin_q4_lm_head_argmax_static": (ctypes.c_int, [_vp, _i32, _i64, _vp, _f32, _PT, _i64, _vp, _vp, _vp,
+                                                       _vp]),
     "marlin_q4_decode_keys": (ctypes.c_int, [_vp, _i64, _vp, _vp, _vp]),
     "marlin_q4_decode_step": (ctypes.c_int, [_vp, _i64, _i64, _i32, _PL, _vp, _f32, _PT, _vp, _vp, _vp,
                                              _vp, _sz, _vp]),
