@@ -72,9 +72,20 @@ int marlin_q4_device_error(int clear);
 /* Programmatic dependent launch (kernels prefetch weights while their predecessor finishes).
  * Enabled by default; enable = 0 launches every kernel with plain stream ordering. */
 void marlin_q4_set_pdl(int enable);
-/* Decode kernels on the 5th-generation tensor cores (tcgen05 + TMEM; k % 512 == 0, m * planes <= 32)
- * where they apply (default), or on the warp-level mma.sync kernels everywhere (enable = 0). */
-void marlin_q4_set_tcgen05(int enable);
+/* Decode kernel family (process-wide; every family computes the same function, within the float
+ * tolerance, and each is tested against the CPU checker):
+ *   MARLIN_Q4_PATH_I8MMA   (default) integer tensor-core MMAs on the raw codes and 4 s8 activation
+ *                          planes, exact int32 accumulation (k % 256 == 0, k >= 512, m <= 16
+ *                          per launch);
+ *   MARLIN_Q4_PATH_TCGEN05 5th-generation tensor cores: bf16 codes in TMEM, tcgen05.mma
+ *                          (k % 512 == 0, m * planes <= 32);
+ *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0).
+ * Shapes a family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns MARLIN_Q4_ERR_ARG
+ * for an unknown path. */
+#define MARLIN_Q4_PATH_I8MMA 0
+#define MARLIN_Q4_PATH_TCGEN05 1
+#define MARLIN_Q4_PATH_BF16MMA 2
+int marlin_q4_set_decode_path(int path);
 
 /* ---- quantize --------------------------------------------------------------------------------
  * Replaces mx::quantize(w, group_size, bits) at src/model/weights.cpp:46 (quantize_weight,

@@ -6,6 +6,8 @@
 #include "marlin_q4.h"
 
 #include "q4_gemv.cuh"
+#include "q4_i8.cuh"
+#include "q4_tc.cuh"
 #include "q4_misc.cuh"
 
 #include <algorithm>
@@ -56,16 +58,11 @@ int check_norm(const uint16_t* w) { return (!w || aligned(w, 16)) ? MARLIN_Q4_OK
 
 Q4Mat view(const marlin_q4_tensor* t) { return Q4Mat{t->weight, t->scales, t->biases, t->n, t->k}; }
 
-// rows per GEMV pass for an activation dtype (m * planes <= 32)
-int64_t rows_per_pass(int32_t act_dtype, bool normed) {
-    return (normed || act_dtype == MARLIN_Q4_F32) ? 10 : 32;
-}
-
 // y[m, n] (y_dtype) for x[m, k]; rows processed in passes of at most rows_per_pass
 int gemv_passes(const void* x, int32_t x_dtype, int64_t m, const uint16_t* norm_w, float eps, const Q4Mat& w0,
                 const Q4Mat& w1, int epi, void* y, int32_t y_dtype, int64_t ldy, const void* resid,
                 int32_t resid_dtype, int64_t ldr, cudaStream_t stream) {
-    const int64_t rp = rows_per_pass(x_dtype, norm_w != nullptr);
+    const int64_t rp = gemv_max_rows(x_dtype, norm_w != nullptr, w0.k);
     for (int64_t r0 = 0; r0 < m; r0 += rp) {
         GemvLaunch L{};
         L.x = static_cast<const uint8_t*>(x) + r0 * w0.k * dtype_size(x_dtype);
@@ -114,14 +111,19 @@ const char* marlin_q4_status_string(int status) {
 int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 
 int marlin_q4_device_error(int clear) {
-    const int v = gemv_device_error(clear != 0);
+    int v = gemv_device_error(clear != 0);
+    const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0);
+    if (!v) v = v_tc;
+    if (!v) v = v_i8;
     if (v < 0) return cuda_status(cudaGetLastError());
     return v;
 }
 
 void marlin_q4_set_pdl(int enable) { g_pdl = enable != 0; }
 
-void marlin_q4_set_tcgen05(int enable) { set_tcgen05(enable != 0); }
+int marlin_q4_set_decode_path(int path) {
+    return set_decode_path(path) ? MARLIN_Q4_OK : MARLIN_Q4_ERR_ARG;
+}
 
 int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_size, int32_t bits, uint32_t* wq,
                        uint16_t* scales, uint16_t* biases, void* stream) {

@@ -260,4 +260,86 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+
+// D (16x8 s32) += A (16x32 s8, row-major) * B (32x8 s8, column-major); exact integer accumulation.
+// Fragments (PTX ISA, mma.m16n8k32 with .s8): lane = 4 * g + t;
+//   a0: row g, k 4t..4t+3;  a1: row g+8, k 4t..4t+3;  a2: row g, k 16+4t..;  a3: row g+8, k 16+4t..
+//   b0: column g, k 4t..4t+3;  b1: column g, k 16+4t..
+//   d0, d1: row g, columns 2t, 2t+1;  d2, d3: row g+8, columns 2t, 2t+1.
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- waits shared by the warp-specialised kernels ------------------------------------------------
+// Bounded wait that also ends early once another role has aborted (timeout recorded on device).
+// Every lane acquires the barrier; the exit is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
+        if ((it & 63u) == 63u) {
+            int stop = 0;
+            if ((threadIdx.x & 31) == 0) {
+                if (*abort) {
+                    stop = 1;
+                } else if (globaltimer_ns() - t0 > 2000000000ull || it > (1u << 28)) {
+                    record_device_error(kDevErrMbarTimeout);
+                    *abort = 1;
+                    stop = 1;
+                }
+            }
+            if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+        }
+    }
+}
+// Single-thread bounded wait (producer / MMA issuer).
+__device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0; it < (1u << 28); ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 63u) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                record_device_error(kDevErrMbarTimeout);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+    *abort = 1;
+    return false;
+}
+
+// Bounded wait used on the exit path only (ignores the abort flag): returns when the phase is
+// complete or after ~2 s.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0; it < (1u << 26); ++it) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+            record_device_error(kDevErrMbarTimeout);
+            return;
+        }
+    }
+}
+
+
+// ---- thread-block clusters --------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(const float* local_ptr, uint32_t rank, float v) {
+    uint32_t raddr;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(local_ptr)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(raddr), "f"(v) : "memory");
+}
+
+
 }  // namespace marlin

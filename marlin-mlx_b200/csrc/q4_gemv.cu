@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "q4_gemv.cuh"
 #include "q4_stage.cuh"
+#include "q4_i8.cuh"
 #include "q4_tc.cuh"
 
 #include <cuda.h>
@@ -762,20 +763,29 @@ uint32_t plan_unit(UnitArgs& a, int NT, int nmat, bool swz, int64_t M, bool norm
 
 }  // namespace
 
-bool g_use_tc = true;
+int g_decode_path = kPathI8;
 
-void set_tcgen05(bool enable) { g_use_tc = enable; }
+bool set_decode_path(int path) {
+    if (path != kPathI8 && path != kPathTc && path != kPathBf16) return false;
+    g_decode_path = path;
+    return true;
+}
 
-int gemv_max_rows(int act_dtype) { return act_dtype == kBF16 ? 32 : 10; }
+int gemv_max_rows(int act_dtype, bool normed, int64_t k) {
+    if (g_decode_path == kPathI8 && i8_supported(k, 1)) return kI8MaxRows;
+    return (normed || act_dtype == kF32) ? 10 : 32;
+}
 int lm_head_max_rows(int act_dtype, bool normed, int64_t k) {
+    if (g_decode_path == kPathI8 && i8_supported(k, 1)) return kI8MaxRows;
     const bool p3 = normed || act_dtype == kF32;
-    if (g_use_tc && tc_supported(k, p3 ? 30 : 32)) return p3 ? 10 : 32;
+    if (g_decode_path == kPathTc && tc_supported(k, p3 ? 30 : 32)) return p3 ? 10 : 32;
     return p3 ? 5 : 16;
 }
 
 cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
     const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
-    if (g_use_tc && tc_supported(L.w0.k, m_eff) && tc_gemv_fits(L)) return launch_tc_gemv(L, stream);
+    if (g_decode_path == kPathI8 && i8_supported(L.w0.k, L.m)) return launch_i8_gemv(L, stream);
+    if (g_decode_path == kPathTc && tc_supported(L.w0.k, m_eff) && tc_gemv_fits(L)) return launch_tc_gemv(L, stream);
     UnitArgs a{};
     a.L = L;
     const int K = (int)L.w0.k;
@@ -833,7 +843,8 @@ cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream) {
     const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
-    if (g_use_tc && tc_supported(L.w.k, m_eff) && tc_lm_head_fits(L)) return launch_tc_lm_head(L, stream);
+    if (g_decode_path == kPathI8 && i8_supported(L.w.k, L.m)) return launch_i8_lm_head(L, stream);
+    if (g_decode_path == kPathTc && tc_supported(L.w.k, m_eff) && tc_lm_head_fits(L)) return launch_tc_lm_head(L, stream);
     LmArgs a{};
     a.L = L;
     const int K = (int)L.w.k;

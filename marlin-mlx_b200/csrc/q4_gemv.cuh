@@ -41,12 +41,14 @@ struct GemvLaunch {
     bool pdl;  // launch with programmatic stream serialization
 };
 
-// Activation rows per pass: the GEMV handles m * planes <= 32 (planes = 1 for bf16, 3 for binary32
-// or RMSNorm'ed input: exact bf16 hi/mid/lo split); the lm_head kernel m * planes <= 16.
-int gemv_max_rows(int act_dtype);
+// Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default), tcgen05/TMEM, bf16
+// mma.sync.  Shapes a family does not cover use the bf16 mma.sync kernels.
+enum DecodePath : int { kPathI8 = 0, kPathTc = 1, kPathBf16 = 2 };
+bool set_decode_path(int path);
+
+// Activation rows per launch of the selected family for this shape (the C ABI loops over passes).
+int gemv_max_rows(int act_dtype, bool normed, int64_t k);
 int lm_head_max_rows(int act_dtype, bool normed, int64_t k);
-// Use the tcgen05 (TMEM) kernels where they apply (default) or the mma.sync kernels only.
-void set_tcgen05(bool enable);
 
 // Launches the decode GEMV family (one CTA per row block, weights fetched before the PDL wait).
 // Returns cudaSuccess or the launch error.  Arguments are validated by the caller.

@@ -1,0 +1,754 @@
+// q4_i8.cu — Q4 decode GEMV family and fused lm_head + argmax on integer tensor-core MMAs (sm_100a).
+//
+// Replaces mx::quantized_matmul(x, w, scales, biases, transpose=true, 64, 4) for decode-sized
+// activations of marlin-mlx (src/model/marlin.cpp:18-25, :31-35, :161-169) and the greedy
+// mx::argmax after the lm_head (src/sampling/sampler.cpp:14-16).
+//
+// Arithmetic.  Per 64-group, y = s * sum(x * q) + b * sum(x) (the reference's dequant w = s*q + b).
+// The codes q (0..15) are the integer MMA's A operand as they are: one LOP3 turns a packed word
+// into four code bytes, a shift and a LOP3 give the other four.  The activation row is written as
+// four signed 8-bit planes with one power-of-two scale c_m per row and CTA:
+//     x = c_m * (i0 + i1 / 128 + i2 / 128^2 + i3 / 128^3),   |i_p| <= 64,
+// exact for every element within 2^-27 of the row's largest magnitude.  mma.m16n8k32 (s8 x s8 ->
+// s32) then forms sum(q * i_p) exactly; the fold per group is y += s * D_p (binary32), the
+// bias term b * sum(x) / c_m rides on plane 0, and the planes combine once per output
+// (sum_p c_m 128^-p y_p).  No dequantized weight is ever materialised.
+//
+// Streaming.  A producer warp moves weights with 2-D TMA into a ring of stages: per stage one
+// 128-byte line (4 groups) of 128 rows with 128-byte swizzle + the rows' scales and biases.  Eight
+// consumer warps each own 16 rows.  The GEMV family splits K over a thread-block cluster and
+// reduces partial sums through distributed shared memory; its weights are requested before
+// griddepcontrol.wait so they stream while the previous kernel finishes.  The lm_head kernel is
+// persistent over 128-row vocabulary blocks and keeps argmax keys (ordered logit << 32 | ~index).
+#include "common.cuh"
+#include "q4_gemv.cuh"
+#include "q4_host.cuh"
+#include "q4_i8.cuh"
+#include "q4_stage.cuh"
+
+#include <algorithm>
+
+namespace marlin {
+namespace {
+
+constexpr int kI8Rows = 128;                          // weight rows per block: 8 warps x 16
+constexpr int kI8Warps = 8;                           // consumer warps
+constexpr int kI8Threads = (kI8Warps + 1) * 32;       // + the TMA producer warp
+constexpr int kI8StageGroups = 4;                     // 64-groups per stage (one 128-byte line per row)
+constexpr uint32_t kI8Packed = kI8Rows * 128;         // 16 KB of packed words per stage
+constexpr uint32_t kI8Sb = kI8Rows * 16;              // scales (or biases) box: 8 groups x 128 rows
+constexpr uint32_t kI8StageBytes = kI8Packed + 2 * kI8Sb;  // 20 KB
+constexpr uint32_t kNib = 0x0F0F0F0Fu;
+constexpr uint32_t kI8SmemLimit = 225 * 1024;
+constexpr uint32_t kI8TwoPerSm = 110 * 1024;          // two CTAs per SM (PDL overlap of neighbours)
+
+// ------------------------------------------------------------------------------------------------
+// activation staging: four s8 planes per row, [group][column][64 B] with column = 4 m + p.
+// Within a group's 64 bytes, unit u (elements 8u..8u+7) occupies bytes 8u..8u+7 as
+// (x0, x2, x4, x6, x1, x3, x5, x7): the order the B fragment of mma.m16n8k32 needs when the A
+// fragment is (q0, q2, q4, q6 | q1, q3, q5, q7) of one packed word.
+// ------------------------------------------------------------------------------------------------
+struct I8X {
+    uint8_t* xq;          // [ng][ncols][64]
+    float* xs;            // [ng][ncols]: plane-0 columns hold sum_g(x) / c_m, the others 0
+    float* cs;            // [ncols]: c_m * 128^-p (0 for padding columns)
+    float* rf;            // [M] RMSNorm factors
+    float* ssq;           // [M * K/8] RMSNorm scratch
+    unsigned int* amax;   // [M] max |x| (binary32 bits) over the staged range
+};
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// exponent e with max|x| < 2^e (clamped so that every plane scale stays a normal binary32)
+__device__ __forceinline__ int row_exp(unsigned int abits) {
+    const int eb = (int)((abits >> 23) & 0xffu);
+    const int e = eb == 0 ? -125 : eb - 126;
+    return max(e, -90);
+}
+
+// Eight activations of row m from column k, RMSNorm'ed as marlin.cpp:12-16 when norm_w is set.
+__device__ __forceinline__ void load_norm8(const void* x, int dtype, int K, const uint16_t* norm_w, const float* rf,
+                                           int m, int k, float (&v)[8]) {
+    load8(x, dtype, (int64_t)m * K + k, v);
+    if (norm_w) {
+        const uint4 nwv = *reinterpret_cast<const uint4*>(norm_w + k);
+        const uint32_t w4[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+        const float r = rf[m];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float wj = bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+            v[j] = __fmul_rn(__fmul_rn(v[j], r), __fadd_rn(1.0f, wj));
+        }
+    }
+}
+
+// Max over the warp of `bits` for the lanes whose row is m0, and for row m1 when the warp's 32
+// consecutive units straddle two rows; one shared-memory atomic per row and warp.
+__device__ __forceinline__ void warp_row_max(unsigned int* amax, unsigned int bits, int m, int base, int total, int upr) {
+    const int m0 = base / upr, m1 = min(base + 31, total - 1) / upr;
+    const unsigned int r0 = __reduce_max_sync(0xffffffffu, m == m0 ? bits : 0u);
+    if ((threadIdx.x & 31) == 0) atomicMax(&amax[m0], r0);
+    if (m1 != m0) {
+        const unsigned int r1 = __reduce_max_sync(0xffffffffu, m == m1 ? bits : 0u);
+        if ((threadIdx.x & 31) == 0) atomicMax(&amax[m1], r1);
+    }
+}
+
+// The four s8 planes of eight activations with row exponent e (|x| < 2^e, up to rounding):
+// x = 2^(e-13) A + 2^(e-27) B with integers |A|, |B| <= 2^13 + 8 (both steps exact), then each of
+// A, B splits into two balanced base-128 digits: A = 128 i0 + i1, i1 in [-64, 63].  Bytes go out in
+// the B-fragment order (x0, x2, x4, x6 | x1, x3, x5, x7).
+__device__ __forceinline__ void planes8(const float (&v)[8], int e, uint32_t (&b)[4][2]) {
+    const float s1 = pow2f(13 - e), d1 = pow2f(e - 13), s2 = pow2f(27 - e);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) b[p][0] = b[p][1] = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float qa = rintf(__fmul_rn(v[j], s1));
+        const int A = (int)qa;
+        const int B = __float2int_rn(__fmul_rn(fmaf(-qa, d1, v[j]), s2));
+        const int i0 = (A + 64) >> 7, i2 = (B + 64) >> 7;
+        const int d[4] = {i0, A - (i0 << 7), i2, B - (i2 << 7)};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) b[p][j & 1] |= ((uint32_t)d[p] & 0xffu) << (8 * (j >> 1));
+    }
+}
+
+// RMSNorm of eight activations as marlin.cpp:12-16: (x * r) * (1 + w), binary32.
+__device__ __forceinline__ void norm8(float (&v)[8], uint4 nwv, float r) {
+    const uint32_t w4[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float wj = bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+        v[j] = __fmul_rn(__fmul_rn(v[j], r), __fadd_rn(1.0f, wj));
+    }
+}
+
+constexpr int kStageU = 2;  // 8-element activation units per thread and chunk, held in registers
+
+// Stage groups [g0, g0 + ng) of the M activation rows (ng % 4 == 0).  All threads of the block
+// call it; it ends with a barrier.  The rows are read in chunks of kStageU units per thread (whole
+// rows when RMSNorm applies, since its factor needs every column; else only the staged range).
+// With one chunk, x is read from global memory once and the norm sums, row maxima and planes come
+// from registers; larger inputs read each chunk twice.
+__device__ void stage_x_i8(const void* x, int dtype, int K, const uint16_t* norm_w, float eps, int g0, int ng, int M,
+                           int ncols, const I8X& t) {
+    const int nt = blockDim.x, tid = threadIdx.x, lane = tid & 31;
+    const bool normed = norm_w != nullptr;
+    const int upr_l = normed ? K / 8 : ng * 8;  // units per row read
+    const int kfirst = normed ? 0 : g0 * kGroup;
+    const int u0 = normed ? g0 * 8 : 0;         // first staged unit within a read row
+    const int total_l = M * upr_l, per_chunk = kStageU * nt;
+    const int nchunk = (total_l + per_chunk - 1) / per_chunk;
+    float v[kStageU][8];
+    uint4 nw[kStageU];
+    auto load_chunk = [&](int c) {
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int idx = c * per_chunk + u * nt + tid;
+            if (idx < total_l) {
+                const int k = kfirst + (idx % upr_l) * 8;
+                load8(x, dtype, (int64_t)(idx / upr_l) * K + k, v[u]);
+                if (normed) nw[u] = *reinterpret_cast<const uint4*>(norm_w + k);
+            }
+        }
+    };
+    load_chunk(0);
+    if (tid < M) t.amax[tid] = 0u;
+    for (int i = tid; i < ng * ncols; i += nt) t.xs[i] = 0.f;
+    const int pad = ncols - 4 * M;
+    for (int i = tid; i < ng * pad * 4; i += nt) {
+        const int gl = i / (pad * 4), rem = i % (pad * 4);
+        *reinterpret_cast<uint4*>(t.xq + ((size_t)gl * ncols + 4 * M + rem / 4) * 64 + (rem % 4) * 16) =
+            make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    // norm sums per unit (reduced by finish_norm_factors in a fixed order) and raw row maxima:
+    // max |x (1 + w)| with RMSNorm (the positive factor r scales the maximum afterwards; the
+    // plane split only needs a bound within a factor of two), else max |x|
+#pragma unroll 1
+    for (int c = 0; c < nchunk; ++c) {
+        if (c > 0) load_chunk(c);
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int base = c * per_chunk + u * nt + tid - lane;  // warp-uniform
+            if (base < total_l) {
+                const int idx = base + lane;
+                unsigned int bits = 0u;
+                int m = -1;
+                if (idx < total_l) {
+                    m = idx / upr_l;
+                    float amx = 0.f;
+                    if (normed) {
+                        t.ssq[idx] = unit_ssq(v[u], dtype);
+                        const uint32_t w4[4] = {nw[u].x, nw[u].y, nw[u].z, nw[u].w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            amx = fmaxf(amx, fabsf(v[u][j] * (1.0f + bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu))));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) amx = fmaxf(amx, fabsf(v[u][j]));
+                    }
+                    bits = __float_as_uint(amx);
+                }
+                warp_row_max(t.amax, bits, m, base, total_l, upr_l);
+            }
+        }
+    }
+    __syncthreads();
+    if (normed) {
+        XGeom xg{nullptr, nullptr, t.rf, t.ssq, M, 1, M, 0, 0};
+        finish_norm_factors(dtype, M, K, eps, xg);  // ends with a barrier
+    }
+    for (int c = tid; c < ncols; c += nt) {
+        const int m = c >> 2, p = c & 3;
+        float mx = 0.f;
+        if (m < M) mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
+        t.cs[c] = m < M ? pow2f(row_exp(__float_as_uint(mx)) - 6 - 7 * p) : 0.f;
+    }
+#pragma unroll 1
+    for (int c = 0; c < nchunk; ++c) {
+        if (nchunk > 1) load_chunk(c);
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int base = c * per_chunk + u * nt + tid - lane;  // warp-uniform
+            if (base < total_l) {
+                const int idx = base + lane;
+                const int m = idx < total_l ? idx / upr_l : 0, ul = idx < total_l ? idx % upr_l - u0 : -1;
+                const bool ok = idx < total_l && ul >= 0 && ul < ng * 8;
+                float s = 0.f, inv0 = 0.f;
+                if (ok) {
+                    if (normed) norm8(v[u], nw[u], t.rf[m]);
+                    const float mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
+                    const int e = row_exp(__float_as_uint(mx));
+                    inv0 = pow2f(6 - e);
+                    uint32_t b[4][2];
+                    planes8(v[u], e, b);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[u][j]);
+                    const int gl = ul >> 3, u8 = ul & 7;
+#pragma unroll
+                    for (int p = 0; p < 4; ++p)
+                        *reinterpret_cast<uint2*>(t.xq + ((size_t)gl * ncols + 4 * m + p) * 64 + u8 * 8) =
+                            make_uint2(b[p][0], b[p][1]);
+                }
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s += __shfl_xor_sync(0xffffffffu, s, 4);
+                if (ok && (lane & 7) == 0) t.xs[(ul >> 3) * ncols + 4 * m] = __fmul_rn(s, inv0);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------------
+// one stage (4 groups) of one warp's 16 rows: y[j][0..1] row g, y[j][2..3] row g+8, columns
+// 8j + 2t + {0, 1} (lane = 4g + t)
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float sel_bf16(uint2 v, int q) {
+    const uint32_t w = q < 2 ? v.x : v.y;
+    return __uint_as_float((q & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+
+template <int NTN>
+__device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int ncols, int warp,
+                                         int lane, float (&y)[NTN][4]) {
+    // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
+    const int g = lane >> 2, tq = lane & 3;
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    const uint8_t* sc = st + kI8Packed;
+    const uint8_t* bi = sc + kI8Sb;
+    const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
+    const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
+    const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
+    const uint2 b1 = *reinterpret_cast<const uint2*>(bi + r1 * 16 + so);
+    uint2 wa[4], wb[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // the group's 32 bytes are units 2q, 2q+1 of the swizzled line
+        const uint32_t off = (uint32_t)((((2 * q + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
+        wa[q] = *reinterpret_cast<const uint2*>(st + r0 * 128 + off);
+        wb[q] = *reinterpret_cast<const uint2*>(st + r1 * 128 + off);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t a0[4] = {wa[q].x & kNib, wb[q].x & kNib, (wa[q].x >> 4) & kNib, (wb[q].x >> 4) & kNib};
+        const uint32_t a1[4] = {wa[q].y & kNib, wb[q].y & kNib, (wa[q].y >> 4) & kNib, (wb[q].y >> 4) & kNib};
+        const float sr0 = sel_bf16(s0, q), sr1 = sel_bf16(s1, q), br0 = sel_bf16(b0, q), br1 = sel_bf16(b1, q);
+        const int gl = gl0 + q;
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
+            int c[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};  // the two K-steps accumulate independently
+            mma_s8_16832(c, a0, xv.x, xv.y);
+            mma_s8_16832(e, a1, xv.z, xv.w);
+            const float2 xs = *reinterpret_cast<const float2*>(t.xs + gl * ncols + 8 * j + 2 * tq);
+            y[j][0] = fmaf(sr0, (float)(c[0] + e[0]), fmaf(br0, xs.x, y[j][0]));
+            y[j][1] = fmaf(sr0, (float)(c[1] + e[1]), fmaf(br0, xs.y, y[j][1]));
+            y[j][2] = fmaf(sr1, (float)(c[2] + e[2]), fmaf(br1, xs.x, y[j][2]));
+            y[j][3] = fmaf(sr1, (float)(c[3] + e[3]), fmaf(br1, xs.y, y[j][3]));
+        }
+    }
+}
+
+// Issue the TMA copies of one stage: groups [gs, gs + 4) of rows [row0, row0 + rows) of one matrix
+// (rows = 128, or 64 per matrix for the gate/up pair with row offset ro).
+__device__ __forceinline__ void i8_issue(uint8_t* st, const CUtensorMap* tw, const CUtensorMap* ts,
+                                         const CUtensorMap* tb, int gs, int64_t row0, int ro, uint64_t* bar) {
+    tma_load_2d(st + ro * 128, tw, gs * 8, (int32_t)row0, bar);
+    tma_load_2d(st + kI8Packed + ro * 16, ts, gs & ~7, (int32_t)row0, bar);
+    tma_load_2d(st + kI8Packed + kI8Sb + ro * 16, tb, gs & ~7, (int32_t)row0, bar);
+}
+
+// ------------------------------------------------------------------------------------------------
+// decode GEMV family: one 128-row block per thread-block cluster, K split over the cluster's CTAs
+// ------------------------------------------------------------------------------------------------
+struct I8UnitArgs {
+    CUtensorMap tw0, ts0, tb0, tw1, ts1, tb1;  // w0 (gate / main) and w1 (up) maps
+    GemvLaunch L;
+    int G, CL, gpc, S, ncols;  // groups, cluster size, groups per CTA, ring stages, activation columns
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_red, off_xq, off_ring;
+};
+
+// One instantiation per activation width serves all three epilogues (a run-time switch), so the
+// gate/up and down launches of a decode step run the same, already cached, instructions.
+template <int NTN>
+__global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_constant__ I8UnitArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int MS = 2 * NTN;  // activation rows per pass
+    const GemvLaunch& L = a.L;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = (int)L.m, CL = a.CL, S = a.S, ncols = a.ncols;
+    const uint32_t rank = CL > 1 ? cluster_rank() : 0u;
+    const int block = blockIdx.x / CL;
+    const int g0 = (int)rank * a.gpc, ng = min(a.gpc, a.G - g0);
+    const int nst = ng / kI8StageGroups;
+    const int EPI = L.epi;
+    const bool kSwiglu = EPI == kEpiSwiglu;
+    const int kHalf = kSwiglu ? kI8Rows / 2 : kI8Rows;  // rows per matrix in the block
+    const int64_t row0 = (int64_t)block * kHalf;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+    uint64_t* empty = full + S;
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
+    float* red = reinterpret_cast<float*>(smem + a.off_red);  // [CL][128][MS], then the SwiGLU exchange
+    uint8_t* ring = smem + a.off_ring;
+    I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
+           reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
+           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
+
+    auto issue = [&](int q) {
+        uint8_t* st = ring + (size_t)(q % S) * kI8StageBytes;
+        const int gs = g0 + q * kI8StageGroups;
+        mbar_arrive_expect_tx(&full[q % S], kI8StageBytes);
+        i8_issue(st, &a.tw0, &a.ts0, &a.tb0, gs, row0, 0, &full[q % S]);
+        if (kSwiglu) i8_issue(st, &a.tw1, &a.ts1, &a.tb1, gs, row0, kHalf, &full[q % S]);
+    };
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kI8Warps);
+        }
+        fence_mbar_init();
+        prefetch_tmap(&a.tw0);
+        // as much of this CTA's weight range as the ring holds, before the dependency wait
+        for (int q = 0; q < min(S, nst); ++q) issue(q);
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
+    stage_x_i8(L.x, L.x_dtype, (int)L.w0.k, L.norm_w, L.eps, g0, ng, M, ncols, tx);
+
+    float y[NTN][4];
+#pragma unroll
+    for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+    if (warp == kI8Warps) {
+        if (lane == 0) {
+            int q = min(S, nst);
+            for (; q < nst; ++q) {
+                if (!thread_wait(&empty[q % S], (uint32_t)(((q / S) - 1) & 1), abort)) break;
+                issue(q);
+            }
+            for (int r = max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
+        }
+    } else {
+        for (int q = 0; q < nst; ++q) {
+            if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
+            const int gs = g0 + q * kI8StageGroups;
+            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, ncols, warp,
+                          lane, y);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[q % S]);
+        }
+        // planes -> one partial per (row, activation row), into the leader's slot for this rank
+        const int g = lane >> 2, tq = lane & 3;
+        const int r0 = 16 * warp + g;
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
+            float p0 = fmaf(cv.x, y[j][0], cv.y * y[j][1]);
+            float p1 = fmaf(cv.x, y[j][2], cv.y * y[j][3]);
+            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+            const int m = 2 * j + (tq >> 1);
+            if ((tq & 1) == 0 && m < M) {
+                float* s0 = red + ((size_t)rank * kI8Rows + r0) * MS + m;
+                float* s1 = red + ((size_t)rank * kI8Rows + r0 + 8) * MS + m;
+                if (rank == 0) {
+                    *s0 = p0;
+                    *s1 = p1;
+                } else {
+                    st_cluster_f32(s0, 0, p0);
+                    st_cluster_f32(s1, 0, p1);
+                }
+            }
+        }
+    }
+    if (CL > 1) cluster_sync_all();
+    else __syncthreads();
+    if (rank != 0 || tid >= kI8Rows) return;
+
+    // leader epilogue: thread = block row lrow; out[m] = sum over the cluster's partials
+    const int lrow = tid;
+    float o[MS];
+#pragma unroll
+    for (int m = 0; m < MS; ++m) {
+        o[m] = 0.f;
+        if (m < M)
+            for (int r = 0; r < CL; ++r) o[m] += red[((size_t)r * kI8Rows + lrow) * MS + m];
+    }
+    if (kSwiglu) {
+        // up rows (64..127) hand their outputs to the gate rows through shared memory
+        float* xch = red + (size_t)CL * kI8Rows * MS;
+        if (lrow >= kHalf) {
+#pragma unroll
+            for (int m = 0; m < MS; ++m) xch[(lrow - kHalf) * MS + m] = o[m];
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (lrow < kHalf) {
+            const int64_t f = row0 + lrow;
+            if (f < L.w0.n) {
+#pragma unroll
+                for (int m = 0; m < MS; ++m) {
+                    if (m < M) {
+                        const float gsum = o[m], u = xch[lrow * MS + m];
+                        if (L.y_dtype == kBF16) {
+                            const float gq = bf16_round(gsum), uq = bf16_round(u);
+                            const float sg = bf16_round(__fdividef(1.0f, 1.0f + expf(-gq)));
+                            const float r = bf16_round(bf16_round(sg * gq) * uq);
+                            static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + f] = (uint16_t)f32_to_bf16_bits(r);
+                        } else {
+                            const float sg = 1.0f / (1.0f + expf(-gsum));
+                            static_cast<float*>(L.y)[(int64_t)m * L.ldy + f] = (sg * gsum) * u;
+                        }
+                    }
+                }
+            }
+        }
+        return;
+    }
+    const int64_t row = row0 + lrow;
+    if (row >= L.w0.n) return;
+#pragma unroll
+    for (int m = 0; m < MS; ++m) {
+        if (m < M) {
+            float v = o[m];
+            if (EPI == kEpiResid) {
+                const float hv = L.resid_dtype == kBF16
+                                     ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[(int64_t)m * L.ldr + row])
+                                     : static_cast<const float*>(L.resid)[(int64_t)m * L.ldr + row];
+                v = hv + v;
+            }
+            if (L.y_dtype == kBF16)
+                static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + row] = (uint16_t)f32_to_bf16_bits(v);
+            else
+                static_cast<float*>(L.y)[(int64_t)m * L.ldy + row] = v;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// fused lm_head + argmax (persistent over 128-row vocabulary blocks)
+// ------------------------------------------------------------------------------------------------
+struct I8LmArgs {
+    CUtensorMap tw, ts, tb;
+    LmHeadLaunch L;
+    int G, S, nblocks, ncols;
+    uint32_t off_bar, off_misc, off_keys, off_scr, off_xs, off_cs, off_xq, off_ring;
+};
+
+__device__ __forceinline__ unsigned long long i8_logit_key(float v, int64_t idx) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+
+template <int NTN>
+__global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_constant__ I8LmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const LmHeadLaunch& L = a.L;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.G, S = a.S, M = (int)L.m, ncols = a.ncols;
+    const int spb = G / kI8StageGroups;  // stages per block
+    const int my_blocks =
+        a.nblocks > (int)blockIdx.x ? (a.nblocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nst = my_blocks * spb;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+    uint64_t* empty = full + S;
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
+    unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);  // [8][M]
+    uint8_t* ring = smem + a.off_ring;
+    I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
+           reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
+           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
+
+    auto issue = [&](int q) {
+        const int bi = q / spb, gs = (q % spb) * kI8StageGroups;
+        const int64_t row0 = (int64_t)(blockIdx.x + (int64_t)bi * gridDim.x) * kI8Rows;
+        uint8_t* st = ring + (size_t)(q % S) * kI8StageBytes;
+        mbar_arrive_expect_tx(&full[q % S], kI8StageBytes);
+        i8_issue(st, &a.tw, &a.ts, &a.tb, gs, row0, 0, &full[q % S]);
+    };
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kI8Warps);
+        }
+        fence_mbar_init();
+        prefetch_tmap(&a.tw);
+        prefetch_tmap(&a.ts);
+        prefetch_tmap(&a.tb);
+        for (int q = 0; q < min(S, nst); ++q) issue(q);
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
+    stage_x_i8(L.x, L.x_dtype, (int)L.w.k, L.norm_w, L.eps, 0, G, M, ncols, tx);
+
+    if (warp == kI8Warps) {
+        if (lane == 0) {
+            int q = min(S, nst);
+            for (; q < nst; ++q) {
+                if (!thread_wait(&empty[q % S], (uint32_t)(((q / S) - 1) & 1), abort)) break;
+                issue(q);
+            }
+            for (int r = max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
+        }
+    } else {
+        const int g = lane >> 2, tq = lane & 3;
+        const bool bf16_logits = L.x_dtype == kBF16 && !L.norm_w;
+        float y[NTN][4];
+        unsigned long long best[NTN];
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+            best[j] = 0ull;
+        }
+        for (int q = 0; q < nst; ++q) {
+            if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
+            const int sp = q % spb, gs = sp * kI8StageGroups;
+            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[q % S]);
+            if (sp == spb - 1) {  // block finished: logits -> argmax keys (max over the warp's rows)
+                const int64_t rowa = (int64_t)(blockIdx.x + (int64_t)(q / spb) * gridDim.x) * kI8Rows + 16 * warp + g;
+                const int64_t rowb = rowa + 8;
+#pragma unroll
+                for (int j = 0; j < NTN; ++j) {
+                    const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
+                    float la = fmaf(cv.x, y[j][0], cv.y * y[j][1]);
+                    float lb = fmaf(cv.x, y[j][2], cv.y * y[j][3]);
+                    la += __shfl_xor_sync(0xffffffffu, la, 1);
+                    lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+                    if (bf16_logits) {
+                        la = bf16_round(la);
+                        lb = bf16_round(lb);
+                    }
+                    const int m = 2 * j + (tq >> 1);
+                    unsigned long long ka = (m < M && rowa < L.w.n) ? i8_logit_key(la, L.vocab_offset + rowa) : 0ull;
+                    const unsigned long long kb =
+                        (m < M && rowb < L.w.n) ? i8_logit_key(lb, L.vocab_offset + rowb) : 0ull;
+                    ka = kb > ka ? kb : ka;
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) {
+                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, ka, o);
+                        ka = other > ka ? other : ka;
+                    }
+                    best[j] = ka > best[j] ? ka : best[j];
+                    y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+                }
+            }
+        }
+        if (g == 0 && (tq & 1) == 0) {
+#pragma unroll
+            for (int j = 0; j < NTN; ++j) {
+                const int m = 2 * j + (tq >> 1);
+                if (m < M) ckeys[warp * M + m] = best[j];
+            }
+        }
+    }
+    __syncthreads();
+    __shared__ bool is_last;
+    if (tid < M) {
+        unsigned long long k = 0ull;
+        for (int w = 0; w < kI8Warps; ++w) k = ckeys[w * M + tid] > k ? ckeys[w * M + tid] : k;
+        if (k) atomicMax(&L.keys[tid], k);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned int prev = atomicAdd(L.counter, 1u);
+        is_last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (is_last) {
+        __threadfence();
+        if (tid < M) {
+            const unsigned long long k = atomicExch(&L.keys[tid], 0ull);
+            if (L.keys_out) L.keys_out[tid] = k;
+            const uint32_t o = (uint32_t)(k >> 32);
+            const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+            if (L.ids) L.ids[tid] = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+            if (L.best) L.best[tid] = __uint_as_float(u);
+        }
+        if (tid == 0) atomicExch(L.counter, 0u);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+int ntn_for(int64_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
+
+// Shared-memory layout common to both kernels; returns the byte offset after the activations.
+uint32_t plan_common(int M, int K, bool normed, int ng, int ncols, uint32_t& off_bar, uint32_t& off_misc,
+                     uint32_t& off_scr, uint32_t& off_xs, uint32_t& off_cs, int S) {
+    uint32_t off = 0;
+    off_bar = off;
+    off += align_up(2u * (uint32_t)S * 8u, 128);
+    off_misc = off;
+    off += 128;  // abort flag + amax[M <= 16]
+    off_scr = off;
+    off += align_up((64 + (normed ? (uint32_t)M * (K / 8) : 0u)) * 4, 128);
+    off_xs = off;
+    off += align_up((uint32_t)ng * ncols * 4, 128);
+    off_cs = off;
+    off += align_up((uint32_t)ncols * 4, 128);
+    return off;
+}
+
+uint32_t plan_i8_unit(const GemvLaunch& L, I8UnitArgs& a) {
+    a.L = L;
+    const int K = (int)L.w0.k;
+    a.G = K / kGroup;
+    const int ntn = ntn_for(L.m);
+    a.ncols = 8 * ntn;
+    const bool swiglu = L.epi == kEpiSwiglu;
+    const int half = swiglu ? kI8Rows / 2 : kI8Rows;
+    const int blocks = (int)((L.w0.n + half - 1) / half);
+    // cluster size: split K until the grid covers the SMs (groups per CTA stay a multiple of 4)
+    int CL = 0;
+    for (int c : {1, 2, 4, 8}) {
+        if (a.G % c || (a.G / c) % kI8StageGroups) continue;
+        CL = c;
+        if ((int64_t)blocks * c >= device_num_sms()) break;
+    }
+    if (!CL) return 0;
+    a.CL = CL;
+    a.gpc = a.G / CL;
+    const int nst = a.gpc / kI8StageGroups;
+    const int ms = 2 * ntn;
+    for (int S = nst; S >= 2 || S == nst; --S) {
+        uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.gpc, a.ncols, a.off_bar, a.off_misc, a.off_scr,
+                                   a.off_xs, a.off_cs, S);
+        a.off_red = off;
+        off += align_up((uint32_t)(CL + 1) * kI8Rows * ms * 4, 128);  // partials + SwiGLU exchange
+        a.off_xq = off;
+        off += (uint32_t)a.gpc * a.ncols * 64;
+        off = align_up(off, 1024);
+        a.off_ring = off;
+        off += (uint32_t)S * kI8StageBytes + 1024;
+        const uint32_t limit = (S == nst && off <= kI8TwoPerSm) ? kI8TwoPerSm : kI8SmemLimit;
+        if (off <= limit) {
+            a.S = S;
+            return off;
+        }
+        if (S <= 2) break;
+    }
+    return 0;
+}
+
+uint32_t plan_i8_lm_head(const LmHeadLaunch& L, I8LmArgs& a) {
+    a.L = L;
+    const int K = (int)L.w.k;
+    a.G = K / kGroup;
+    a.ncols = 8 * ntn_for(L.m);
+    a.nblocks = (int)((L.w.n + kI8Rows - 1) / kI8Rows);
+    for (int S = 12; S >= 2; --S) {
+        uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.G, a.ncols, a.off_bar, a.off_misc, a.off_scr,
+                                   a.off_xs, a.off_cs, S);
+        a.off_keys = off;
+        off += align_up(kI8Warps * (uint32_t)L.m * 8, 128);
+        a.off_xq = off;
+        off += (uint32_t)a.G * a.ncols * 64;
+        off = align_up(off, 1024);
+        a.off_ring = off;
+        off += (uint32_t)S * kI8StageBytes + 1024;
+        if (off <= kI8SmemLimit) {
+            a.S = S;
+            return off;
+        }
+    }
+    return 0;
+}
+
+template <int NTN>
+cudaError_t dispatch_i8_unit(const I8UnitArgs& a, int grid, uint32_t smem, cudaStream_t stream) {
+    return launch_ex(i8_unit_kernel<NTN>, a, grid, kI8Threads, a.CL, smem, a.L.pdl, stream);
+}
+
+}  // namespace
+
+bool i8_supported(int64_t k, int64_t m) {
+    // k >= 512: the scales/biases boxes are 8 groups wide and may not exceed the tensor
+    return k % 256 == 0 && k >= 512 && k <= 16384 && m >= 1 && m <= kI8MaxRows && tmap_encode_fn() != nullptr;
+}
+
+cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream) {
+    I8UnitArgs a{};
+    const uint32_t smem = plan_i8_unit(L, a);
+    if (!smem) return cudaErrorInvalidConfiguration;
+    const bool swiglu = L.epi == kEpiSwiglu;
+    const int half = swiglu ? kI8Rows / 2 : kI8Rows;
+    if (!encode_q4_maps(L.w0, half, &a.tw0, &a.ts0, &a.tb0)) return cudaErrorInvalidValue;
+    if (swiglu && !encode_q4_maps(L.w1, half, &a.tw1, &a.ts1, &a.tb1)) return cudaErrorInvalidValue;
+    const int blocks = (int)((L.w0.n + half - 1) / half);
+    const int grid = blocks * a.CL;
+    switch (a.ncols / 8) {
+        case 1: return dispatch_i8_unit<1>(a, grid, smem, stream);
+        case 2: return dispatch_i8_unit<2>(a, grid, smem, stream);
+        case 4: return dispatch_i8_unit<4>(a, grid, smem, stream);
+        default: return dispatch_i8_unit<8>(a, grid, smem, stream);
+    }
+}
+
+cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream) {
+    I8LmArgs a{};
+    const uint32_t smem = plan_i8_lm_head(L, a);
+    if (!smem) return cudaErrorInvalidConfiguration;
+    if (!encode_q4_maps(L.w, kI8Rows, &a.tw, &a.ts, &a.tb)) return cudaErrorInvalidValue;
+    const int grid = std::max(1, std::min(device_num_sms(), a.nblocks));
+    switch (a.ncols / 8) {
+        case 1: return launch_ex(i8_lm_head_kernel<1>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
+        case 2: return launch_ex(i8_lm_head_kernel<2>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
+        case 4: return launch_ex(i8_lm_head_kernel<4>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
+        default: return launch_ex(i8_lm_head_kernel<8>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
+    }
+}
+
+int i8_device_error(bool clear) { return tu_device_error(clear); }
+
+}  // namespace marlin

@@ -1,0 +1,24 @@
+// q4_i8.cuh — launchers of the integer-MMA Q4 decode kernels (the default decode path).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q4_gemv.cuh"
+
+namespace marlin {
+
+// Activation rows per launch of the integer-MMA kernels (4 planes x 16 rows = 64 MMA columns).
+constexpr int kI8MaxRows = 16;
+
+// True when the integer-MMA kernels handle this shape: k a multiple of 256 in [512, 16384] and
+// 1 <= m <= kI8MaxRows.
+bool i8_supported(int64_t k, int64_t m);
+// Decode GEMV family (same contract as launch_q4_gemv).
+cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream);
+// Fused lm_head + argmax (same contract as launch_q4_lm_head_argmax).
+cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream);
+// Device error word of this translation unit (see gemv_device_error).
+int i8_device_error(bool clear);
+
+}  // namespace marlin

@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "q4_gemv.cuh"
 #include "q4_stage.cuh"
+#include "q4_host.cuh"
 #include "q4_tc.cuh"
 
 #include <cuda.h>
@@ -138,45 +139,6 @@ __device__ void stage_x_tc(const void* x, int dtype, int K, const uint16_t* norm
 // ------------------------------------------------------------------------------------------------
 // shared pieces
 // ------------------------------------------------------------------------------------------------
-// Bounded wait that also ends early once another role has aborted (timeout recorded on device).
-// Every lane acquires the barrier; the exit is warp-uniform.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
-        if ((it & 63u) == 63u) {
-            int stop = 0;
-            if ((threadIdx.x & 31) == 0) {
-                if (*abort) {
-                    stop = 1;
-                } else if (globaltimer_ns() - t0 > 2000000000ull || it > (1u << 28)) {
-                    record_device_error(kDevErrMbarTimeout);
-                    *abort = 1;
-                    stop = 1;
-                }
-            }
-            if (__shfl_sync(0xffffffffu, stop, 0)) return false;
-        }
-    }
-}
-// Single-thread bounded wait (producer / MMA issuer).
-__device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 0; it < (1u << 28); ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 63u) {
-            if (*abort) return false;
-            if (globaltimer_ns() - t0 > 2000000000ull) {
-                record_device_error(kDevErrMbarTimeout);
-                *abort = 1;
-                return false;
-            }
-        }
-    }
-    *abort = 1;
-    return false;
-}
-
 __device__ __forceinline__ void tma_load_2d_cta(void* dst, const CUtensorMap* tm, int32_t x, int32_t y, uint64_t* bar) {
     tma_load_2d(dst, tm, x, y, bar);
 }
@@ -259,13 +221,36 @@ __device__ __forceinline__ void fold_group(float (&y)[C::USED], const float (&d)
 }
 
 // ------------------------------------------------------------------------------------------------
-// fused lm_head + argmax (persistent)
+// fused lm_head + argmax (persistent, one CTA per SM, all 512 TMEM columns)
+//
+// Warp roles (416 threads):
+//   warps 0-7  dequant: warp w serves TMEM lane quarter w & 3 (rows 32(w&3) .. +31) and group
+//              w >> 2 of each 2-group batch; after a named barrier over these 8 warps, one elected
+//              thread issues the batch's 8 MMAs and commits them to d_ready[buf];
+//   warps 8-11 fold: wait d_ready, read the two D blocks with tcgen05.ld, release the buffer
+//              (d_free), apply scale and bias in binary32 and keep the running argmax keys;
+//   warp 12    TMA producer for the stage ring.
+// NB buffers of (2 x 32 A columns + 2 x NCOL D columns) rotate through TMEM, so up to 2 NB groups
+// are between dequant and fold: enough to cover the MMA -> commit -> mbarrier latency.
 // ------------------------------------------------------------------------------------------------
+constexpr int kLmDeqWarps = 8;
+constexpr int kLmThreads = (kLmDeqWarps + 4 + 1) * 32;
+constexpr int kLmBatch = 2;  // 64-groups per MMA batch
+constexpr uint32_t kLmTmemCols = 512;
+
+template <class C>
+struct LmBuf {
+    static constexpr int ACOLS = kLmBatch * 32;
+    static constexpr int DCOLS = kLmBatch * C::NCOL;
+    static constexpr int NB = (int)kLmTmemCols / (ACOLS + DCOLS);  // 5 (NCOL 16) or 4 (NCOL 32)
+    static constexpr int D0 = NB * ACOLS;                          // first D column
+};
+
 struct TcLmArgs {
     CUtensorMap tw, ts, tb;  // packed words [n][k/8] box [32 x 128]; scales, biases [n][k/64] box [8 x 128]
     LmHeadLaunch L;
     int P, Meff, G, S, ntiles;
-    uint32_t off_ring, off_xb, off_xs, off_scr, off_bar, off_misc;
+    uint32_t off_ring, off_xb, off_xs, off_scr, off_bar, off_misc, off_sbq;
 };
 
 __device__ __forceinline__ unsigned long long logit_key(float v, int64_t idx) {
@@ -274,44 +259,52 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int64_t idx) {
     return ((unsigned long long)o << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1) tc_lm_head_kernel(const __grid_constant__ TcLmArgs a) {
+__global__ void __launch_bounds__(kLmThreads, 1) tc_lm_head_kernel(const __grid_constant__ TcLmArgs a) {
+    using B = LmBuf<C>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const LmHeadLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G, S = a.S, M = (int)L.m;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bar);
-    uint64_t* full = bars;            // [S]
-    uint64_t* empty = bars + S;       // [S]
-    uint64_t* a_full = bars + 2 * S;  // [2]
-    uint64_t* d_ready = a_full + 2;   // [2]
-    uint64_t* d_free = d_ready + 2;   // [2]
+    uint64_t* full = bars;             // [S]   TMA bytes landed
+    uint64_t* empty = bars + S;        // [S]   8 dequant warps done with the stage
+    uint64_t* d_ready = bars + 2 * S;  // [NB]  MMAs of the batch complete (+ issuer's arrive)
+    uint64_t* d_free = d_ready + B::NB;  // [NB] 4 fold warps done with the buffer
+    uint64_t* fin = d_free + B::NB;    // [1]   exit drain of the issuer's MMAs
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + a.off_misc);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc + 4);
     unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(smem + a.off_misc + 64);  // [4][M]
+    float2* sbq = reinterpret_cast<float2*>(smem + a.off_sbq);  // [NB][2][128] (16 s, b - 16 s)
     uint8_t* ring = smem + a.off_ring;
     TcX tx{smem + a.off_xb, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_scr),
            reinterpret_cast<float*>(smem + a.off_scr) + 64};
-    const int spt = (G + kStageGroups - 1) / kStageGroups;  // stages per tile
+    const int spt = G / kStageGroups;  // stages per tile (G % 8 == 0)
+    const int bpt = G / kLmBatch;      // batches per tile
     const int my_tiles = a.ntiles > (int)blockIdx.x ? (a.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int nstages = my_tiles * spt;
+    const int nbatch = my_tiles * bpt;
 
-    if (warp == 5) {
-        tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 8) {
+        tmem_alloc(tmem_slot, kLmTmemCols);
         tmem_relinquish();
     }
     if (tid == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 4);
+            mbar_init(&empty[s], kLmDeqWarps);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&a_full[b], 4);
-            mbar_init(&d_ready[b], 1);
+        for (int b = 0; b < B::NB; ++b) {
+            mbar_init(&d_ready[b], 2);
             mbar_init(&d_free[b], 4);
         }
+        mbar_init(fin, 1);
         fence_mbar_init();
     }
     tc_fence_before();
@@ -322,20 +315,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_lm_head_kernel(const __grid_co
     auto issue_stage = [&](int q) {  // stage q of this CTA's sequence
         const int ti = q / spt, sp = q % spt;
         const int64_t row0 = (int64_t)(blockIdx.x + (int64_t)ti * gridDim.x) * kRows;
-        const int gs = sp * kStageGroups, ngr = min(kStageGroups, G - gs);
+        const int gs = sp * kStageGroups;
         uint8_t* st = ring + (size_t)(q % S) * kStageBytes;
-        const int nbox = (ngr + 3) / 4;
-        mbar_arrive_expect_tx(&full[q % S], nbox * kBoxBytes + 2u * kRows * 16u);
-        for (int c = 0; c < nbox; ++c)
+        mbar_arrive_expect_tx(&full[q % S], 2 * kBoxBytes + 2u * kRows * 16u);
+        for (int c = 0; c < 2; ++c)
             tma_load_2d(st + c * kBoxBytes, &a.tw, (gs / 4 + c) * 32, (int32_t)row0, &full[q % S]);
         tma_load_2d(st + 2 * kBoxBytes, &a.ts, gs, (int32_t)row0, &full[q % S]);
         tma_load_2d(st + 2 * kBoxBytes + kRows * 16, &a.tb, gs, (int32_t)row0, &full[q % S]);
     };
-    if (warp == 4 && lane == 0) {
+    int issued = 0;
+    if (warp == 12 && lane == 0) {
         prefetch_tmap(&a.tw);
         prefetch_tmap(&a.ts);
         prefetch_tmap(&a.tb);
-        for (int q = 0; q < min(S, nstages); ++q) issue_stage(q);
+        for (; issued < min(S, nstages); ++issued) issue_stage(issued);
     }
     pdl_wait();
     pdl_launch_dependents();
@@ -345,121 +338,128 @@ __global__ void __launch_bounds__(kThreads, 1) tc_lm_head_kernel(const __grid_co
     __syncthreads();
     tc_fence_after();
 
-    const int ngroups = my_tiles * G;
-    if (warp == 4) {
+    if (warp == 12) {
         if (lane == 0) {
-            for (int q = S; q < nstages; ++q) {
+            for (; issued < nstages; ++issued) {
+                const int q = issued;
                 if (!thread_wait(&empty[q % S], (uint32_t)(((q / S) - 1) & 1), abort)) break;
                 issue_stage(q);
             }
+            // exit only once every copy this thread started has landed
+            for (int q = max(0, issued - S); q < issued; ++q) drain_wait(&full[q % S], (uint32_t)((q / S) & 1));
         }
-    } else if (warp == 5) {
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc_bf16(kRows, C::NCOL);
-            for (int gi = 0; gi < ngroups; ++gi) {
-                const int buf = gi & 1;
-                if (!thread_wait(&a_full[buf], (uint32_t)((gi >> 1) & 1), abort)) break;
-                if (gi >= 2 && !thread_wait(&d_free[buf], (uint32_t)(((gi - 2) >> 1) & 1), abort)) break;
+    } else if (warp < kLmDeqWarps) {
+        const int quarter = warp & 3, gsub = warp >> 2;
+        const int lrow = 32 * quarter + lane;
+        const uint32_t lane_addr = (uint32_t)(32 * quarter) << 16;
+        const uint32_t idesc = umma_idesc_bf16(kRows, C::NCOL);
+        bool ok = true;
+        for (int bi = 0; bi < nbatch; ++bi) {
+            const int buf = bi % B::NB;
+            const int ti = bi / bpt, gb = (bi % bpt) * kLmBatch;  // first group of the batch
+            const int gl = gb + gsub;
+            const int q = ti * spt + gl / kStageGroups;
+            const int s = q % S, gs = gl % kStageGroups;
+            if (ok && gs < kLmBatch) ok = warp_wait(&full[s], (uint32_t)((q / S) & 1), abort);
+            if (ok && bi >= B::NB) ok = warp_wait(&d_free[buf], (uint32_t)(((bi / B::NB) - 1) & 1), abort);
+            if (ok) {
+                const uint8_t* st = ring + (size_t)s * kStageBytes;
+                uint32_t av[32];
+                dequant_group(st + (gs >> 2) * kBoxBytes + lrow * 128, lrow, gs & 3, av);
+                const uint16_t sraw = *reinterpret_cast<const uint16_t*>(st + 2 * kBoxBytes + lrow * 16 + gs * 2);
+                const uint16_t braw =
+                    *reinterpret_cast<const uint16_t*>(st + 2 * kBoxBytes + kRows * 16 + lrow * 16 + gs * 2);
+                const float sf = bf16_bits_to_f32(sraw), bfv = bf16_bits_to_f32(braw);
+                sbq[(buf * kLmBatch + gsub) * kRows + lrow] = make_float2(sf * 16.0f, bfv - sf * 16.0f);
+                if (gs >= kStageGroups - kLmBatch) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads stage s
+                }
+                tmem_st32(tmem + lane_addr + buf * B::ACOLS + gsub * 32, av);
+                tmem_wait_st();
+            }
+            tc_fence_before();
+            named_bar_sync(1, kLmDeqWarps * 32);
+            if (warp == 0 && lane == 0) {
                 tc_fence_after();
-                const int gl = gi % G;
+                if (!*abort) {
 #pragma unroll
-                for (int s = 0; s < 4; ++s)
-                    umma_tmem_a(tmem + 64 + buf * C::NCOL, tmem + buf * 32 + 8 * s,
-                                umma_desc_sw128(tx.xb + gl * (C::NCOL * 128) + 32 * s), idesc, s > 0);
-                umma_commit(&d_ready[buf]);
+                    for (int g = 0; g < kLmBatch; ++g) {
+                        const uint8_t* xg = tx.xb + (gb + g) * (C::NCOL * 128);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            umma_tmem_a(tmem + B::D0 + buf * B::DCOLS + g * C::NCOL,
+                                        tmem + buf * B::ACOLS + g * 32 + 8 * k, umma_desc_sw128(xg + 32 * k), idesc,
+                                        k > 0);
+                    }
+                    umma_commit(&d_ready[buf]);
+                }
+                mbar_arrive(&d_ready[buf]);  // orders the sbq stores (named barrier above) before the fold
             }
         }
+        if (warp == 0 && lane == 0) {  // every MMA this thread issued has completed before TMEM is freed
+            umma_commit(fin);
+            drain_wait(fin, 0);
+        }
     } else {
-        // dequant / fold warps: thread = row 32*warp + lane of the tile
-        const int lrow = 32 * warp + lane;
-        const uint32_t lane_addr = (uint32_t)(32 * warp) << 16;
+        // fold warps: thread = row 32 * (warp & 3) + lane of the tile
+        const int quarter = warp & 3;
+        const int lrow = 32 * quarter + lane;
+        const uint32_t lane_addr = (uint32_t)(32 * quarter) << 16;
         float y[C::USED];
-        unsigned long long best[C::MS];
+        unsigned long long best = 0ull;  // lane m keeps the best key of activation row m
 #pragma unroll
         for (int j = 0; j < C::USED; ++j) y[j] = 0.f;
-#pragma unroll
-        for (int m = 0; m < C::MS; ++m) best[m] = 0ull;
         const bool bf16_logits = L.x_dtype == kBF16 && !L.norm_w;
-        float2 sb_prev = make_float2(0.f, 0.f);
-        uint4 sv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0);
-        auto fold = [&](int gj, float2 sbj) -> bool {
-            const int buf = gj & 1;
-            if (!warp_wait(&d_ready[buf], (uint32_t)((gj >> 1) & 1), abort)) return false;
+        for (int bi = 0; bi < nbatch; ++bi) {
+            const int buf = bi % B::NB;
+            if (!warp_wait(&d_ready[buf], (uint32_t)((bi / B::NB) & 1), abort)) break;
             tc_fence_after();
+            const int ti = bi / bpt, gb = (bi % bpt) * kLmBatch;
+            const uint32_t dcol = tmem + lane_addr + B::D0 + buf * B::DCOLS;
+            const float2 sb0 = sbq[(buf * kLmBatch + 0) * kRows + lrow];
+            const float2 sb1 = sbq[(buf * kLmBatch + 1) * kRows + lrow];
+            {
+                float d[C::LDC];
+                tmem_ld_cols<C::LDC>(dcol, d);
+                fold_group<C>(y, d, tx.xs + gb * 32, sb0, M);
+            }
             float d[C::LDC];
-            tmem_ld_cols<C::LDC>(tmem + lane_addr + 64 + buf * C::NCOL, d);
+            tmem_ld_cols<C::LDC>(dcol + C::NCOL, d);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&d_free[buf]);
-            const int gl = gj % G;
-            fold_group<C>(y, d, tx.xs + gl * 32, sbj, M);
-            if (gl == G - 1) {  // tile finished: logits -> argmax keys
-                const int64_t row = (int64_t)(blockIdx.x + (int64_t)(gj / G) * gridDim.x) * kRows + lrow;
-                if (row < L.w.n) {
+            fold_group<C>(y, d, tx.xs + (gb + 1) * 32, sb1, M);
+            if (gb + kLmBatch == G) {  // tile finished: logits -> argmax keys (warp max per row)
+                const int64_t row = (int64_t)(blockIdx.x + (int64_t)ti * gridDim.x) * kRows + lrow;
 #pragma unroll
-                    for (int m = 0; m < C::MS; ++m) {
-                        if (C::MFIX || m < M) {
-                            float v = 0.f;
+                for (int m = 0; m < C::MS; ++m) {
+                    if (C::MFIX || m < M) {
+                        float v = 0.f;
 #pragma unroll
-                            for (int p = 0; p < C::P; ++p) v += y[m * C::P + p];
-                            if (bf16_logits) v = bf16_round(v);
-                            const unsigned long long k = logit_key(v, L.vocab_offset + row);
-                            best[m] = k > best[m] ? k : best[m];
+                        for (int p = 0; p < C::P; ++p) v += y[m * C::P + p];
+                        if (bf16_logits) v = bf16_round(v);
+                        unsigned long long k = row < L.w.n ? logit_key(v, L.vocab_offset + row) : 0ull;
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) {
+                            const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
+                            k = other > k ? other : k;
                         }
+                        if (lane == m) best = k > best ? k : best;
                     }
                 }
 #pragma unroll
                 for (int j = 0; j < C::USED; ++j) y[j] = 0.f;
             }
-            return true;
-        };
-        bool ok = true;
-        for (int gi = 0; gi < ngroups && ok; ++gi) {
-            const int ti = gi / G, gl = gi % G;
-            const int q = ti * spt + gl / kStageGroups;
-            const int s = q % S;
-            const uint8_t* st = ring + (size_t)s * kStageBytes;
-            const int gs = gl % kStageGroups;
-            if (gs == 0) {
-                if (!warp_wait(&full[s], (uint32_t)((q / S) & 1), abort)) break;
-                sv = *reinterpret_cast<const uint4*>(st + 2 * kBoxBytes + lrow * 16);
-                bv = *reinterpret_cast<const uint4*>(st + 2 * kBoxBytes + kRows * 16 + lrow * 16);
-            }
-            uint32_t av[32];
-            dequant_group(st + (gs >> 2) * kBoxBytes + lrow * 128, lrow, gs & 3, av);
-            const float2 sb_cur = stage_sb(sv, bv, gs);
-            if (gs == kStageGroups - 1 || gl == G - 1) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads stage s
-            }
-            const int buf = gi & 1;
-            tmem_st32(tmem + lane_addr + buf * 32, av);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[buf]);
-            if (gi >= 1) ok = fold(gi - 1, sb_prev);
-            sb_prev = sb_cur;
         }
-        if (ok && ngroups > 0) fold(ngroups - 1, sb_prev);
-        // CTA reduction of the keys: warp max, then across the 4 dequant warps
-#pragma unroll
-        for (int m = 0; m < C::MS; ++m) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const unsigned long long other = __shfl_xor_sync(0xffffffffu, best[m], o);
-                best[m] = other > best[m] ? other : best[m];
-            }
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int m = 0; m < C::MS; ++m)
-                if (m < M) ckeys[warp * M + m] = best[m];
-        }
+        if (lane < M) ckeys[quarter * M + lane] = best;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) tmem_dealloc(tmem, kTmemCols);
+    if (warp == 8) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kLmTmemCols);
+    }
     __shared__ bool is_last;
     if (tid < M) {
         unsigned long long k = 0ull;
@@ -496,20 +496,6 @@ struct TcUnitArgs {
     int P, Meff, G, CL, gpc;  // gpc = groups per CTA
     uint32_t off_ring, off_xb, off_xs, off_scr, off_bar, off_misc, off_red;
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ void st_cluster_f32(const float* local_ptr, uint32_t rank, float v) {
-    uint32_t raddr;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(local_ptr)), "r"(rank));
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(raddr), "f"(v) : "memory");
-}
 
 template <class C, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_unit_kernel(const __grid_constant__ TcUnitArgs a) {
@@ -710,103 +696,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_unit_kernel(const __grid_const
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFn tc_encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-bool encode_maps(const Q4Mat& W, int box_rows, CUtensorMap* tw, CUtensorMap* ts, CUtensorMap* tb) {
-    EncodeTiledFn fn = tc_encode_fn();
-    if (!fn) return false;
-    const cuuint32_t es[2] = {1, 1};
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)(W.k / 8), (cuuint64_t)W.n};
-        const cuuint64_t strides[1] = {(cuuint64_t)(W.k / 2)};
-        const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
-        if (fn(tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(W.w), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    const cuuint64_t dims[2] = {(cuuint64_t)(W.k / 64), (cuuint64_t)W.n};
-    const cuuint64_t strides[1] = {(cuuint64_t)(W.k / 64 * 2)};
-    const cuuint32_t box[2] = {8, (cuuint32_t)box_rows};
-    for (int i = 0; i < 2; ++i) {
-        if (fn(i ? tb : ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(i ? W.b : W.s), dims, strides, box,
-               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    return true;
-}
-
-int tc_num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 constexpr uint32_t kTcSmemLimit = 225 * 1024;
 constexpr uint32_t kTcMinSmem = 80 * 1024;  // <= 2 TMEM-holding CTAs per SM (2 x 128 of 512 columns)
-
-template <typename KernelT, typename ArgT>
-cudaError_t tc_launch(KernelT kernel, const ArgT& args, int grid, int cluster, uint32_t smem, bool pdl,
-                      cudaStream_t stream) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    int na = 0;
-    if (pdl) {
-        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[na].val.programmaticStreamSerializationAllowed = 1;
-        ++na;
-    }
-    if (cluster > 1) {
-        attr[na].id = cudaLaunchAttributeClusterDimension;
-        attr[na].val.clusterDim.x = cluster;
-        attr[na].val.clusterDim.y = 1;
-        attr[na].val.clusterDim.z = 1;
-        ++na;
-    }
-    cfg.attrs = attr;
-    cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, kernel, args);
-}
 
 template <class C>
 cudaError_t dispatch_tc_unit(const TcUnitArgs& a, int grid, int CL, uint32_t smem, int epi, bool pdl,
                              cudaStream_t stream) {
-    if (epi == kEpiSwiglu) return tc_launch(tc_unit_kernel<C, kEpiSwiglu>, a, grid, CL, smem, pdl, stream);
-    if (epi == kEpiResid) return tc_launch(tc_unit_kernel<C, kEpiResid>, a, grid, CL, smem, pdl, stream);
-    return tc_launch(tc_unit_kernel<C, kEpiStore>, a, grid, CL, smem, pdl, stream);
+    if (epi == kEpiSwiglu) return launch_ex(tc_unit_kernel<C, kEpiSwiglu>, a, grid, kThreads, CL, smem, pdl, stream);
+    if (epi == kEpiResid) return launch_ex(tc_unit_kernel<C, kEpiResid>, a, grid, kThreads, CL, smem, pdl, stream);
+    return launch_ex(tc_unit_kernel<C, kEpiStore>, a, grid, kThreads, CL, smem, pdl, stream);
 }
 
 }  // namespace
 
 bool tc_supported(int64_t k, int64_t m_eff) {
-    return k % 512 == 0 && k >= 512 && m_eff >= 1 && m_eff <= 32 && tc_encode_fn() != nullptr;
+    return k % 512 == 0 && k >= 512 && m_eff >= 1 && m_eff <= 32 && tmap_encode_fn() != nullptr;
 }
 
 namespace {
@@ -831,16 +735,16 @@ cudaError_t launch_tc_lm_head(const LmHeadLaunch& L, cudaStream_t stream) {
     int ncol = 0;
     const uint32_t smem = plan_tc_lm_head(L, a, ncol);
     if (!smem) return cudaErrorInvalidConfiguration;
-    if (!encode_maps(L.w, kRows, &a.tw, &a.ts, &a.tb)) return cudaErrorInvalidValue;
-    const int grid = std::max(1, std::min(tc_num_sms(), a.ntiles));
+    if (!encode_q4_maps(L.w, kRows, &a.tw, &a.ts, &a.tb)) return cudaErrorInvalidValue;
+    const int grid = std::max(1, std::min(device_num_sms(), a.ntiles));
     if (a.P == 3) {
-        if (L.m == 1) return tc_launch(tc_lm_head_kernel<TcCfg<16, 3, 1>>, a, grid, 1, smem, L.pdl, stream);
-        if (ncol == 16) return tc_launch(tc_lm_head_kernel<TcCfg<16, 3, 0>>, a, grid, 1, smem, L.pdl, stream);
-        return tc_launch(tc_lm_head_kernel<TcCfg<32, 3, 0>>, a, grid, 1, smem, L.pdl, stream);
+        if (L.m == 1) return launch_ex(tc_lm_head_kernel<TcCfg<16, 3, 1>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
+        if (ncol == 16) return launch_ex(tc_lm_head_kernel<TcCfg<16, 3, 0>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
+        return launch_ex(tc_lm_head_kernel<TcCfg<32, 3, 0>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
     }
-    if (L.m == 1) return tc_launch(tc_lm_head_kernel<TcCfg<16, 1, 1>>, a, grid, 1, smem, L.pdl, stream);
-    if (ncol == 16) return tc_launch(tc_lm_head_kernel<TcCfg<16, 1, 0>>, a, grid, 1, smem, L.pdl, stream);
-    return tc_launch(tc_lm_head_kernel<TcCfg<32, 1, 0>>, a, grid, 1, smem, L.pdl, stream);
+    if (L.m == 1) return launch_ex(tc_lm_head_kernel<TcCfg<16, 1, 1>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
+    if (ncol == 16) return launch_ex(tc_lm_head_kernel<TcCfg<16, 1, 0>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
+    return launch_ex(tc_lm_head_kernel<TcCfg<32, 1, 0>>, a, grid, kLmThreads, 1, smem, L.pdl, stream);
 }
 
 cudaError_t launch_tc_gemv(const GemvLaunch& L, cudaStream_t stream) {
@@ -870,14 +774,17 @@ uint32_t plan_tc_lm_head(const LmHeadLaunch& L, TcLmArgs& a, int& ncol) {
     a.G = K / kGroup;
     a.P = (L.norm_w || L.x_dtype == kF32) ? 3 : 1;
     a.Meff = (int)L.m * a.P;
-    if (!tc_supported(K, a.Meff)) return 0;
+    if (!tc_supported(K, a.Meff) || a.G % kStageGroups != 0) return 0;
     ncol = a.Meff <= 16 ? 16 : 32;
+    const int nb = ncol == 16 ? LmBuf<TcCfg<16, 1, 0>>::NB : LmBuf<TcCfg<32, 1, 0>>::NB;
     a.ntiles = (int)((L.w.n + kRows - 1) / kRows);
     uint32_t off = 0;
     a.off_bar = off;
-    off += 256;
+    off += 512;  // 2 S + 2 NB + 1 mbarriers (S <= 12)
     a.off_misc = off;
     off += 64 + 4 * 32 * 8;
+    a.off_sbq = off;
+    off += (uint32_t)nb * kLmBatch * kRows * 8;
     a.off_scr = off;
     off += align_up((64 + (L.norm_w ? (uint32_t)L.m * (K / 8) : 0u)) * 4, 128);
     a.off_xs = off;
@@ -906,15 +813,15 @@ uint32_t plan_tc_gemv(const GemvLaunch& L, TcUnitArgs& a, int& ncol, bool encode
     // (groups per CTA stay a multiple of 8: the scales box x-coordinate must be 16-byte aligned)
     int CL = 1;
     for (int c : {2, 4, 8}) {
-        if ((int64_t)tiles * CL >= tc_num_sms()) break;
+        if ((int64_t)tiles * CL >= device_num_sms()) break;
         if (a.G % c == 0 && (a.G / c) % 8 == 0) CL = c;
     }
     if ((a.G / CL) % 8 != 0) return 0;
     a.CL = CL;
     a.gpc = a.G / CL;
     if (encode) {
-        if (!encode_maps(L.w0, half, &a.tw0, &a.ts0, &a.tb0)) return 0;
-        if (swiglu && !encode_maps(L.w1, half, &a.tw1, &a.ts1, &a.tb1)) return 0;
+        if (!encode_q4_maps(L.w0, half, &a.tw0, &a.ts0, &a.tb0)) return 0;
+        if (swiglu && !encode_q4_maps(L.w1, half, &a.tw1, &a.ts1, &a.tb1)) return 0;
     }
     const int nst = (a.gpc + kStageGroups - 1) / kStageGroups;
     if (nst > 8) return 0;
@@ -940,5 +847,7 @@ uint32_t plan_tc_gemv(const GemvLaunch& L, TcUnitArgs& a, int& ncol, bool encode
 }
 
 }  // namespace
+
+int tc_device_error(bool clear) { return tu_device_error(clear); }
 
 }  // namespace marlin

@@ -17,5 +17,7 @@ bool tc_lm_head_fits(const LmHeadLaunch& L);
 cudaError_t launch_tc_gemv(const GemvLaunch& L, cudaStream_t stream);
 // Fused lm_head + argmax on tcgen05 (same contract as launch_q4_lm_head_argmax).
 cudaError_t launch_tc_lm_head(const LmHeadLaunch& L, cudaStream_t stream);
+// Device error word of this translation unit (see gemv_device_error).
+int tc_device_error(bool clear);
 
 }  // namespace marlin

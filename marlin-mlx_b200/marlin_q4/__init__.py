@@ -6,8 +6,8 @@ package binds it for torch tensors (tests, benchmarks, the tensor-parallel drive
 from ._lib import LIB_PATH, MarlinQ4Error, load  # noqa: F401
 from .ops import (DecodeStep, Layer, LmHeadWorkspace, QuantizedTensor, decode_keys, device_error,  # noqa: F401
                   gate_up_swiglu, lm_head_argmax, matmul_residual, mlp_forward, qmatmul, quantize_weight,
-                  residual_add, rms_norm, set_pdl, set_tcgen05, synth_bf16)
+                  residual_add, rms_norm, set_decode_path, set_pdl, synth_bf16)
 
 __all__ = ["QuantizedTensor", "quantize_weight", "qmatmul", "rms_norm", "gate_up_swiglu", "matmul_residual",
            "mlp_forward", "residual_add", "lm_head_argmax", "LmHeadWorkspace", "decode_keys", "Layer",
-           "DecodeStep", "synth_bf16", "device_error", "set_pdl", "set_tcgen05", "load", "LIB_PATH", "MarlinQ4Error"]
+           "DecodeStep", "synth_bf16", "device_error", "set_pdl", "set_decode_path", "load", "LIB_PATH", "MarlinQ4Error"]

@@ -254,6 +254,9 @@ def set_pdl(enable: bool) -> None:
     _lib.load().marlin_q4_set_pdl(1 if enable else 0)
 
 
-def set_tcgen05(enable: bool) -> None:
-    """Select the tcgen05/TMEM decode kernels (default) or the mma.sync kernels for every shape."""
-    _lib.load().marlin_q4_set_tcgen05(1 if enable else 0)
+DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "tcgen05": _lib.PATH_TCGEN05, "bf16": _lib.PATH_BF16MMA}
+
+
+def set_decode_path(path: str) -> None:
+    """Select the decode kernel family: "i8" (integer MMAs, default), "tcgen05" or "bf16" (mma.sync)."""
+    check(_lib.load().marlin_q4_set_decode_path(DECODE_PATHS[path]), "marlin_q4_set_decode_path")

@@ -1,12 +1,13 @@
 """Standalone driver of the decode kernels, for profilers (ncu) and quick timing.
 
-    python -m marlin_q4.prof [--m 1] [--reps 3] [--time]
+    python -m marlin_q4.prof [--m 1] [--reps 3] [--time] [--path i8|tcgen05|bf16]
 
 Builds one decode layer (gate/up/down Q4 [6144,2048]/[2048,6144]) and the Q4 lm_head
 [248320, 2048] from the seeded generator, then launches, in this order, `reps` times each:
 gate_up_swiglu (RMSNorm fused), matmul_residual (down + residual), lm_head_argmax (final norm
 fused), and qmatmul (config 1: bf16 x [1, 2048] . W[6144, 2048]^T).  About 1.6 GB on the device.
-With --time, prints each family's CUDA-event time per launch (back-to-back launches, no graph).
+With --time, prints each family's CUDA-event time per launch: `reps` launches captured in one CUDA
+graph (so host launch cost is excluded), replayed after a warm-up replay.
 """
 from __future__ import annotations
 
@@ -24,8 +25,10 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--time", action="store_true")
+    ap.add_argument("--path", default="i8", choices=sorted(mq.ops.DECODE_PATHS))
     a = ap.parse_args()
     torch.cuda.set_device(0)
+    mq.set_decode_path(a.path)
     g = mq.quantize_weight(mq.synth_bf16((I, H), 1000, 0.0, 0.02))
     u = mq.quantize_weight(mq.synth_bf16((I, H), 1001, 0.0, 0.02))
     d = mq.quantize_weight(mq.synth_bf16((H, I), 1002, 0.0, 0.02))
@@ -48,13 +51,19 @@ def main() -> None:
         if a.time:
             f()
             torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(a.reps):
+                    f()
+            graph.replay()
+            torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(a.reps):
-                f()
+            graph.replay()
             e1.record()
             e1.synchronize()
             print(f"{name}: {e0.elapsed_time(e1) / a.reps * 1e3:.2f} us/launch")
+            del graph
         else:
             for _ in range(a.reps):
                 f()

@@ -1,6 +1,5 @@
-"""GPU parity of the two decode kernel families: tcgen05/TMEM (default where k % 512 == 0 and
-m * planes <= 32) and the warp-level mma.sync kernels, each against the CPU oracle and against
-each other on the same inputs."""
+"""GPU parity of the three decode kernel families — integer MMAs on the codes (default), tcgen05/TMEM
+and bf16 mma.sync — each against the CPU oracle and against each other on the same inputs."""
 import numpy as np
 import pytest
 import torch
@@ -12,11 +11,11 @@ from gpu_util import TOL, act, f32, host_act, host_q4, make_q4, max_rel_row_err,
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["tcgen05", "mma.sync"])
+@pytest.fixture(params=["i8", "tcgen05", "bf16"])
 def path(request):
-    mq.set_tcgen05(request.param == "tcgen05")
+    mq.set_decode_path(request.param)
     yield request.param
-    mq.set_tcgen05(True)
+    mq.set_decode_path("i8")
 
 
 @pytest.fixture(scope="module")
@@ -75,9 +74,10 @@ def test_lm_head_paths(oracle, mats, path, m, dtype, norm):
 def test_paths_agree_on_decode_layer(mats):
     h = act((2, 2048), 110, torch.float32)
     outs = []
-    for tc in (True, False):
-        mq.set_tcgen05(tc)
+    for p in ("i8", "tcgen05", "bf16"):
+        mq.set_decode_path(p)
         a = mq.gate_up_swiglu(h, mats["g"], mats["u"], norm_weight=mats["nw"])
         outs.append(f32(mq.matmul_residual(a, mats["d"], h)))
-    mq.set_tcgen05(True)
-    assert max_rel_row_err(outs[0], outs[1].astype(np.float64)) < 1e-5
+    mq.set_decode_path("i8")
+    for o in outs[1:]:
+        assert max_rel_row_err(outs[0], o.astype(np.float64)) < 1e-5
