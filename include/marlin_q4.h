@@ -75,8 +75,7 @@ void marlin_q4_set_pdl(int enable);
 /* Decode kernel family (process-wide; every family computes the same function, within the float
  * tolerance, and each is tested against the CPU checker):
  *   MARLIN_Q4_PATH_I8MMA   (default) integer tensor-core MMAs on the raw codes and 4 s8 activation
- *                          planes, exact int32 accumulation (k % 256 == 0, k >= 512, m <= 16
- *                          per launch);
+ *                          planes, exact int32 accumulation (k % 512 == 0, m <= 16 per launch);
  *   MARLIN_Q4_PATH_TCGEN05 5th-generation tensor cores: bf16 codes in TMEM, tcgen05.mma
  *                          (k % 512 == 0, m * planes <= 32);
  *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0).
@@ -98,7 +97,10 @@ int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_si
 /* ---- quantized matmul --------------------------------------------------------------------------
  * Replaces mx::quantized_matmul(x, w.weight, w.scales, w.biases, transpose=true, 64, 4) in
  * qmatmul (src/model/marlin.cpp:18-25; declared src/core/types.h:84) and MarlinModel::lm_head
- * (src/model/marlin.cpp:161-169).  x: [m, k] of x_dtype; y: [m, n] of x_dtype.  Any m >= 1. */
+ * (src/model/marlin.cpp:161-169).  x: [m, k] of x_dtype; y: [m, n] of x_dtype.  Any m >= 1.
+ * bf16 x with m > 16 rows and k % 512 == 0 (prefill) runs one tcgen05 GEMM that dequantizes each
+ * weight once to bf16 (s*q + b, one rounding) in shared memory; decode-sized m keeps every product
+ * exact up to binary32 accumulation.  gate_up_swiglu and matmul_residual dispatch the same way. */
 int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, void* y,
                      void* stream);
 

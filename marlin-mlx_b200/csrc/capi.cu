@@ -7,6 +7,7 @@
 
 #include "q4_gemv.cuh"
 #include "q4_i8.cuh"
+#include "q4_prefill.cuh"
 #include "q4_tc.cuh"
 #include "q4_misc.cuh"
 
@@ -62,6 +63,26 @@ Q4Mat view(const marlin_q4_tensor* t) { return Q4Mat{t->weight, t->scales, t->bi
 int gemv_passes(const void* x, int32_t x_dtype, int64_t m, const uint16_t* norm_w, float eps, const Q4Mat& w0,
                 const Q4Mat& w1, int epi, void* y, int32_t y_dtype, int64_t ldy, const void* resid,
                 int32_t resid_dtype, int64_t ldr, cudaStream_t stream) {
+    {
+        // many bf16 rows (prefill): one tcgen05 GEMM launch over all of them
+        GemvLaunch L{};
+        L.x = x;
+        L.x_dtype = x_dtype;
+        L.m = m;
+        L.norm_w = norm_w;
+        L.eps = eps;
+        L.w0 = w0;
+        L.w1 = w1;
+        L.y = y;
+        L.y_dtype = y_dtype;
+        L.ldy = ldy;
+        L.resid = resid;
+        L.resid_dtype = resid_dtype;
+        L.ldr = ldr;
+        L.epi = epi;
+        L.pdl = g_pdl;
+        if (prefill_applies(L)) return cuda_status(launch_prefill(L, stream));
+    }
     const int64_t rp = gemv_max_rows(x_dtype, norm_w != nullptr, w0.k);
     for (int64_t r0 = 0; r0 < m; r0 += rp) {
         GemvLaunch L{};
@@ -112,9 +133,11 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
-    const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0);
+    const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0),
+              v_pf = prefill_device_error(clear != 0);
     if (!v) v = v_tc;
     if (!v) v = v_i8;
+    if (!v) v = v_pf;
     if (v < 0) return cuda_status(cudaGetLastError());
     return v;
 }

@@ -234,6 +234,10 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem_ptr) {
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// Instruction descriptor, kind::f16: D f32, A/B IEEE half, both K-major, M = m, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, single issuing thread.
 __device__ __forceinline__ void umma_tmem_a(uint32_t d_taddr, uint32_t a_taddr, uint64_t b_desc, uint32_t idesc,
                                             bool accumulate) {
@@ -270,6 +274,15 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4]
     asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Orders the computation of `v` before whatever follows (an empty-slot release): a ring stage may be
+// handed back to the producer only once every value loaded from it has been consumed, not merely
+// once the loads were issued.
+template <int N>
+__device__ __forceinline__ void hold_regs(const float (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" ::"f"(v[i]));
 }
 
 // ---- waits shared by the warp-specialised kernels ------------------------------------------------

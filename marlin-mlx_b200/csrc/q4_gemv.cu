@@ -554,6 +554,10 @@ __global__ void __launch_bounds__(kLmThreads, 1) q4_lm_head_kernel(const __grid_
                     group_mma<MT, HALF>(A, X, wv, sb, acc[t]);
                 }
             }
+#pragma unroll
+            for (int t = 0; t < kLmTiles; ++t)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) hold_regs(acc[t][mt]);  // stage data consumed before release
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads stage s
             float* rb = red + (size_t)(i & 1) * kLmConsumers * a.M_eff * kLmRows;

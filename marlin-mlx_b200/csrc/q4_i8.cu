@@ -378,6 +378,8 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
             const int gs = g0 + q * kI8StageGroups;
             i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, ncols, warp,
                           lane, y);
+#pragma unroll
+            for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q % S]);
         }
@@ -551,6 +553,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             const int sp = q % spb, gs = sp * kI8StageGroups;
             i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
+#pragma unroll
+            for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q % S]);
             if (sp == spb - 1) {  // block finished: logits -> argmax keys (max over the warp's rows)
@@ -713,8 +717,9 @@ cudaError_t dispatch_i8_unit(const I8UnitArgs& a, int grid, uint32_t smem, cudaS
 }  // namespace
 
 bool i8_supported(int64_t k, int64_t m) {
-    // k >= 512: the scales/biases boxes are 8 groups wide and may not exceed the tensor
-    return k % 256 == 0 && k >= 512 && k <= 16384 && m >= 1 && m <= kI8MaxRows && tmap_encode_fn() != nullptr;
+    // k % 512: the scales/biases tensor maps need a row stride (k/64 * 2 bytes) that is a
+    // multiple of 16 bytes
+    return k % 512 == 0 && k <= 16384 && m >= 1 && m <= kI8MaxRows && tmap_encode_fn() != nullptr;
 }
 
 cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream) {

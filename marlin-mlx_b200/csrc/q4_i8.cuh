@@ -11,7 +11,7 @@ namespace marlin {
 // Activation rows per launch of the integer-MMA kernels (4 planes x 16 rows = 64 MMA columns).
 constexpr int kI8MaxRows = 16;
 
-// True when the integer-MMA kernels handle this shape: k a multiple of 256 in [512, 16384] and
+// True when the integer-MMA kernels handle this shape: k a multiple of 512, at most 16384, and
 // 1 <= m <= kI8MaxRows.
 bool i8_supported(int64_t k, int64_t m);
 // Decode GEMV family (same contract as launch_q4_gemv).

@@ -371,12 +371,12 @@ __global__ void __launch_bounds__(kLmThreads, 1) tc_lm_head_kernel(const __grid_
                     *reinterpret_cast<const uint16_t*>(st + 2 * kBoxBytes + kRows * 16 + lrow * 16 + gs * 2);
                 const float sf = bf16_bits_to_f32(sraw), bfv = bf16_bits_to_f32(braw);
                 sbq[(buf * kLmBatch + gsub) * kRows + lrow] = make_float2(sf * 16.0f, bfv - sf * 16.0f);
-                if (gs >= kStageGroups - kLmBatch) {
+                tmem_st32(tmem + lane_addr + buf * B::ACOLS + gsub * 32, av);
+                tmem_wait_st();
+                if (gs >= kStageGroups - kLmBatch) {  // released once its words are in TMEM
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads stage s
                 }
-                tmem_st32(tmem + lane_addr + buf * B::ACOLS + gsub * 32, av);
-                tmem_wait_st();
             }
             tc_fence_before();
             named_bar_sync(1, kLmDeqWarps * 32);

@@ -26,9 +26,13 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--time", action="store_true")
     ap.add_argument("--path", default="i8", choices=sorted(mq.ops.DECODE_PATHS))
+    ap.add_argument("--prefill", type=int, default=0, help="time the C4 prefill layer with this many bf16 rows")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     mq.set_decode_path(a.path)
+    if a.prefill:
+        prefill(a)
+        return
     g = mq.quantize_weight(mq.synth_bf16((I, H), 1000, 0.0, 0.02))
     u = mq.quantize_weight(mq.synth_bf16((I, H), 1001, 0.0, 0.02))
     d = mq.quantize_weight(mq.synth_bf16((H, I), 1002, 0.0, 0.02))
@@ -67,6 +71,31 @@ def main() -> None:
         else:
             for _ in range(a.reps):
                 f()
+    torch.cuda.synchronize()
+    assert mq.device_error() == 0
+
+
+def prefill(a) -> None:
+    """C4: x bf16 [m, 2048] -> gate/up + SwiGLU -> down, each Q4 GEMM on the tcgen05 path."""
+    g = mq.quantize_weight(mq.synth_bf16((I, H), 1000, 0.0, 0.02))
+    u = mq.quantize_weight(mq.synth_bf16((I, H), 1001, 0.0, 0.02))
+    d = mq.quantize_weight(mq.synth_bf16((H, I), 1002, 0.0, 0.02))
+    x = mq.synth_bf16((a.prefill, H), 3000, 0.0, 1.0)
+    act = torch.empty((a.prefill, I), dtype=torch.bfloat16, device="cuda")
+    fams = {"gate_up_swiglu": (lambda: mq.gate_up_swiglu(x, g, u, out=act), 2 * 2.0 * a.prefill * I * H),
+            "down": (lambda: mq.qmatmul(act, d), 2.0 * a.prefill * I * H)}
+    for name, (f, flops) in fams.items():
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.reps):
+            f()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / a.reps * 1e3
+        print(f"{name}: {us:.2f} us/launch, {flops / us / 1e6:.1f} TFLOP/s")
     torch.cuda.synchronize()
     assert mq.device_error() == 0
 

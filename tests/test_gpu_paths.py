@@ -39,7 +39,8 @@ def test_qmatmul_paths(oracle, mats, path, m, dtype):
         ref = oracle.qmatmul(host_act(x), hq)
         if dtype == torch.bfloat16:
             assert max_rel_row_err(qo.bf16_to_f32(u16(y)), ref) < TOL
-            assert np.mean(u16(y) == qo.f32_to_bf16(ref)) > 0.99
+            # above 16 rows bf16 inputs take the prefill GEMM (weights dequantized to bf16)
+            assert np.mean(u16(y) == qo.f32_to_bf16(ref)) > (0.99 if m <= 16 else 0.5)
         else:
             assert max_rel_row_err(f32(y), ref) < 2e-5
     assert mq.device_error() == 0

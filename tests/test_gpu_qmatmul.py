@@ -1,7 +1,10 @@
 """GPU parity: Q4 quantized_matmul (transpose=true, gs 64) against the CPU oracle.
 
 bf16 activations -> bf16 output: within the path's tolerance (max rel error 1e-2 vs the fp32-
-accumulated reference) and equal to the oracle's bf16 rounding for nearly every element.
+accumulated reference) and, for decode-sized m (<= 16), equal to the oracle's bf16 rounding for
+nearly every element.  Above 16 rows bf16 inputs take the tcgen05 prefill GEMM, which rounds the
+dequantized weights to bf16 (as a bf16 tensor-core operand must be), so there only the tolerance
+and a majority of identical bf16 outputs are required.
 binary32 activations -> binary32 output: the kernel splits x exactly into three bf16 planes, so it
 must agree with the fp32 oracle to accumulation-order noise (max rel row error 2e-5)."""
 import numpy as np
@@ -34,7 +37,7 @@ def _check(oracle, x, q, hq):
         yb = u16(y)
         assert max_rel_row_err(qo.bf16_to_f32(yb), ref) < TOL
         same = np.mean(yb == qo.f32_to_bf16(ref))
-        assert same > 0.99, same
+        assert same > (0.99 if x.reshape(-1, x.shape[-1]).shape[0] <= 16 else 0.5), same
     else:
         assert max_rel_row_err(f32(y), ref) < 2e-5
     assert mq.device_error() == 0
