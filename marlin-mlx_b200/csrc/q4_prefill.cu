@@ -64,6 +64,7 @@ struct PrefillArgs {
     GemvLaunch L;
     int M, N, G;           // activation rows, output columns (features for SwiGLU), K groups
     int mtiles, ntiles;    // tile grid
+    int vec;               // 1: y (and resid) rows allow 16-byte vector access at 16-column steps
 };
 
 __device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
     uint64_t* bfull = sbempty + 2;        // [kPNB] 8 dequant warps
     uint64_t* bfree = bfull + kPNB;       // [kPNB] MMA commit
     uint64_t* dfull = bfree + kPNB;       // [2]
-    uint64_t* dempty = dfull + 2;         // [2] 4 epilogue warps
+    uint64_t* dempty = dfull + 2;         // [2] 4 epilogue warps (per accumulator; per half when MH == 2)
     uint64_t* fin = dempty + 2;           // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -259,12 +260,10 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             RingPos px, pb;
             bool ok = true;
             for (int lt = 0; lt < my_tiles && ok; ++lt) {
-                // MH == 1: accumulators alternate between tiles; MH == 2: both belong to every tile
+                // MH == 1: accumulators alternate between tiles; MH == 2: both belong to every tile, and
+                // half h is reused as soon as the epilogue has drained it (checked before its first MMA)
                 const int acc = MH == 1 ? (lt & 1) : 0;
-                const int use = MH == 1 ? (lt >> 1) : lt;  // earlier uses of this accumulator set
-                if (use >= 1 && (MH == 2 || lt >= 2) &&
-                    !thread_wait(&dempty[acc], (uint32_t)((use - 1) & 1), abort))
-                    break;
+                if (MH == 1 && lt >= 2 && !thread_wait(&dempty[acc], (uint32_t)(((lt >> 1) - 1) & 1), abort)) break;
                 for (int g = 0; g < G; ++g) {
                     if (!thread_wait(&xfull[px.slot], (uint32_t)(px.round & 1), abort) ||
                         !thread_wait(&bfull[pb.slot], (uint32_t)(pb.round & 1), abort)) {
@@ -275,11 +274,20 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                     const uint8_t* xa = xring + (size_t)px.slot * P::XSTAGE;
                     const uint8_t* wb = bbuf + (size_t)pb.slot * kPB;
 #pragma unroll
-                    for (int h = 0; h < MH; ++h)
+                    for (int h = 0; h < MH; ++h) {
+                        if (MH == 2 && g == 0 && lt >= 1) {
+                            if (!thread_wait(&dempty[h], (uint32_t)((lt - 1) & 1), abort)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             umma_smem_a(tmem + (acc + h) * kPN, umma_desc_sw128(xa + h * kPA + 32 * k),
                                         umma_desc_sw128(wb + 32 * k), idesc, g > 0 || k > 0);
+                    }
+                    if (!ok) break;
                     umma_commit(&xempty[px.slot]);
                     umma_commit(&bfree[pb.slot]);
                     if (g == G - 1) umma_commit(&dfull[acc]);
@@ -334,9 +342,11 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             }
         }
     } else {
-        // epilogue: TMEM lane quarter = warp & 3, lane = activation row within each 128-row half
+        // epilogue: TMEM lane quarter = warp & 3, lane = activation row within each 128-row half.
+        // Each thread writes 16 consecutive columns of its row per step (16-byte stores).
         const int quarter = warp & 3;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+        const bool ybf = L.y_dtype == kBF16;
         for (int lt = 0; lt < my_tiles; ++lt) {
             const int acc = MH == 1 ? (lt & 1) : 0;
             const int use = MH == 1 ? (lt >> 1) : lt;
@@ -348,58 +358,90 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 const int64_t m = ((int64_t)mt * MH + h) * kPM + 32 * quarter + lane;
                 const bool row_ok = m < a.M;
                 const uint32_t dcol = lane_base + (acc + h) * kPN;
-                if (swiglu) {
-                    for (int c0 = 0; c0 < kPN / 2; c0 += 16) {
-                        uint32_t gr[16], ur[16];
-                        tmem_ld16(dcol + c0, gr);
-                        tmem_ld16(dcol + kPN / 2 + c0, ur);
+                const int ncols = swiglu ? kPN / 2 : kPN;
+                for (int c0 = 0; c0 < ncols; c0 += 16) {
+                    uint32_t r0[16];
+                    float v[16];
+                    tmem_ld16(dcol + c0, r0);
+                    if (swiglu) {
+                        uint32_t u0[16];
+                        tmem_ld16(dcol + kPN / 2 + c0, u0);
                         tmem_wait_ld();
-                        const int64_t f0 = (int64_t)nt * (kPN / 2) + c0;
-                        if (row_ok) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float g0 = __uint_as_float(r0[i]), x0 = __uint_as_float(u0[i]);
+                            v[i] = ybf ? swiglu_bf16(g0, x0) : (g0 / (1.0f + expf(-g0))) * x0;
+                        }
+                    } else {
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r0[i]);
+                    }
+                    if (!row_ok) continue;
+                    const int64_t col0 = (int64_t)nt * ncols + c0;
+                    const bool full = a.vec && col0 + 16 <= a.N;
+                    if (epi == kEpiResid) {
+                        if (full && L.resid_dtype == kF32) {
+                            const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(L.resid) + m * L.ldr + col0);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float4 rv = rp[i];
+                                v[4 * i] += rv.x;
+                                v[4 * i + 1] += rv.y;
+                                v[4 * i + 2] += rv.z;
+                                v[4 * i + 3] += rv.w;
+                            }
+                        } else if (full) {
+                            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(L.resid) + m * L.ldr + col0);
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                const uint4 rv = rp[i];
+                                const uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    v[8 * i + 2 * j] += bf16_bits_to_f32(w4[j] & 0xffffu);
+                                    v[8 * i + 2 * j + 1] += bf16_bits_to_f32(w4[j] >> 16);
+                                }
+                            }
+                        } else {
 #pragma unroll
                             for (int i = 0; i < 16; ++i) {
-                                const int64_t f = f0 + i;
-                                if (f >= a.N) continue;
-                                const float gv = __uint_as_float(gr[i]), uv = __uint_as_float(ur[i]);
-                                if (L.y_dtype == kBF16)
-                                    static_cast<uint16_t*>(L.y)[m * L.ldy + f] =
-                                        (uint16_t)f32_to_bf16_bits(swiglu_bf16(gv, uv));
-                                else
-                                    static_cast<float*>(L.y)[m * L.ldy + f] = (gv / (1.0f + expf(-gv))) * uv;
+                                if (col0 + i >= a.N) continue;
+                                v[i] += L.resid_dtype == kBF16
+                                            ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[m * L.ldr + col0 + i])
+                                            : static_cast<const float*>(L.resid)[m * L.ldr + col0 + i];
                             }
                         }
                     }
-                } else {
-                    for (int c0 = 0; c0 < kPN; c0 += 16) {
-                        uint32_t dr[16];
-                        tmem_ld16(dcol + c0, dr);
-                        tmem_wait_ld();
-                        const int64_t n0 = (int64_t)nt * kPN + c0;
-                        if (row_ok) {
+                    if (full && ybf) {
+                        uint4* yp = reinterpret_cast<uint4*>(static_cast<uint16_t*>(L.y) + m * L.ldy + col0);
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const int64_t col = n0 + i;
-                                if (col >= a.N) continue;
-                                float v = __uint_as_float(dr[i]);
-                                if (epi == kEpiResid) {
-                                    const float hv =
-                                        L.resid_dtype == kBF16
-                                            ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[m * L.ldr + col])
-                                            : static_cast<const float*>(L.resid)[m * L.ldr + col];
-                                    v = hv + v;
-                                }
-                                if (L.y_dtype == kBF16)
-                                    static_cast<uint16_t*>(L.y)[m * L.ldy + col] = (uint16_t)f32_to_bf16_bits(v);
-                                else
-                                    static_cast<float*>(L.y)[m * L.ldy + col] = v;
-                            }
+                        for (int i = 0; i < 2; ++i) {
+                            uint32_t p[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                p[j] = f32_to_bf16_bits(v[8 * i + 2 * j]) | (f32_to_bf16_bits(v[8 * i + 2 * j + 1]) << 16);
+                            yp[i] = make_uint4(p[0], p[1], p[2], p[3]);
+                        }
+                    } else if (full) {
+                        float4* yp = reinterpret_cast<float4*>(static_cast<float*>(L.y) + m * L.ldy + col0);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) yp[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            if (col0 + i >= a.N) continue;
+                            if (ybf)
+                                static_cast<uint16_t*>(L.y)[m * L.ldy + col0 + i] = (uint16_t)f32_to_bf16_bits(v[i]);
+                            else
+                                static_cast<float*>(L.y)[m * L.ldy + col0 + i] = v[i];
                         }
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&dempty[MH == 1 ? acc : h]);  // this accumulator half is drained
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dempty[acc]);
         }
     }
     tc_fence_before();
@@ -464,6 +506,10 @@ cudaError_t launch_prefill(const GemvLaunch& L, cudaStream_t stream) {
     };
     if (!enc(L.w0, &a.tw0, &a.ts0, &a.tb0)) return cudaErrorInvalidValue;
     if (swiglu && !enc(L.w1, &a.tw1, &a.ts1, &a.tb1)) return cudaErrorInvalidValue;
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    const size_t ysz = L.y_dtype == kBF16 ? 2 : 4, rsz = L.resid_dtype == kBF16 ? 2 : 4;
+    a.vec = al16(L.y) && (L.ldy * (int64_t)ysz) % 16 == 0 &&
+            (L.epi != kEpiResid || (al16(L.resid) && (L.ldr * (int64_t)rsz) % 16 == 0));
     const int tiles = a.mtiles * a.ntiles;
     const int grid = std::max(1, std::min(device_num_sms(), tiles));
     if (mh == 2) return launch_ex(q4_prefill_kernel<2>, a, grid, kPThreads, 1, PPlan<2>::SMEM, L.pdl, stream);
