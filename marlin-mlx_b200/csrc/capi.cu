@@ -8,6 +8,7 @@
 #include "q4_gemv.cuh"
 #include "q4_i8.cuh"
 #include "q4_prefill.cuh"
+#include "q4_stack.cuh"
 #include "q4_tc.cuh"
 #include "q4_misc.cuh"
 
@@ -134,10 +135,11 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
     const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0),
-              v_pf = prefill_device_error(clear != 0);
+              v_pf = prefill_device_error(clear != 0), v_st = stack_device_error(clear != 0);
     if (!v) v = v_tc;
     if (!v) v = v_i8;
     if (!v) v = v_pf;
+    if (!v) v = v_st;
     if (v < 0) return cuda_status(cudaGetLastError());
     return v;
 }
@@ -278,9 +280,20 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
                                           static_cast<cudaStream_t>(stream)));
 }
 
+// Workspace of marlin_q4_decode_step: a zero-invariant head (grid-barrier words and the argmax keys,
+// zero before the first call and left zero by every call, whichever kernels run) followed by
+// scratch for either the one-kernel step or the per-kernel composition.
+namespace {
+size_t step_zero_bytes(int64_t m) { return 256 + align16((size_t)m * 8 + 16); }
+size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
+    return align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
+}
+}  // namespace
+
 size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate) {
     if (m <= 0 || hidden <= 0 || intermediate <= 0) return 0;
-    return align16((size_t)m * hidden * 4) + align16((size_t)m * intermediate * 4) + marlin_q4_lm_head_workspace_size(m);
+    return step_zero_bytes(m) + std::max(step_compose_bytes(m, hidden, intermediate),
+                                         stack_scratch_size(m, hidden, intermediate));
 }
 
 int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
@@ -293,25 +306,55 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     if (!aligned(h0, 16) || !aligned(final_norm, 16) || (h_out && !aligned(h_out, 16))) return MARLIN_Q4_ERR_ALIGN;
     if ((rc = check_tensor(lm))) return rc;
     if (lm->k != hidden) return MARLIN_Q4_ERR_SHAPE;
-    int64_t inter = 1;
+    int64_t inter = layers[0].gate_proj.n;
+    bool uniform = true;
     for (int32_t l = 0; l < n_layers; ++l) {
         const marlin_q4_layer& L = layers[l];
         if (!L.post_attn_norm) return MARLIN_Q4_ERR_ARG;
+        if (!aligned(L.post_attn_norm, 16)) return MARLIN_Q4_ERR_ALIGN;
         if ((rc = check_tensor(&L.gate_proj)) || (rc = check_tensor(&L.up_proj)) || (rc = check_tensor(&L.down_proj)))
             return rc;
         if (L.gate_proj.k != hidden || L.up_proj.k != hidden || L.up_proj.n != L.gate_proj.n ||
             L.down_proj.k != L.gate_proj.n || L.down_proj.n != hidden)
             return MARLIN_Q4_ERR_SHAPE;
+        uniform = uniform && L.gate_proj.n == inter;
         inter = std::max<int64_t>(inter, L.gate_proj.n);
     }
-    if (!workspace || !aligned(workspace, 16) ||
+    if (!workspace || !aligned(workspace, 256) ||
         workspace_bytes < marlin_q4_decode_step_workspace_size(m, hidden, inter))
         return MARLIN_Q4_ERR_WORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    float* h = reinterpret_cast<float*>(ws);
-    float* act = reinterpret_cast<float*>(ws + align16((size_t)m * hidden * 4));
-    void* lmws = ws + align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
+    uint8_t* scratch = ws + step_zero_bytes(m);
+    if (decode_path() == kPathOneKernel && uniform && stack_supported(m, hidden, inter, n_layers)) {
+        // the whole step as one persistent kernel
+        StackLayer sl[kStackMaxLayers];
+        for (int32_t l = 0; l < n_layers; ++l)
+            sl[l] = StackLayer{layers[l].post_attn_norm, view(&layers[l].gate_proj), view(&layers[l].up_proj),
+                               view(&layers[l].down_proj)};
+        const Q4Mat lmv = view(lm);
+        StackLaunch S{};
+        S.h0 = h0;
+        S.h0_dtype = MARLIN_Q4_BF16;
+        S.m = m;
+        S.hidden = hidden;
+        S.inter = inter;
+        S.n_layers = n_layers;
+        S.layers = sl;
+        S.final_norm = final_norm;
+        S.eps = eps;
+        S.lm = &lmv;
+        S.ids = ids;
+        S.best = best;
+        S.h_out = h_out;
+        S.bar = reinterpret_cast<unsigned*>(ws);
+        S.keys = reinterpret_cast<unsigned long long*>(ws + 256);
+        S.scratch = scratch;
+        return cuda_status(launch_stack(S, st));
+    }
+    void* lmws = ws + 256;  // keys + counter, zero-invariant
+    float* h = reinterpret_cast<float*>(scratch);
+    float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
     const void* cur = h0;
     int32_t cur_dtype = MARLIN_Q4_BF16;

@@ -769,18 +769,20 @@ uint32_t plan_unit(UnitArgs& a, int NT, int nmat, bool swz, int64_t M, bool norm
 
 int g_decode_path = kPathI8;
 
+int decode_path() { return g_decode_path; }
+
 bool set_decode_path(int path) {
-    if (path != kPathI8 && path != kPathTc && path != kPathBf16) return false;
+    if (path != kPathI8 && path != kPathTc && path != kPathBf16 && path != kPathOneKernel) return false;
     g_decode_path = path;
     return true;
 }
 
 int gemv_max_rows(int act_dtype, bool normed, int64_t k) {
-    if (g_decode_path == kPathI8 && i8_supported(k, 1)) return kI8MaxRows;
+    if (path_is_i8(g_decode_path) && i8_supported(k, 1)) return kI8MaxRows;
     return (normed || act_dtype == kF32) ? 10 : 32;
 }
 int lm_head_max_rows(int act_dtype, bool normed, int64_t k) {
-    if (g_decode_path == kPathI8 && i8_supported(k, 1)) return kI8MaxRows;
+    if (path_is_i8(g_decode_path) && i8_supported(k, 1)) return kI8MaxRows;
     const bool p3 = normed || act_dtype == kF32;
     if (g_decode_path == kPathTc && tc_supported(k, p3 ? 30 : 32)) return p3 ? 10 : 32;
     return p3 ? 5 : 16;
@@ -788,7 +790,7 @@ int lm_head_max_rows(int act_dtype, bool normed, int64_t k) {
 
 cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
     const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
-    if (g_decode_path == kPathI8 && i8_supported(L.w0.k, L.m)) return launch_i8_gemv(L, stream);
+    if (path_is_i8(g_decode_path) && i8_supported(L.w0.k, L.m)) return launch_i8_gemv(L, stream);
     if (g_decode_path == kPathTc && tc_supported(L.w0.k, m_eff) && tc_gemv_fits(L)) return launch_tc_gemv(L, stream);
     UnitArgs a{};
     a.L = L;
@@ -847,7 +849,7 @@ cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream) {
     const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
-    if (g_decode_path == kPathI8 && i8_supported(L.w.k, L.m)) return launch_i8_lm_head(L, stream);
+    if (path_is_i8(g_decode_path) && i8_supported(L.w.k, L.m)) return launch_i8_lm_head(L, stream);
     if (g_decode_path == kPathTc && tc_supported(L.w.k, m_eff) && tc_lm_head_fits(L)) return launch_tc_lm_head(L, stream);
     LmArgs a{};
     a.L = L;

@@ -42,9 +42,13 @@ struct GemvLaunch {
 };
 
 // Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default), tcgen05/TMEM, bf16
-// mma.sync.  Shapes a family does not cover use the bf16 mma.sync kernels.
-enum DecodePath : int { kPathI8 = 0, kPathTc = 1, kPathBf16 = 2 };
+// mma.sync, and integer MMAs with the decode step as one kernel.  Shapes a family does not cover use
+// the bf16 mma.sync kernels.
+enum DecodePath : int { kPathI8 = 0, kPathTc = 1, kPathBf16 = 2, kPathOneKernel = 3 };
 bool set_decode_path(int path);
+int decode_path();
+// True for the families whose GEMV / lm_head kernels are the integer-MMA ones.
+inline bool path_is_i8(int p) { return p == kPathI8 || p == kPathOneKernel; }
 
 // Activation rows per launch of the selected family for this shape (the C ABI loops over passes).
 int gemv_max_rows(int act_dtype, bool normed, int64_t k);

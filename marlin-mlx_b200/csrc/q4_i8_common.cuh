@@ -1,0 +1,258 @@
+// q4_i8_common.cuh — pieces of the integer-MMA Q4 decode path shared by its kernels: activation
+// staging into four exact s8 planes (with the fused RMSNorm) and the per-stage tensor-core step.
+// Staging is written for a "team" of threads (the whole block, or the consumer warps of a
+// warp-specialised kernel) that synchronises through team.sync().
+#pragma once
+
+#include "common.cuh"
+#include "q4_gemv.cuh"
+#include "q4_stage.cuh"
+
+namespace marlin {
+namespace {
+
+constexpr uint32_t kNib = 0x0F0F0F0Fu;
+
+// Every thread of the block.
+struct BlockTeam {
+    __device__ __forceinline__ int size() const { return blockDim.x; }
+    __device__ __forceinline__ int rank() const { return threadIdx.x; }
+    __device__ __forceinline__ void sync() { __syncthreads(); }
+};
+
+// RMSNorm factors r_m = 1/sqrt(mean + eps) from the per-unit sums t.ssq, in the fixed order of
+// finish_norm_factors (units lane-strided, then a shuffle tree).  Ends with team.sync().
+template <class Team>
+__device__ void norm_factors_team(Team& team, int dtype, int M, int K, float eps, float* rf, const float* ssq) {
+    const int lane = team.rank() & 31, warp = team.rank() >> 5, nw = team.size() >> 5;
+    const int upr = K / 8;
+    for (int m = warp; m < M; m += nw) {
+        float s = 0.f;
+        for (int u = lane; u < upr; u += 32) s = __fadd_rn(s, ssq[m * upr + u]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == 0) {
+            float var;
+            if (dtype == kBF16)
+                var = bf16_round(__fmul_rn(bf16_round(s), bf16_round((float)(1.0 / (double)K))));
+            else
+                var = __fmul_rn(s, (float)(1.0 / (double)K));
+            rf[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        }
+    }
+    team.sync();
+}
+
+// ------------------------------------------------------------------------------------------------
+// activation staging: four s8 planes per row, [group][column][64 B] with column = 4 m + p.
+// Within a group's 64 bytes, unit u (elements 8u..8u+7) occupies bytes 8u..8u+7 as
+// (x0, x2, x4, x6, x1, x3, x5, x7): the order the B fragment of mma.m16n8k32 needs when the A
+// fragment is (q0, q2, q4, q6 | q1, q3, q5, q7) of one packed word.
+// ------------------------------------------------------------------------------------------------
+struct I8X {
+    uint8_t* xq;          // [ng][ncols][64]
+    float* xs;            // [ng][ncols]: plane-0 columns hold sum_g(x) / c_m, the others 0
+    float* cs;            // [ncols]: c_m * 128^-p (0 for padding columns)
+    float* rf;            // [M] RMSNorm factors
+    float* ssq;           // [M * K/8] RMSNorm scratch
+    unsigned int* amax;   // [M] max |x| (binary32 bits) over the staged range
+};
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// exponent e with max|x| < 2^e (clamped so that every plane scale stays a normal binary32)
+__device__ __forceinline__ int row_exp(unsigned int abits) {
+    const int eb = (int)((abits >> 23) & 0xffu);
+    const int e = eb == 0 ? -125 : eb - 126;
+    return max(e, -90);
+}
+
+// Eight activations of row m from column k, RMSNorm'ed as marlin.cpp:12-16 when norm_w is set.
+__device__ __forceinline__ void load_norm8(const void* x, int dtype, int K, const uint16_t* norm_w, const float* rf,
+                                           int m, int k, float (&v)[8]) {
+    load8(x, dtype, (int64_t)m * K + k, v);
+    if (norm_w) {
+        const uint4 nwv = *reinterpret_cast<const uint4*>(norm_w + k);
+        const uint32_t w4[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+        const float r = rf[m];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float wj = bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+            v[j] = __fmul_rn(__fmul_rn(v[j], r), __fadd_rn(1.0f, wj));
+        }
+    }
+}
+
+// Max over the warp of `bits` for the lanes whose row is m0, and for row m1 when the warp's 32
+// consecutive units straddle two rows; one shared-memory atomic per row and warp.
+__device__ __forceinline__ void warp_row_max(unsigned int* amax, unsigned int bits, int m, int base, int total, int upr) {
+    const int m0 = base / upr, m1 = min(base + 31, total - 1) / upr;
+    const unsigned int r0 = __reduce_max_sync(0xffffffffu, m == m0 ? bits : 0u);
+    if ((threadIdx.x & 31) == 0) atomicMax(&amax[m0], r0);
+    if (m1 != m0) {
+        const unsigned int r1 = __reduce_max_sync(0xffffffffu, m == m1 ? bits : 0u);
+        if ((threadIdx.x & 31) == 0) atomicMax(&amax[m1], r1);
+    }
+}
+
+// The four s8 planes of eight activations with row exponent e (|x| < 2^e, up to rounding):
+// x = 2^(e-13) A + 2^(e-27) B with integers |A|, |B| <= 2^13 + 8 (both steps exact), then each of
+// A, B splits into two balanced base-128 digits: A = 128 i0 + i1, i1 in [-64, 63].  Bytes go out in
+// the B-fragment order (x0, x2, x4, x6 | x1, x3, x5, x7).
+__device__ __forceinline__ void planes8(const float (&v)[8], int e, uint32_t (&b)[4][2]) {
+    const float s1 = pow2f(13 - e), d1 = pow2f(e - 13), s2 = pow2f(27 - e);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) b[p][0] = b[p][1] = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float qa = rintf(__fmul_rn(v[j], s1));
+        const int A = (int)qa;
+        const int B = __float2int_rn(__fmul_rn(fmaf(-qa, d1, v[j]), s2));
+        const int i0 = (A + 64) >> 7, i2 = (B + 64) >> 7;
+        const int d[4] = {i0, A - (i0 << 7), i2, B - (i2 << 7)};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) b[p][j & 1] |= ((uint32_t)d[p] & 0xffu) << (8 * (j >> 1));
+    }
+}
+
+// RMSNorm of eight activations as marlin.cpp:12-16: (x * r) * (1 + w), binary32.
+__device__ __forceinline__ void norm8(float (&v)[8], uint4 nwv, float r) {
+    const uint32_t w4[4] = {nwv.x, nwv.y, nwv.z, nwv.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float wj = bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+        v[j] = __fmul_rn(__fmul_rn(v[j], r), __fadd_rn(1.0f, wj));
+    }
+}
+
+constexpr int kStageU = 2;  // 8-element activation units per thread and chunk, held in registers
+
+// Stage groups [g0, g0 + ng) of the M activation rows (ng % 4 == 0).  All threads of the block
+// call it; it ends with a barrier.  The rows are read in chunks of kStageU units per thread (whole
+// rows when RMSNorm applies, since its factor needs every column; else only the staged range).
+// With one chunk, x is read from global memory once and the norm sums, row maxima and planes come
+// from registers; larger inputs read each chunk twice.
+template <class Team>
+__device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, const uint16_t* norm_w, float eps, int g0,
+                                int ng, int M, int ncols, const I8X& t) {
+    const int nt = team.size(), tid = team.rank(), lane = tid & 31;
+    const bool normed = norm_w != nullptr;
+    const int upr_l = normed ? K / 8 : ng * 8;  // units per row read
+    const int kfirst = normed ? 0 : g0 * kGroup;
+    const int u0 = normed ? g0 * 8 : 0;         // first staged unit within a read row
+    const int total_l = M * upr_l, per_chunk = kStageU * nt;
+    const int nchunk = (total_l + per_chunk - 1) / per_chunk;
+    float v[kStageU][8];
+    uint4 nw[kStageU];
+    auto load_chunk = [&](int c) {
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int idx = c * per_chunk + u * nt + tid;
+            if (idx < total_l) {
+                const int k = kfirst + (idx % upr_l) * 8;
+                load8(x, dtype, (int64_t)(idx / upr_l) * K + k, v[u]);
+                if (normed) nw[u] = *reinterpret_cast<const uint4*>(norm_w + k);
+            }
+        }
+    };
+    load_chunk(0);
+    if (tid < M) t.amax[tid] = 0u;
+    for (int i = tid; i < ng * ncols; i += nt) t.xs[i] = 0.f;
+    const int pad = ncols - 4 * M;
+    for (int i = tid; i < ng * pad * 4; i += nt) {
+        const int gl = i / (pad * 4), rem = i % (pad * 4);
+        *reinterpret_cast<uint4*>(t.xq + ((size_t)gl * ncols + 4 * M + rem / 4) * 64 + (rem % 4) * 16) =
+            make_uint4(0, 0, 0, 0);
+    }
+    team.sync();
+    // norm sums per unit (reduced by finish_norm_factors in a fixed order) and raw row maxima:
+    // max |x (1 + w)| with RMSNorm (the positive factor r scales the maximum afterwards; the
+    // plane split only needs a bound within a factor of two), else max |x|
+#pragma unroll 1
+    for (int c = 0; c < nchunk; ++c) {
+        if (c > 0) load_chunk(c);
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int base = c * per_chunk + u * nt + tid - lane;  // warp-uniform
+            if (base < total_l) {
+                const int idx = base + lane;
+                unsigned int bits = 0u;
+                int m = -1;
+                if (idx < total_l) {
+                    m = idx / upr_l;
+                    float amx = 0.f;
+                    if (normed) {
+                        t.ssq[idx] = unit_ssq(v[u], dtype);
+                        const uint32_t w4[4] = {nw[u].x, nw[u].y, nw[u].z, nw[u].w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            amx = fmaxf(amx, fabsf(v[u][j] * (1.0f + bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu))));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) amx = fmaxf(amx, fabsf(v[u][j]));
+                    }
+                    bits = __float_as_uint(amx);
+                }
+                warp_row_max(t.amax, bits, m, base, total_l, upr_l);
+            }
+        }
+    }
+    team.sync();
+    if (normed) norm_factors_team(team, dtype, M, K, eps, t.rf, t.ssq);  // ends with a barrier
+    for (int c = tid; c < ncols; c += nt) {
+        const int m = c >> 2, p = c & 3;
+        float mx = 0.f;
+        if (m < M) mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
+        t.cs[c] = m < M ? pow2f(row_exp(__float_as_uint(mx)) - 6 - 7 * p) : 0.f;
+    }
+#pragma unroll 1
+    for (int c = 0; c < nchunk; ++c) {
+        if (nchunk > 1) load_chunk(c);
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int base = c * per_chunk + u * nt + tid - lane;  // warp-uniform
+            if (base < total_l) {
+                const int idx = base + lane;
+                const int m = idx < total_l ? idx / upr_l : 0, ul = idx < total_l ? idx % upr_l - u0 : -1;
+                const bool ok = idx < total_l && ul >= 0 && ul < ng * 8;
+                float s = 0.f, inv0 = 0.f;
+                if (ok) {
+                    if (normed) norm8(v[u], nw[u], t.rf[m]);
+                    const float mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
+                    const int e = row_exp(__float_as_uint(mx));
+                    inv0 = pow2f(6 - e);
+                    uint32_t b[4][2];
+                    planes8(v[u], e, b);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[u][j]);
+                    const int gl = ul >> 3, u8 = ul & 7;
+#pragma unroll
+                    for (int p = 0; p < 4; ++p)
+                        *reinterpret_cast<uint2*>(t.xq + ((size_t)gl * ncols + 4 * m + p) * 64 + u8 * 8) =
+                            make_uint2(b[p][0], b[p][1]);
+                }
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s += __shfl_xor_sync(0xffffffffu, s, 4);
+                if (ok && (lane & 7) == 0) t.xs[(ul >> 3) * ncols + 4 * m] = __fmul_rn(s, inv0);
+            }
+        }
+    }
+    team.sync();
+}
+
+// Whole-block staging (the GEMV family and the lm_head kernel).
+__device__ __forceinline__ void stage_x_i8(const void* x, int dtype, int K, const uint16_t* norm_w, float eps, int g0,
+                                           int ng, int M, int ncols, const I8X& t) {
+    BlockTeam team;
+    stage_x_i8_team(team, x, dtype, K, norm_w, eps, g0, ng, M, ncols, t);
+}
+
+// bf16 value q (0..3) of four packed in a uint2, as binary32.
+__device__ __forceinline__ float sel_bf16(uint2 v, int q) {
+    const uint32_t w = q < 2 ? v.x : v.y;
+    return __uint_as_float((q & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+
+}  // namespace
+}  // namespace marlin

@@ -254,9 +254,11 @@ def set_pdl(enable: bool) -> None:
     _lib.load().marlin_q4_set_pdl(1 if enable else 0)
 
 
-DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "tcgen05": _lib.PATH_TCGEN05, "bf16": _lib.PATH_BF16MMA}
+DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "tcgen05": _lib.PATH_TCGEN05, "bf16": _lib.PATH_BF16MMA,
+                "onekernel": _lib.PATH_ONEKERNEL}
 
 
 def set_decode_path(path: str) -> None:
-    """Select the decode kernel family: "i8" (integer MMAs, default), "tcgen05" or "bf16" (mma.sync)."""
+    """Select the decode kernel family: "i8" (integer MMAs, default), "tcgen05", "bf16" (mma.sync) or
+    "onekernel" (integer MMAs; marlin_q4_decode_step as one persistent kernel)."""
     check(_lib.load().marlin_q4_set_decode_path(DECODE_PATHS[path]), "marlin_q4_set_decode_path")

@@ -1,5 +1,8 @@
 """GPU parity: the full Q4 decode stack (config 5) — 24 x [RMSNorm(1+w) -> Q4 MLP -> residual] ->
-final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights."""
+final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
+
+Both forms of the step are checked: the per-kernel composition (default) and the one persistent
+cooperative kernel ("onekernel" family, m <= 8, grid barriers between phases)."""
 import numpy as np
 import pytest
 import torch
@@ -27,8 +30,15 @@ def model():
     return layers, host_layers, lm, host_q4(lm), fn, u16(fn)
 
 
-@pytest.mark.parametrize("m", [1, 3, 12])
-def test_decode_step_matches_oracle(oracle, model, m):
+@pytest.fixture(params=["i8", "onekernel"])
+def family(request):
+    mq.set_decode_path(request.param)
+    yield request.param
+    mq.set_decode_path("i8")
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 12, 16])
+def test_decode_step_matches_oracle(oracle, model, family, m):
     layers, hl, lm, hlm, fn, hfn = model
     step = mq.DecodeStep(layers, fn, lm, m)
     h0 = mq.synth_bf16((m, H), 3000 + m, 0.0, 1.0)
@@ -60,3 +70,36 @@ def test_decode_step_in_cuda_graph(model):
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(step.ids, ids_eager)
+
+
+@pytest.mark.parametrize("m", [1, 5])
+def test_one_kernel_step_matches_composition(model, m):
+    """The one-kernel step against the per-kernel composition (tcgen05 family)."""
+    layers, _, lm, _, fn, _ = model
+    h0 = mq.synth_bf16((m, H), 3200 + m, 0.0, 1.0)
+    mq.set_decode_path("onekernel")
+    try:
+        ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, m)(h0))
+    finally:
+        mq.set_decode_path("i8")
+    mq.set_decode_path("tcgen05")
+    try:
+        ids_c, _, h_c = mq.DecodeStep(layers, fn, lm, m)(h0)
+        torch.cuda.synchronize()
+    finally:
+        mq.set_decode_path("i8")
+    assert max_rel_row_err(f32(h), f32(h_c).astype(np.float64)) < 1e-4
+    assert torch.equal(ids, ids_c)
+    assert mq.device_error() == 0
+
+
+@pytest.mark.parametrize("nl", [1, 2])
+def test_short_stacks(oracle, model, family, nl):
+    layers, hl, lm, hlm, fn, hfn = model
+    step = mq.DecodeStep(layers[:nl], fn, lm, 2)
+    h0 = mq.synth_bf16((2, H), 3300 + nl, 0.0, 1.0)
+    ids, _, h = step(h0)
+    torch.cuda.synchronize()
+    rids, _, rh = oracle.decode_step(u16(h0), hl[:nl], hfn, hlm)
+    assert max_rel_row_err(f32(h), rh) < 1e-4
+    assert np.array_equal(ids.cpu().numpy(), rids)
