@@ -79,8 +79,8 @@ void marlin_q4_set_pdl(int enable);
  *   MARLIN_Q4_PATH_TCGEN05 5th-generation tensor cores: bf16 codes in TMEM, tcgen05.mma
  *                          (k % 512 == 0, m * planes <= 32);
  *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0);
- *   MARLIN_Q4_PATH_ONEKERNEL the integer-MMA kernels, and marlin_q4_decode_step as one persistent
- *                          cooperative kernel (m <= 8, at most 24 equal layers).
+ *   MARLIN_Q4_PATH_ONEKERNEL the integer-MMA kernels, and the layers of marlin_q4_decode_step as one
+ *                          persistent cooperative kernel (m <= 4, at most 24 equal layers).
  * Shapes a family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns MARLIN_Q4_ERR_ARG
  * for an unknown path. */
 #define MARLIN_Q4_PATH_I8MMA 0
@@ -178,9 +178,10 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
  * (src/sampling/sampler.cpp:15).  h0: bf16 [m, hidden] embedding rows.  ids [m]; best [m]
  * (optional); h_out: binary32 [m, hidden] hidden state before the final norm (optional).
  * n_layers >= 1.
- * Runs as two kernels per layer plus the lm_head; with MARLIN_Q4_PATH_ONEKERNEL (m <= 8, k a
- * multiple of 512, at most 24 layers of equal shape) as one persistent cooperative kernel (all SMs,
- * software grid barriers between the gate/up and down phases of each layer).
+ * Runs as two kernels per layer plus the lm_head; with MARLIN_Q4_PATH_ONEKERNEL (m <= 4, hidden a
+ * multiple of 512, intermediate of 1024, at most 24 layers of equal shape) the layers run as one
+ * persistent cooperative kernel (all SMs, software grid barriers between the gate/up and down
+ * phases of each layer) before the lm_head kernel.
  * workspace: >= marlin_q4_decode_step_workspace_size bytes, 256-byte aligned, zero-filled before
  * the first call (its head is left zeroed by every call). */
 int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,

@@ -326,13 +326,13 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     uint8_t* scratch = ws + step_zero_bytes(m);
+    void* lmws = ws + 256;  // keys + counter, zero-invariant
     if (decode_path() == kPathOneKernel && uniform && stack_supported(m, hidden, inter, n_layers)) {
-        // the whole step as one persistent kernel
+        // all layers as one persistent kernel, then the fused lm_head + argmax
         StackLayer sl[kStackMaxLayers];
         for (int32_t l = 0; l < n_layers; ++l)
             sl[l] = StackLayer{layers[l].post_attn_norm, view(&layers[l].gate_proj), view(&layers[l].up_proj),
                                view(&layers[l].down_proj)};
-        const Q4Mat lmv = view(lm);
         StackLaunch S{};
         S.h0 = h0;
         S.h0_dtype = MARLIN_Q4_BF16;
@@ -341,18 +341,14 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
         S.inter = inter;
         S.n_layers = n_layers;
         S.layers = sl;
-        S.final_norm = final_norm;
         S.eps = eps;
-        S.lm = &lmv;
-        S.ids = ids;
-        S.best = best;
         S.h_out = h_out;
         S.bar = reinterpret_cast<unsigned*>(ws);
-        S.keys = reinterpret_cast<unsigned long long*>(ws + 256);
         S.scratch = scratch;
-        return cuda_status(launch_stack(S, st));
+        if ((rc = cuda_status(launch_stack(S, st)))) return rc;
+        return marlin_q4_lm_head_argmax(stack_output(S), MARLIN_Q4_F32, m, final_norm, eps, lm, 0, ids, best, nullptr,
+                                        lmws, marlin_q4_lm_head_workspace_size(m), st);
     }
-    void* lmws = ws + 256;  // keys + counter, zero-invariant
     float* h = reinterpret_cast<float*>(scratch);
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;

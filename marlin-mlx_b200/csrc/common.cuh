@@ -45,6 +45,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared-memory base rounded up to a 1024-byte shared address (TMA swizzle atoms and
+// UMMA descriptors need it).  Formed as the shared array plus an offset, never through an integer
+// cast, so the pointer stays in the shared state space and accesses through it compile to
+// shared-memory instructions rather than generic ones.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* base) {
+    return base + ((1024u - (smem_u32(base) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -84,15 +92,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Wait bound in SM clock cycles: about 2 s at 2 GHz (longer at lower clocks).  The cycle counter
+// is cheap to read; the global timer is not, so it stays off the wait paths.
+constexpr unsigned long long kWaitCycles = 4000000000ull;
+__device__ __forceinline__ unsigned long long cycles_now() { return (unsigned long long)clock64(); }
+
 // Bounded wait on an mbarrier phase.  try_wait suspends the thread for a hardware-defined time
-// while the phase is pending; the loop gives up after 2 s of wall time (global timer) or 2^28
-// polls, records kDevErrMbarTimeout and returns false.  Returns true when the phase completed.
+// while the phase is pending; the loop gives up after kWaitCycles or 2^28 polls, records
+// kDevErrMbarTimeout and returns false.  Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const unsigned long long t0 = cycles_now();
     for (uint32_t it = 1; it < (1u << 28); ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && globaltimer_ns() - t0 > 2000000000ull) break;
+        if ((it & 255u) == 0 && cycles_now() - t0 > kWaitCycles) break;
     }
     record_device_error(kDevErrMbarTimeout);
     return false;
@@ -289,7 +302,8 @@ __device__ __forceinline__ void hold_regs(const float (&v)[N]) {
 // Bounded wait that also ends early once another role has aborted (timeout recorded on device).
 // Every lane acquires the barrier; the exit is warp-uniform.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const uint64_t t0 = globaltimer_ns();
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
+    const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0;; ++it) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
         if ((it & 63u) == 63u) {
@@ -297,7 +311,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
             if ((threadIdx.x & 31) == 0) {
                 if (*abort) {
                     stop = 1;
-                } else if (globaltimer_ns() - t0 > 2000000000ull || it > (1u << 28)) {
+                } else if (cycles_now() - t0 > kWaitCycles || it > (1u << 28)) {
                     record_device_error(kDevErrMbarTimeout);
                     *abort = 1;
                     stop = 1;
@@ -309,12 +323,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 }
 // Single-thread bounded wait (producer / MMA issuer).
 __device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const uint64_t t0 = globaltimer_ns();
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0; it < (1u << 28); ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 63u) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > 2000000000ull) {
+            if (cycles_now() - t0 > kWaitCycles) {
                 record_device_error(kDevErrMbarTimeout);
                 *abort = 1;
                 return false;
@@ -328,10 +343,11 @@ __device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, vola
 // Bounded wait used on the exit path only (ignores the abort flag): returns when the phase is
 // complete or after ~2 s.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-    const uint64_t t0 = globaltimer_ns();
+    if (mbar_try_wait(bar, parity)) return;
+    const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0; it < (1u << 26); ++it) {
         if (mbar_try_wait(bar, parity)) return;
-        if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+        if ((it & 63u) == 63u && cycles_now() - t0 > kWaitCycles) {
             record_device_error(kDevErrMbarTimeout);
             return;
         }

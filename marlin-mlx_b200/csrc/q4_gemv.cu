@@ -237,7 +237,7 @@ __device__ __forceinline__ float swiglu_apply(float gv, float uv, int dtype) {
 template <int NT, int MT, bool HALF, int EPI, bool SWZ>
 __global__ void __launch_bounds__(256, 2) q4_unit_kernel(const __grid_constant__ UnitArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, wk = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
     const int NWK = a.NWK, G = a.G;
@@ -453,7 +453,7 @@ __device__ __forceinline__ void lm_issue(const LmArgs& a, int64_t blk, uint8_t* 
 template <int MT, bool HALF>
 __global__ void __launch_bounds__(kLmThreads, 1) q4_lm_head_kernel(const __grid_constant__ LmArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const LmHeadLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
     const int G = a.G, S = a.S;

@@ -110,7 +110,7 @@ struct I8UnitArgs {
 template <int NTN>
 __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_constant__ I8UnitArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     constexpr int MS = 2 * NTN;  // activation rows per pass
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -284,7 +284,7 @@ __device__ __forceinline__ unsigned long long i8_logit_key(float v, int64_t idx)
 template <int NTN>
 __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_constant__ I8LmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const LmHeadLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G, S = a.S, M = (int)L.m, ncols = a.ncols;

@@ -113,7 +113,7 @@ template <int MH>
 __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_constant__ PrefillArgs a) {
     using P = PPlan<MH>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G, epi = L.epi;

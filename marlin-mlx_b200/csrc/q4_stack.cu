@@ -1,27 +1,27 @@
-// q4_stack.cu — the whole Q4 decode step as one persistent cooperative kernel (sm_100a).
+// q4_stack.cu — the decode step's layer stack as one persistent cooperative kernel (sm_100a).
 //
 // Replaces, for decode-sized batches, the per-layer sequence of marlin-mlx's text model restricted
 // to its Q4 sublayers (src/model/marlin.cpp:103-146: h += mlp(rms_norm(h)) with mlp_forward
-// :31-35), the final norm (:145), the Q4 lm_head (:161-169) and the greedy argmax
-// (src/sampling/sampler.cpp:14-16): one launch per token instead of 2 x layers + 1 dependent
-// kernels (each dependent kernel boundary costs about 3 us on B200).
+// :31-35): one launch for all layers instead of two dependent kernels per layer (each dependent
+// kernel boundary costs about 3 us on B200).  The final norm, lm_head and argmax follow as the
+// fused lm_head kernel.
 //
 // All CTAs are resident (cooperative launch, one per SM).  Per layer:
-//   phase A  work item = 16 features: the 16 gate rows and 16 up rows over K = hidden, SwiGLU in the
-//            epilogue, binary32 act written to global memory;
-//   phase B  work item = 32 rows of down_proj x 16 groups of K: a binary32 partial of h written to
-//            part[chunk] (deterministic: no atomics);
-// separated by software grid barriers among the consumer warps.  The next phase's staging forms
-// h = h_prev + sum over chunks of part (fixed order), RMSNorms it and splits it into the exact s8
-// planes of the integer-MMA path (see q4_i8.cu).  After the last layer the lm_head phase streams
-// 32-row vocabulary items and keeps packed argmax keys.
+//   phase A  work item = 16 features: the 16 gate rows and 16 up rows over K = hidden.  Each CTA
+//            stages RMSNorm(h) once as the exact s8 planes of the integer-MMA path (q4_i8.cu),
+//            accumulates all of its items in registers, then reduces once and writes
+//            act = SwiGLU(gate, up) (binary32) plus a per-row max |act| (atomicMax on the bits);
+//   phase B  work item = 16 rows of down_proj over all of K = intermediate: each consumer warp
+//            stages its own K slice of act against the global row maximum (no block barrier),
+//            the eight K slices meet in shared memory in a fixed order, and the residual add
+//            writes those 16 rows of the next h (deterministic, no partial sums in memory);
+// separated by software grid barriers among the consumer warps (a monotonic arrival counter).
 //
-// Warp roles: warps 0-7 consume (warp w: 16-row tile w & 1 of the item, 64-groups 2(w >> 1) and
-// 2(w >> 1) + 1 of each 8-group stage; partial sums meet in shared memory at the end of the item);
-// warp 8 is the TMA producer, which walks the same schedule across items, phases and layers, so
-// the next phase's weights stream while the consumers wait at a grid barrier.
+// Warp roles: warps 0-7 consume; warp 8 is the TMA producer, which walks the same schedule across
+// items, phases and layers, so the next phase's weights stream while the consumers wait at a grid
+// barrier or stage activations.
 //
-// Every wait is bounded: a grid barrier or mbarrier that does not complete within 2 s records a
+// Every wait is bounded: a grid barrier or mbarrier that does not complete within ~2 s records a
 // device error and raises an abort flag that every CTA checks, so all CTAs leave.
 #include "common.cuh"
 #include "q4_gemv.cuh"
@@ -31,32 +31,48 @@
 
 #include <algorithm>
 
+// Optional instrumentation hooks, empty in the library build: STACK_MARK(layer, point) by consumer
+// thread 0 of every CTA; STACK_ISSUE(n) by the producer when it issues ring stage n of this CTA's
+// schedule, STACK_READY(n) by consumer thread 0 when that stage has landed.
+#ifndef STACK_MARK
+#define STACK_MARK(l, k)
+#endif
+#ifndef STACK_ISSUE
+#define STACK_ISSUE(n)
+#endif
+#ifndef STACK_READY
+#define STACK_READY(n)
+#endif
+
 namespace marlin {
 namespace {
 
-constexpr int kSRows = 32;                         // weight rows per work item (two 16-row tiles)
-constexpr int kSGroups = 8;                        // 64-groups per ring stage
-constexpr uint32_t kSLine = kSRows * 128;          // one 4-group line box of 32 rows: 4 KB
-constexpr uint32_t kSPacked = 2 * kSLine;          // 8 KB of packed words per stage
-constexpr uint32_t kSSb = kSRows * 16;             // scales or biases: 8 groups x 32 rows
-constexpr uint32_t kSStage = kSPacked + 2 * kSSb;  // 9 KB
-constexpr int kSCons = 8;                          // consumer warps
+constexpr uint32_t kSPacked = 8192;                  // packed words per ring stage
+constexpr uint32_t kSStage = kSPacked + 1024;        // + scales and biases: 9 KB
+constexpr int kSCons = 8;                            // consumer warps
 constexpr int kSThreads = (kSCons + 1) * 32;
-constexpr int kSBGroups = 16;                      // K groups per down-projection item
+constexpr int kSAGroups = 8;                         // phase A stage: 32 rows (16 gate + 16 up) x 8 groups
+constexpr int kSBGroups = 16;                        // phase B stage: 16 rows x 16 groups
+constexpr int kSAItems = 4;                          // phase A items per CTA at most
 constexpr uint32_t kSSmemLimit = 225 * 1024;
+constexpr int kSMinStages = 6;
+
+// Words of the zero-invariant control block (StackLaunch::bar).
+constexpr int kBarArrive = 0, kBarAbort = 1, kBarDone = 2, kBarAmax = 4;  // amax: [2][kStackMaxRows]
 
 // Bounded barrier among `n` warps built on an mbarrier (arrival count n): every lane of the warp
-// waits for the phase; after 2 s (or once the CTA has aborted) it gives up, records `100 + where`
+// waits for the phase; after kWaitCycles (or once the CTA has aborted) it gives up, records `100 + where`
 // and raises the CTA's abort flag, so no consumer can block forever.  `ph` is this warp's phase bit.
 __device__ __forceinline__ void warp_group_bar(uint64_t* bar, uint32_t& ph, volatile int* abort, int where) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-    const uint64_t t0 = globaltimer_ns();
+    unsigned long long t0 = 0;
     for (uint32_t it = 0;; ++it) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, ph) ? 1 : 0)) break;
+        if (it == 0) t0 = cycles_now();
         if ((it & 63u) == 63u) {
             int stop = 0;
-            if ((threadIdx.x & 31) == 0 && (*abort || globaltimer_ns() - t0 > 2000000000ull)) {
+            if ((threadIdx.x & 31) == 0 && (*abort || cycles_now() - t0 > kWaitCycles)) {
                 if (!*abort) record_device_error(100 + where);
                 *abort = 1;
                 stop = 1;
@@ -78,81 +94,77 @@ struct ConsumerTeam {
     __device__ __forceinline__ void sync() { warp_group_bar(bar, ph, abort, where); }
 };
 
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Software grid barrier among the consumer warps of every CTA (all CTAs are co-resident by the
+// cooperative launch): the team barrier orders this CTA's writes before thread 0's release-add on
+// a counter that only grows during a call; thread 0 polls until the counter reaches `target`
+// (= CTAs x barriers passed), then an acquire fence and the team barrier make every CTA's writes
+// visible to the whole team.  Returns false once any CTA has aborted.
+__device__ bool grid_sync(ConsumerTeam& team, unsigned* bar, unsigned target) {
+    team.where = 1;
+    team.sync();
+    if (threadIdx.x == 0 && !*team.abort) {
+        red_release_gpu_add(bar + kBarArrive, 1u);
+        const volatile unsigned* gabort = bar + kBarAbort;
+        const unsigned long long t0 = cycles_now();
+        for (uint32_t it = 0;; ++it) {
+            if (ld_relaxed_gpu(bar + kBarArrive) >= target) break;
+            if ((it & 15u) == 15u) {
+                if (*gabort) {
+                    *team.abort = 1;
+                    break;
+                }
+                if (cycles_now() - t0 > kWaitCycles) {
+                    record_device_error(kDevErrMbarTimeout);
+                    atomicExch(bar + kBarAbort, 1u);
+                    *team.abort = 1;
+                    break;
+                }
+            }
+        }
+        fence_acq_rel_gpu();
+    }
+    team.where = 2;
+    team.sync();
+    return !*team.abort;
+}
+
 struct StackLayerMaps {
-    CUtensorMap g, gs, gb, u, us, ub, d, ds, db;
+    CUtensorMap g, gs, gb, u, us, ub, d, ds, db;  // every box is 16 rows high
 };
 
 struct StackArgs {
     StackLayerMaps layer[kStackMaxLayers];
-    CUtensorMap lw, ls, lb;
     const uint16_t* norm_w[kStackMaxLayers];
     const void* h0;
     int h0_dtype;
-    const uint16_t* final_norm;
     float eps;
-    int nl, M, H, I, GA, bchunks, ncols, S;
-    int items_a, items_b, items_l;
-    int64_t V;
-    float* hbuf;  // [2][M][H] residual stream (binary32)
-    float* act;   // [M][I]
-    float* part;  // [bchunks][M][H] down-projection partials
-    unsigned* bar;  // [0] arrivals, [1] generation, [2] abort, [3] CTAs finished
-    unsigned long long* keys;  // [M] argmax keys (zero on entry, left zero)
-    int32_t* ids;
-    float* best;
-    float* h_out;  // optional [M][H]: h before the final norm
-    uint32_t off_bar, off_misc, off_ckeys, off_scr, off_xs, off_cs, off_xq, off_h, off_red, off_ring;
+    int nl, M, H, I, GA, nsb, ncols, S, items_a, items_b;
+    float* hbuf;    // [2][M][H] residual stream between layers (binary32)
+    float* h_last;  // [M][H] the last layer's output
+    float* act;     // [M][I]
+    unsigned* bar;  // control block (zero on entry, left zero)
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring;
 };
 
-__device__ __forceinline__ unsigned long long stack_key(float v, int64_t idx) {
-    const uint32_t u = __float_as_uint(v);
-    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)o << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
-}
-
-// Software grid barrier among the consumer warps of every CTA (all CTAs are co-resident by the
-// cooperative launch).  The last arriver resets the arrival count and advances the generation.
-// Returns false once any CTA has aborted (timeout anywhere).
-__device__ bool grid_sync(ConsumerTeam& team, unsigned* bar, volatile int* abort) {
-    team.where = 1;
-    team.sync();
-    if (threadIdx.x == 0 && !*abort) {
-        volatile unsigned* gen = bar + 1;
-        volatile unsigned* gabort = bar + 2;
-        const unsigned g = *gen;
-        __threadfence();
-        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
-            const uint64_t t0 = globaltimer_ns();
-            while (*gen == g) {
-                if (*gabort) {
-                    *abort = 1;
-                    break;
-                }
-                if (globaltimer_ns() - t0 > 2000000000ull) {
-                    record_device_error(kDevErrMbarTimeout);
-                    atomicExch(bar + 2, 1u);
-                    *abort = 1;
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
-        __threadfence();
-    }
-    team.where = 2;
-    team.sync();
-    return !*abort;
-}
-
-// One 8-group stage of a 32-row item for consumer warp (tile t, groups 2kp, 2kp+1): the same
+// Phase A, one 8-group stage, consumer warp (tile t = gate/up, groups 2kp and 2kp + 1): the same
 // tensor-core step as the decode GEMV (codes x s8 planes, exact int32, binary32 fold).
+// Stage layout: line c (groups 4c..4c+3) at c * 4 KB, gate rows 0-15 then up rows 16-31, 128 B
+// per row with 128-byte swizzle; scales [32 rows][8] at 8 KB, biases [32 rows][8] at 8.5 KB.
 template <int NTN>
-__device__ __forceinline__ void stack_stage(const uint8_t* st, int gl0, const I8X& t, int ncols, int tile, int kp,
-                                            int lane, float (&y)[NTN][4]) {
+__device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const I8X& t, int ncols, int tile, int kp,
+                                              int lane, float (&y)[NTN][4]) {
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * tile + g, r1 = r0 + 8;
 #pragma unroll
@@ -160,12 +172,12 @@ __device__ __forceinline__ void stack_stage(const uint8_t* st, int gl0, const I8
         const int q = 2 * kp + qq;
         const int c = q >> 2, gq = q & 3;
         const uint32_t off = (uint32_t)((((2 * gq + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
-        const uint2 wa = *reinterpret_cast<const uint2*>(st + c * kSLine + r0 * 128 + off);
-        const uint2 wb = *reinterpret_cast<const uint2*>(st + c * kSLine + r1 * 128 + off);
+        const uint2 wa = *reinterpret_cast<const uint2*>(st + c * 4096 + r0 * 128 + off);
+        const uint2 wb = *reinterpret_cast<const uint2*>(st + c * 4096 + r1 * 128 + off);
         const float sr0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + r0 * 16 + 2 * q));
         const float sr1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + r1 * 16 + 2 * q));
-        const float br0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + kSSb + r0 * 16 + 2 * q));
-        const float br1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + kSSb + r1 * 16 + 2 * q));
+        const float br0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + r0 * 16 + 2 * q));
+        const float br1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + r1 * 16 + 2 * q));
         const uint32_t a0[4] = {wa.x & kNib, wb.x & kNib, (wa.x >> 4) & kNib, (wb.x >> 4) & kNib};
         const uint32_t a1[4] = {wa.y & kNib, wb.y & kNib, (wa.y >> 4) & kNib, (wb.y >> 4) & kNib};
         const int gl = gl0 + q;
@@ -184,29 +196,124 @@ __device__ __forceinline__ void stack_stage(const uint8_t* st, int gl0, const I8
     }
 }
 
+// Phase B, one 16-group stage, consumer warp w (groups 2w and 2w + 1 of the stage = its local
+// groups 2s, 2s + 1).  Stage layout: line c (groups 4c..4c+3) at c * 2 KB, 16 rows x 128 B,
+// 128-byte swizzle; scales [2 boxes][16 rows][8] at 8 KB, biases likewise at 8.5 KB.
+template <int NTN>
+__device__ __forceinline__ void stack_stage_b(const uint8_t* st, int s, const uint8_t* xqw, const float* xsw,
+                                              int ncols, int warp, int lane, float (&y)[NTN][4]) {
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const int q = 2 * warp + e;
+        const int c = q >> 2, gq = q & 3;
+        const uint32_t off = (uint32_t)((((2 * gq + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
+        const uint2 wa = *reinterpret_cast<const uint2*>(st + c * 2048 + g * 128 + off);
+        const uint2 wb = *reinterpret_cast<const uint2*>(st + c * 2048 + (g + 8) * 128 + off);
+        const uint32_t so = (uint32_t)((q >> 3) * 256 + 2 * (q & 7));
+        const float sr0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + so + g * 16));
+        const float sr1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + so + (g + 8) * 16));
+        const float br0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + so + g * 16));
+        const float br1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + so + (g + 8) * 16));
+        const uint32_t a0[4] = {wa.x & kNib, wb.x & kNib, (wa.x >> 4) & kNib, (wb.x >> 4) & kNib};
+        const uint32_t a1[4] = {wa.y & kNib, wb.y & kNib, (wa.y >> 4) & kNib, (wb.y >> 4) & kNib};
+        const int lg = 2 * s + e;
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xqw + ((size_t)(lg * ncols + 8 * j + g) * 64 + 16 * tq));
+            int cc[4] = {0, 0, 0, 0}, ee[4] = {0, 0, 0, 0};
+            mma_s8_16832(cc, a0, xv.x, xv.y);
+            mma_s8_16832(ee, a1, xv.z, xv.w);
+            const float2 xs = *reinterpret_cast<const float2*>(xsw + lg * ncols + 8 * j + 2 * tq);
+            y[j][0] = fmaf(sr0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
+            y[j][1] = fmaf(sr0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
+            y[j][2] = fmaf(sr1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
+            y[j][3] = fmaf(sr1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
+        }
+    }
+}
+
+// Phase B staging by one warp: its 2 * nsb local groups (local group lg = K group
+// 16 (lg >> 1) + 2 warp + (lg & 1)) of the M act rows as s8 planes against row exponents e[m]
+// from the global maxima, with the plane-0 sums / c_m.  Same byte layout as stage_x_i8_team.
+__device__ __forceinline__ void stage_b_warp(const float* act, int I, int M, int ncols, int nsb, int warp, int lane,
+                                             const int (&e)[kStackMaxRows], uint8_t* xqw, float* xsw) {
+    const int nlg = 2 * nsb;
+    for (int i = lane; i < nlg * ncols; i += 32) xsw[i] = 0.f;
+    const int pad = ncols - 4 * M;
+    for (int i = lane; i < nlg * pad * 4; i += 32) {
+        const int lg = i / (pad * 4), rem = i % (pad * 4);
+        *reinterpret_cast<uint4*>(xqw + ((size_t)lg * ncols + 4 * M + rem / 4) * 64 + (rem % 4) * 16) =
+            make_uint4(0, 0, 0, 0);
+    }
+    __syncwarp();
+    constexpr int kU = 4;           // units per lane loaded together
+    const int total = nlg * M * 8;  // a multiple of 32 (nlg is even, 8 units per group)
+#pragma unroll 1
+    for (int base = 0; base < total; base += 32 * kU) {
+        float v[kU][8];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int idx = base + 32 * u + lane;
+            if (idx < total) {
+                const int un = idx & 7, rest = idx >> 3, lg = rest % nlg, m = rest / nlg;
+                const int gk = 16 * (lg >> 1) + 2 * warp + (lg & 1);
+                const float* p = act + (size_t)m * I + 64 * gk + 8 * un;
+                const float4 x0 = *reinterpret_cast<const float4*>(p);
+                const float4 x1 = *reinterpret_cast<const float4*>(p + 4);
+                v[u][0] = x0.x; v[u][1] = x0.y; v[u][2] = x0.z; v[u][3] = x0.w;
+                v[u][4] = x1.x; v[u][5] = x1.y; v[u][6] = x1.z; v[u][7] = x1.w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int idx = base + 32 * u + lane;
+            if (base + 32 * u < total) {  // warp-uniform
+                const int un = idx & 7, rest = idx >> 3, lg = rest % nlg, m = rest / nlg;
+                int em = e[0];
+#pragma unroll
+                for (int r = 1; r < kStackMaxRows; ++r) em = m == r ? e[r] : em;
+                uint32_t b[4][2];
+                planes8(v[u], em, b);
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+                    *reinterpret_cast<uint2*>(xqw + ((size_t)lg * ncols + 4 * m + p) * 64 + un * 8) =
+                        make_uint2(b[p][0], b[p][1]);
+                float s = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[u][j]);
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s += __shfl_xor_sync(0xffffffffu, s, 4);
+                if (un == 0) xsw[lg * ncols + 4 * m] = __fmul_rn(s, pow2f(6 - em));
+            }
+        }
+    }
+    __syncwarp();
+}
+
 template <int NTN>
 __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_constant__ StackArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     constexpr int MS = 2 * NTN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = a.M, S = a.S, ncols = a.ncols, H = a.H, I = a.I, nb = (int)gridDim.x, cta = (int)blockIdx.x;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
     uint64_t* empty = full + S;
     volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
-    uint64_t* team_bars = reinterpret_cast<uint64_t*>(smem + a.off_misc + 16);  // [0] 8 consumers, [1] warps 0-1
-    unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(smem + a.off_ckeys);  // [2][MS]
-    float* hs = reinterpret_cast<float*>(smem + a.off_h);    // [M][H]
-    float* red = reinterpret_cast<float*>(smem + a.off_red);  // [4][32][ncols], then [16][MS] exchange
+    uint64_t* team_bar = reinterpret_cast<uint64_t*>(smem + a.off_misc + 16);
+    float* red = reinterpret_cast<float*>(smem + a.off_red);
     uint8_t* ring = smem + a.off_ring;
     I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
            reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
            reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
-    const int spa = a.GA / kSGroups;         // stages per phase-A and lm_head item
-    const int spb = kSBGroups / kSGroups;    // stages per phase-B item
+    const int spa = a.GA / kSAGroups;  // stages per phase-A item
+    const int nsb = a.nsb;             // stages per phase-B item
     const int na = a.items_a > cta ? (a.items_a - 1 - cta) / nb + 1 : 0;
-    const int nbi = a.items_b > cta ? (a.items_b - 1 - cta) / nb + 1 : 0;
-    const int nli = a.items_l > cta ? (a.items_l - 1 - cta) / nb + 1 : 0;
+    const bool has_b = cta < a.items_b;
+    unsigned* gbar = a.bar;
+    unsigned* amax_g = a.bar + kBarAmax;
 
     if (tid == 0) {
         *abort = 0;
@@ -214,8 +321,7 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kSCons);
         }
-        mbar_init(&team_bars[0], kSCons);
-        mbar_init(&team_bars[1], 2);
+        mbar_init(team_bar, kSCons);
         fence_mbar_init();
     }
     __syncthreads();
@@ -230,6 +336,7 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
                     ok = false;
                     return nullptr;
                 }
+                STACK_ISSUE(issued);
                 mbar_arrive_expect_tx(&full[slot], kSStage);
                 return ring + (size_t)slot * kSStage;
             };
@@ -242,48 +349,41 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
             };
             for (int l = 0; l < a.nl && ok; ++l) {
                 const StackLayerMaps& mp = a.layer[l];
+                if (l == 0) {
+                    prefetch_tmap(&mp.g);
+                    prefetch_tmap(&mp.u);
+                    prefetch_tmap(&mp.d);
+                }
                 for (int i = 0; i < na && ok; ++i) {
                     const int f0 = 16 * (cta + i * nb);
                     for (int s = 0; s < spa && ok; ++s) {
                         uint8_t* st = acquire();
                         if (!st) break;
-                        const int gs = kSGroups * s;
+                        const int gs = kSAGroups * s;
                         for (int c = 0; c < 2; ++c) {
-                            tma_load_2d(st + c * kSLine, &mp.g, (gs + 4 * c) * 8, f0, &full[slot]);
-                            tma_load_2d(st + c * kSLine + kSLine / 2, &mp.u, (gs + 4 * c) * 8, f0, &full[slot]);
+                            tma_load_2d(st + c * 4096, &mp.g, (gs + 4 * c) * 8, f0, &full[slot]);
+                            tma_load_2d(st + c * 4096 + 2048, &mp.u, (gs + 4 * c) * 8, f0, &full[slot]);
                         }
                         tma_load_2d(st + kSPacked, &mp.gs, gs, f0, &full[slot]);
-                        tma_load_2d(st + kSPacked + kSSb / 2, &mp.us, gs, f0, &full[slot]);
-                        tma_load_2d(st + kSPacked + kSSb, &mp.gb, gs, f0, &full[slot]);
-                        tma_load_2d(st + kSPacked + kSSb + kSSb / 2, &mp.ub, gs, f0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 256, &mp.us, gs, f0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 512, &mp.gb, gs, f0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 768, &mp.ub, gs, f0, &full[slot]);
                         advance();
                     }
                 }
-                for (int i = 0; i < nbi && ok; ++i) {
-                    const int item = cta + i * nb, rb = item / a.bchunks, ch = item % a.bchunks;
-                    for (int s = 0; s < spb && ok; ++s) {
+                if (has_b) {
+                    const int r0 = 16 * cta;
+                    for (int s = 0; s < nsb && ok; ++s) {
                         uint8_t* st = acquire();
                         if (!st) break;
-                        const int gs = kSBGroups * ch + kSGroups * s;
-                        for (int c = 0; c < 2; ++c)
-                            tma_load_2d(st + c * kSLine, &mp.d, (gs + 4 * c) * 8, kSRows * rb, &full[slot]);
-                        tma_load_2d(st + kSPacked, &mp.ds, gs, kSRows * rb, &full[slot]);
-                        tma_load_2d(st + kSPacked + kSSb, &mp.db, gs, kSRows * rb, &full[slot]);
+                        const int gs = kSBGroups * s;
+                        for (int c = 0; c < 4; ++c) tma_load_2d(st + c * 2048, &mp.d, (gs + 4 * c) * 8, r0, &full[slot]);
+                        tma_load_2d(st + kSPacked, &mp.ds, gs, r0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 256, &mp.ds, gs + 8, r0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 512, &mp.db, gs, r0, &full[slot]);
+                        tma_load_2d(st + kSPacked + 768, &mp.db, gs + 8, r0, &full[slot]);
                         advance();
                     }
-                }
-            }
-            for (int i = 0; i < nli && ok; ++i) {
-                const int item = cta + i * nb;
-                for (int s = 0; s < spa && ok; ++s) {
-                    uint8_t* st = acquire();
-                    if (!st) break;
-                    const int gs = kSGroups * s;
-                    for (int c = 0; c < 2; ++c)
-                        tma_load_2d(st + c * kSLine, &a.lw, (gs + 4 * c) * 8, kSRows * item, &full[slot]);
-                    tma_load_2d(st + kSPacked, &a.ls, gs, kSRows * item, &full[slot]);
-                    tma_load_2d(st + kSPacked + kSSb, &a.lb, gs, kSRows * item, &full[slot]);
-                    advance();
                 }
             }
             // exit only once every copy this thread started has landed
@@ -293,287 +393,188 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
         // ---------------------------------------------------------------- consumers (warps 0-7)
         const int tile = warp & 1, kp = warp >> 1;
         const int g = lane >> 2, tq = lane & 3;
-        ConsumerTeam team{&team_bars[0], abort};
-        uint32_t ph2 = 0;  // phase of the warps 0-1 exchange barrier
-        int slot = 0, round = 0;
+        ConsumerTeam team{team_bar, abort};
+        int slot = 0, round = 0, consumed = 0;
+        unsigned nbar = 0;
         bool ok = true;
-        unsigned long long best[NTN];
-#pragma unroll
-        for (int j = 0; j < NTN; ++j) best[j] = 0ull;
+        auto wait_stage = [&]() -> const uint8_t* {
+            if (ok && !warp_wait(&full[slot], (uint32_t)(round & 1), abort)) ok = false;
+            STACK_READY(consumed);
+            return ok ? ring + (size_t)slot * kSStage : nullptr;
+        };
+        auto release_stage = [&]() {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            ++consumed;
+            if (++slot == S) {
+                slot = 0;
+                ++round;
+            }
+        };
 
-        // h = prev + sum of the down partials (fixed chunk order) into shared memory
-        auto build_h = [&](const void* prev, int prev_dtype, float* hw) {
-            const int n = M * H;
-            for (int e = tid * 4; e < n; e += 256 * 4) {
-                float4 v;
-                if (prev_dtype == kBF16) {
-                    const uint2 p = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(prev) + e);
-                    v = make_float4(bf16_bits_to_f32(p.x & 0xffffu), bf16_bits_to_f32(p.x >> 16),
-                                    bf16_bits_to_f32(p.y & 0xffffu), bf16_bits_to_f32(p.y >> 16));
-                } else {
-                    v = *reinterpret_cast<const float4*>(static_cast<const float*>(prev) + e);
+        for (int l = 0; l < a.nl; ++l) {
+            const void* hin = l == 0 ? a.h0 : a.hbuf + (size_t)((l - 1) & 1) * M * H;
+            const int hin_dtype = l == 0 ? a.h0_dtype : kF32;
+            float* hout = l == a.nl - 1 ? a.h_last : a.hbuf + (size_t)(l & 1) * M * H;
+            STACK_MARK(l, 0);
+            // the other amax slot was last read in phase B of layer l - 1 (before the barrier that
+            // ended it) and is next written in phase A of layer l + 1
+            if (cta == 0 && tid < M && l > 0) amax_g[((l - 1) & 1) * kStackMaxRows + tid] = 0u;
+
+            // ---- phase A: x = RMSNorm(h) as s8 planes, then all of this CTA's 16-feature items
+            stage_x_i8_team(team, hin, hin_dtype, H, a.norm_w[l], a.eps, 0, a.GA, M, ncols, tx);
+            STACK_MARK(l, 1);
+            float y[kSAItems][NTN][4];
+#pragma unroll
+            for (int i = 0; i < kSAItems; ++i)
+#pragma unroll
+                for (int j = 0; j < NTN; ++j) y[i][j][0] = y[i][j][1] = y[i][j][2] = y[i][j][3] = 0.f;
+#pragma unroll
+            for (int i = 0; i < kSAItems; ++i) {
+                if (i < na) {
+                    for (int s = 0; s < spa; ++s) {
+                        const uint8_t* st = wait_stage();
+                        if (st) stack_stage_a<NTN>(st, kSAGroups * s, tx, ncols, tile, kp, lane, y[i]);
+#pragma unroll
+                        for (int j = 0; j < NTN; ++j) hold_regs(y[i][j]);  // consumed before release
+                        release_stage();
+                    }
                 }
-                for (int c = 0; c < a.bchunks; ++c) {
-                    const float4 p = *reinterpret_cast<const float4*>(a.part + (size_t)c * n + e);
-                    v.x += p.x;
-                    v.y += p.y;
-                    v.z += p.z;
-                    v.w += p.w;
+            }
+            STACK_MARK(l, 2);
+            // planes -> one value per (K part, item, row, activation row)
+#pragma unroll
+            for (int i = 0; i < kSAItems; ++i) {
+                if (i < na) {
+#pragma unroll
+                    for (int j = 0; j < NTN; ++j) {
+                        const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
+                        float p0 = fmaf(cv.x, y[i][j][0], cv.y * y[i][j][1]);
+                        float p1 = fmaf(cv.x, y[i][j][2], cv.y * y[i][j][3]);
+                        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+                        p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+                        const int m = 2 * j + (tq >> 1);
+                        if ((tq & 1) == 0 && m < M) {
+                            float* r = red + ((size_t)(kp * kSAItems + i) * 32 + 16 * tile + g) * MS + m;
+                            r[0] = p0;
+                            r[8 * MS] = p1;
+                        }
+                    }
                 }
-                *reinterpret_cast<float4*>(hs + e) = v;
-                if (hw) *reinterpret_cast<float4*>(hw + e) = v;
             }
             team.where = 3;
             team.sync();
-        };
-        // consume one item of nst stages starting at K group gl0 of the staged activations
-        auto run_item = [&](int nst, int gl0, float (&y)[NTN][4]) {
+            {
+                // SwiGLU per (item, feature, activation row), the 4 K parts summed in a fixed order
+                const int per = 16 * M;
+                unsigned bits = 0u;
+                int mm = -1;
+                if (tid < na * per) {
+                    const int i = tid / per, f = (tid / M) % 16, m = tid % M;
+                    float gsum = 0.f, usum = 0.f;
 #pragma unroll
-            for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
-            for (int s = 0; s < nst; ++s) {
-                if (ok && !warp_wait(&full[slot], (uint32_t)(round & 1), abort)) ok = false;
-                if (ok) stack_stage<NTN>(ring + (size_t)slot * kSStage, gl0 + kSGroups * s, tx, ncols, tile, kp, lane, y);
-#pragma unroll
-                for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-                if (++slot == S) {
-                    slot = 0;
-                    ++round;
+                    for (int k = 0; k < 4; ++k) {
+                        gsum += red[((size_t)(k * kSAItems + i) * 32 + f) * MS + m];
+                        usum += red[((size_t)(k * kSAItems + i) * 32 + 16 + f) * MS + m];
+                    }
+                    const float v = ((1.0f / (1.0f + expf(-gsum))) * gsum) * usum;
+                    a.act[(size_t)m * I + 16 * (cta + i * nb) + f] = v;
+                    bits = __float_as_uint(fabsf(v));
+                    mm = m;
+                }
+                for (int m = 0; m < M; ++m) {
+                    const unsigned r = __reduce_max_sync(0xffffffffu, mm == m ? bits : 0u);
+                    if (lane == 0 && r) atomicMax(&amax_g[(l & 1) * kStackMaxRows + m], r);
                 }
             }
-        };
-        // partial sums of the 4 K-parts -> per (item row, activation row) outputs for warps 0-1:
-        // returns, for lanes with (tq & 1) == 0, Y for rows 16*tile + g (ya) and + 8 (yb) and
-        // activation row m = 2j + (tq >> 1)
-        auto reduce_item = [&](const float (&y)[NTN][4], float (&ya)[NTN], float (&yb)[NTN]) {
+            STACK_MARK(l, 3);
+            if (!grid_sync(team, gbar, (++nbar) * (unsigned)nb)) ok = false;
+            STACK_MARK(l, 4);
+
+            // ---- phase B: 16 rows of down_proj over all of K, + residual
+            if (has_b) {
+                int e[kStackMaxRows];
 #pragma unroll
-            for (int j = 0; j < NTN; ++j) {
-                const int col = 8 * j + 2 * tq;
-                float* r0 = red + ((size_t)(kp * kSRows + 16 * tile + g) * ncols + col);
-                float* r1 = r0 + 8 * ncols;
-                r0[0] = y[j][0];
-                r0[1] = y[j][1];
-                r1[0] = y[j][2];
-                r1[1] = y[j][3];
-            }
-            team.where = 4;
-            team.sync();
-            if (warp < 2) {
+                for (int m = 0; m < kStackMaxRows; ++m)
+                    e[m] = m < M ? row_exp(*reinterpret_cast<volatile unsigned*>(&amax_g[(l & 1) * kStackMaxRows + m]))
+                                 : 0;
+                uint8_t* xqw = tx.xq + (size_t)warp * (2 * nsb) * ncols * 64;
+                float* xsw = tx.xs + (size_t)warp * (2 * nsb) * ncols;
+                stage_b_warp(a.act, I, M, ncols, nsb, warp, lane, e, xqw, xsw);
+                STACK_MARK(l, 5);
+                float yb[NTN][4];
+#pragma unroll
+                for (int j = 0; j < NTN; ++j) yb[j][0] = yb[j][1] = yb[j][2] = yb[j][3] = 0.f;
+                for (int s = 0; s < nsb; ++s) {
+                    const uint8_t* st = wait_stage();
+                    if (st) stack_stage_b<NTN>(st, s, xqw, xsw, ncols, warp, lane, yb);
+#pragma unroll
+                    for (int j = 0; j < NTN; ++j) hold_regs(yb[j]);
+                    release_stage();
+                }
+                STACK_MARK(l, 6);
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
-                    const int col = 8 * j + 2 * tq;
-                    float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-                    for (int k = 0; k < 4; ++k) {
-                        const float* r0 = red + ((size_t)(k * kSRows + 16 * tile + g) * ncols + col);
-                        const float* r1 = r0 + 8 * ncols;
-                        t0 += r0[0];
-                        t1 += r0[1];
-                        t2 += r1[0];
-                        t3 += r1[1];
-                    }
-                    const float2 cv = *reinterpret_cast<const float2*>(tx.cs + col);
-                    float pa = fmaf(cv.x, t0, cv.y * t1), pb = fmaf(cv.x, t2, cv.y * t3);
-                    pa += __shfl_xor_sync(0xffffffffu, pa, 1);
-                    pb += __shfl_xor_sync(0xffffffffu, pb, 1);
-                    ya[j] = pa;
-                    yb[j] = pb;
-                }
-            }
-            team.where = 5;
-            team.sync();  // red is free again
-        };
-
-        const void* prev = a.h0;
-        int prev_dtype = a.h0_dtype;
-        for (int l = 0; l < a.nl; ++l) {
-            // ---- phase A staging: x = RMSNorm(h) split into s8 planes (all GA groups)
-            if (l == 0) {
-                stage_x_i8_team(team, a.h0, a.h0_dtype, H, a.norm_w[0], a.eps, 0, a.GA, M, ncols, tx);
-            } else {
-                float* hw = a.hbuf + (size_t)(l & 1) * M * H;
-                build_h(prev, prev_dtype, cta == 0 ? hw : nullptr);
-                stage_x_i8_team(team, hs, kF32, H, a.norm_w[l], a.eps, 0, a.GA, M, ncols, tx);
-                prev = hw;
-                prev_dtype = kF32;
-            }
-            for (int i = 0; i < na; ++i) {
-                float y[NTN][4], ya[NTN], yb[NTN];
-                run_item(spa, 0, y);
-                reduce_item(y, ya, yb);
-                // SwiGLU of the 16 features: tile 0 rows are gate, tile 1 rows are up
-                const int f0 = 16 * (cta + i * nb);
-                if (warp == 1 && (tq & 1) == 0) {
+                    const int m = 2 * j + (tq >> 1);
+                    int em = e[0];
 #pragma unroll
-                    for (int j = 0; j < NTN; ++j) {
-                        const int m = 2 * j + (tq >> 1);
-                        if (m < MS) {
-                            red[g * MS + m] = ya[j];
-                            red[(g + 8) * MS + m] = yb[j];
-                        }
+                    for (int r = 1; r < kStackMaxRows; ++r) em = m == r ? e[r] : em;
+                    const int p = 2 * (tq & 1);
+                    const float cx = m < M ? pow2f(em - 6 - 7 * p) : 0.f;
+                    const float cy = m < M ? pow2f(em - 13 - 7 * p) : 0.f;
+                    float p0 = fmaf(cx, yb[j][0], cy * yb[j][1]);
+                    float p1 = fmaf(cx, yb[j][2], cy * yb[j][3]);
+                    p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+                    p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+                    if ((tq & 1) == 0 && m < M) {
+                        red[((size_t)warp * 16 + g) * MS + m] = p0;
+                        red[((size_t)warp * 16 + g + 8) * MS + m] = p1;
                     }
                 }
-                if (warp < 2) warp_group_bar(&team_bars[1], ph2, abort, 6);
-                if (warp == 0 && (tq & 1) == 0) {
+                team.where = 4;
+                team.sync();
+                if (tid < 16 * M) {
+                    const int m = tid / 16, r = tid % 16;
+                    float v = 0.f;
 #pragma unroll
-                    for (int j = 0; j < NTN; ++j) {
-                        const int m = 2 * j + (tq >> 1);
-                        if (m < M) {
-                            const float ga = ya[j], gb = yb[j];
-                            const float ua = red[g * MS + m], ub = red[(g + 8) * MS + m];
-                            a.act[(size_t)m * I + f0 + g] = ((1.0f / (1.0f + expf(-ga))) * ga) * ua;
-                            a.act[(size_t)m * I + f0 + g + 8] = ((1.0f / (1.0f + expf(-gb))) * gb) * ub;
-                        }
-                    }
-                }
-                if (warp < 2) warp_group_bar(&team_bars[1], ph2, abort, 7);
-            }
-            if (!grid_sync(team, a.bar, abort)) ok = false;
-            // ---- phase B: down-projection partials, K chunk by chunk
-            for (int i = 0; i < nbi; ++i) {
-                const int item = cta + i * nb, rb = item / a.bchunks, ch = item % a.bchunks;
-                stage_x_i8_team(team, a.act, kF32, I, nullptr, 0.f, kSBGroups * ch, kSBGroups, M, ncols, tx);
-                float y[NTN][4], ya[NTN], yb[NTN];
-                run_item(spb, 0, y);
-                reduce_item(y, ya, yb);
-                if (warp < 2 && (tq & 1) == 0) {
-                    const int row = kSRows * rb + 16 * tile + g;
-#pragma unroll
-                    for (int j = 0; j < NTN; ++j) {
-                        const int m = 2 * j + (tq >> 1);
-                        if (m < M) {
-                            float* pc = a.part + ((size_t)ch * M + m) * H;
-                            pc[row] = ya[j];
-                            pc[row + 8] = yb[j];
-                        }
-                    }
+                    for (int w = 0; w < kSCons; ++w) v += red[((size_t)w * 16 + r) * MS + m];
+                    const size_t o = (size_t)m * H + 16 * cta + r;
+                    const float hv = hin_dtype == kBF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(hin)[o])
+                                                         : static_cast<const float*>(hin)[o];
+                    hout[o] = hv + v;
                 }
             }
-            if (!grid_sync(team, a.bar, abort)) ok = false;
-        }
-        // ---- final h, and the lm_head + argmax phase
-        build_h(prev, prev_dtype, (cta == 0 && a.h_out) ? a.h_out : nullptr);
-        if (a.items_l > 0) {
-            stage_x_i8_team(team, hs, kF32, H, a.final_norm, a.eps, 0, a.GA, M, ncols, tx);
-            for (int i = 0; i < nli; ++i) {
-                const int item = cta + i * nb;
-                float y[NTN][4], ya[NTN], yb[NTN];
-                run_item(spa, 0, y);
-                reduce_item(y, ya, yb);
-                if (warp < 2) {
-                    const int64_t rowa = (int64_t)kSRows * item + 16 * tile + g, rowb = rowa + 8;
-#pragma unroll
-                    for (int j = 0; j < NTN; ++j) {
-                        const int m = 2 * j + (tq >> 1);
-                        unsigned long long ka = (m < M && rowa < a.V) ? stack_key(ya[j], rowa) : 0ull;
-                        const unsigned long long kb = (m < M && rowb < a.V) ? stack_key(yb[j], rowb) : 0ull;
-                        ka = kb > ka ? kb : ka;
-#pragma unroll
-                        for (int o = 4; o < 32; o <<= 1) {
-                            const unsigned long long other = __shfl_xor_sync(0xffffffffu, ka, o);
-                            ka = other > ka ? other : ka;
-                        }
-                        best[j] = ka > best[j] ? ka : best[j];
-                    }
-                }
-            }
-            if (warp < 2 && g == 0 && (tq & 1) == 0) {
-#pragma unroll
-                for (int j = 0; j < NTN; ++j) ckeys[warp * MS + 2 * j + (tq >> 1)] = best[j];
-            }
+            STACK_MARK(l, 7);
+            if (l < a.nl - 1 && !grid_sync(team, gbar, (++nbar) * (unsigned)nb)) ok = false;
         }
         (void)ok;
     }
     __syncthreads();
     __shared__ bool is_last;
-    if (a.items_l > 0 && tid < M) {
-        const unsigned long long k = ckeys[tid] > ckeys[MS + tid] ? ckeys[tid] : ckeys[MS + tid];
-        if (k) atomicMax(&a.keys[tid], k);
-    }
     __threadfence();
+    if (tid == 0) is_last = atomicAdd(gbar + kBarDone, 1u) == gridDim.x - 1;
     __syncthreads();
-    if (tid == 0) {
-        const unsigned int prevc = atomicAdd(a.bar + 3, 1u);
-        is_last = (prevc == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (is_last) {
+    if (is_last && tid == 0) {
         __threadfence();
-        if (a.items_l > 0 && tid < M) {
-            const unsigned long long k = atomicExch(&a.keys[tid], 0ull);
-            const uint32_t o = (uint32_t)(k >> 32);
-            const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
-            if (a.ids) a.ids[tid] = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
-            if (a.best) a.best[tid] = __uint_as_float(u);
-        }
-        if (tid == 0) {
-            atomicExch(a.bar + 3, 0u);
-            atomicExch(a.bar + 2, 0u);  // a timed-out call does not poison the next one
-        }
+        // the control block returns to zero for the next call (a timed-out call does not poison it)
+        atomicExch(gbar + kBarArrive, 0u);
+        atomicExch(gbar + kBarAbort, 0u);
+        for (int r = 0; r < 2 * kStackMaxRows; ++r) atomicExch(amax_g + r, 0u);
+        atomicExch(gbar + kBarDone, 0u);
     }
 }
 
-bool encode_rows(const Q4Mat& W, int rows, CUtensorMap* tw, CUtensorMap* ts, CUtensorMap* tb) {
-    return encode_q4_maps(W, rows, tw, ts, tb);
-}
+// Shared-memory plan of one launch; false when it does not fit.
+struct StackPlan {
+    int ntn, ncols, S;
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring, smem;
+};
 
-}  // namespace
-
-size_t stack_scratch_size(int64_t m, int64_t hidden, int64_t inter) {
-    const int64_t bchunks = inter / 64 / kSBGroups;
-    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
-    return al((size_t)2 * m * hidden * 4) + al((size_t)m * inter * 4) + al((size_t)bchunks * m * hidden * 4);
-}
-
-bool stack_supported(int64_t m, int64_t hidden, int64_t inter, int n_layers) {
-    return m >= 1 && m <= kStackMaxRows && n_layers >= 1 && n_layers <= kStackMaxLayers && hidden % 512 == 0 &&
-           hidden <= 8192 && inter % (64 * kSBGroups) == 0 && inter % 512 == 0 && inter % 16 == 0 &&
-           tmap_encode_fn() != nullptr;
-}
-
-cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream) {
-    StackArgs a{};
-    const int M = (int)L.m, H = (int)L.hidden, I = (int)L.inter;
-    const int ntn = M <= 2 ? 1 : (M <= 4 ? 2 : 4);
-    a.nl = L.n_layers;
-    a.M = M;
-    a.H = H;
-    a.I = I;
-    a.GA = H / 64;
-    a.bchunks = I / 64 / kSBGroups;
-    a.ncols = 8 * ntn;
-    a.items_a = I / 16;
-    a.items_b = (H / kSRows) * a.bchunks;
-    a.items_l = L.lm ? (int)((L.lm->n + kSRows - 1) / kSRows) : 0;
-    a.V = L.lm ? L.lm->n : 0;
-    a.h0 = L.h0;
-    a.h0_dtype = L.h0_dtype;
-    a.final_norm = L.final_norm;
-    a.eps = L.eps;
-    for (int l = 0; l < a.nl; ++l) {
-        const StackLayer& s = L.layers[l];
-        a.norm_w[l] = s.norm;
-        StackLayerMaps& mp = a.layer[l];
-        if (!encode_rows(s.gate, 16, &mp.g, &mp.gs, &mp.gb) || !encode_rows(s.up, 16, &mp.u, &mp.us, &mp.ub) ||
-            !encode_rows(s.down, kSRows, &mp.d, &mp.ds, &mp.db))
-            return cudaErrorInvalidValue;
-    }
-    if (L.lm && !encode_rows(*L.lm, kSRows, &a.lw, &a.ls, &a.lb)) return cudaErrorInvalidValue;
-    // scratch
-    uint8_t* ws = static_cast<uint8_t*>(L.scratch);
-    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
-    a.hbuf = reinterpret_cast<float*>(ws);
-    ws += al((size_t)2 * M * H * 4);
-    a.act = reinterpret_cast<float*>(ws);
-    ws += al((size_t)M * I * 4);
-    a.part = reinterpret_cast<float*>(ws);
-    a.bar = L.bar;
-    a.keys = L.keys;
-    a.ids = L.ids;
-    a.best = L.best;
-    a.h_out = L.h_out;
-    // shared memory
-    const int MS = 2 * ntn;
+bool stack_plan(int64_t m, int64_t hidden, int64_t inter, StackPlan& p) {
+    p.ntn = m <= 2 ? 1 : 2;
+    p.ncols = 8 * p.ntn;
+    const int MS = 2 * p.ntn;
+    const uint32_t GA = (uint32_t)(hidden / 64), nlg = (uint32_t)(2 * (inter / 64 / kSBGroups));
     uint32_t off = 0;
     auto take = [&](uint32_t bytes, uint32_t align) {
         off = (off + align - 1) / align * align;
@@ -581,35 +582,91 @@ cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream) {
         off += bytes;
         return o;
     };
-    const uint32_t bars_bytes = 2 * 32 * 8;  // up to 32 stages
-    a.off_bar = take(bars_bytes, 8);
-    a.off_misc = take(128, 16);
-    a.off_ckeys = take(2 * MS * 8, 16);
-    a.off_scr = take((64 + (uint32_t)M * (H / 8)) * 4, 16);
-    a.off_xs = take((uint32_t)a.GA * a.ncols * 4 * 2, 16);  // phase A / lm_head stage all of K; B stages 16 groups
-    a.off_cs = take(a.ncols * 4, 16);
-    a.off_xq = take((uint32_t)std::max(a.GA, kSBGroups) * a.ncols * 64, 128);
-    a.off_h = take((uint32_t)M * H * 4, 16);
-    a.off_red = take((uint32_t)4 * kSRows * a.ncols * 4 + 16 * MS * 4, 16);
+    p.off_bar = take(2 * 32 * 8, 8);  // up to 32 stages
+    p.off_misc = take(128, 16);
+    p.off_scr = take((64 + (uint32_t)m * (uint32_t)(hidden / 8)) * 4, 16);
+    p.off_cs = take(p.ncols * 4, 16);
+    p.off_xs = take(std::max(GA, kSCons * nlg) * p.ncols * 4, 16);
+    p.off_xq = take(std::max(GA, kSCons * nlg) * p.ncols * 64, 128);
+    p.off_red = take(std::max<uint32_t>(4 * kSAItems * 32, kSCons * 16) * MS * 4, 16);
     off = (off + 1023) / 1024 * 1024;
-    a.off_ring = off;
+    p.off_ring = off;
     const uint32_t avail = kSSmemLimit > off + 1024 ? kSSmemLimit - off - 1024 : 0;
-    a.S = std::min<int>(32, (int)(avail / kSStage));
-    if (a.S < 4) return cudaErrorInvalidConfiguration;
-    const uint32_t smem = off + (uint32_t)a.S * kSStage + 1024;
+    p.S = std::min<int>(32, (int)(avail / kSStage));
+    p.smem = off + (uint32_t)p.S * kSStage + 1024;
+    return p.S >= kSMinStages;
+}
+
+}  // namespace
+
+size_t stack_scratch_size(int64_t m, int64_t hidden, int64_t inter) {
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    return al((size_t)3 * m * hidden * 4) + al((size_t)m * inter * 4);
+}
+
+bool stack_supported(int64_t m, int64_t hidden, int64_t inter, int n_layers) {
+    if (!(m >= 1 && m <= kStackMaxRows && n_layers >= 1 && n_layers <= kStackMaxLayers && hidden % 512 == 0 &&
+          inter % (64 * kSBGroups) == 0 && tmap_encode_fn() != nullptr))
+        return false;
+    const int sms = device_num_sms();
+    if (hidden / 16 > sms || inter / 16 > (int64_t)kSAItems * sms) return false;
+    StackPlan p;
+    return stack_plan(m, hidden, inter, p);
+}
+
+cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream) {
+    if (!stack_supported(L.m, L.hidden, L.inter, L.n_layers)) return cudaErrorInvalidValue;
+    StackPlan p;
+    stack_plan(L.m, L.hidden, L.inter, p);
+    StackArgs a{};
+    const int M = (int)L.m, H = (int)L.hidden, I = (int)L.inter;
+    a.nl = L.n_layers;
+    a.M = M;
+    a.H = H;
+    a.I = I;
+    a.GA = H / 64;
+    a.nsb = I / 64 / kSBGroups;
+    a.ncols = p.ncols;
+    a.S = p.S;
+    a.items_a = I / 16;
+    a.items_b = H / 16;
+    a.h0 = L.h0;
+    a.h0_dtype = L.h0_dtype;
+    a.eps = L.eps;
+    for (int l = 0; l < a.nl; ++l) {
+        const StackLayer& s = L.layers[l];
+        a.norm_w[l] = s.norm;
+        StackLayerMaps& mp = a.layer[l];
+        if (!encode_q4_maps(s.gate, 16, &mp.g, &mp.gs, &mp.gb) || !encode_q4_maps(s.up, 16, &mp.u, &mp.us, &mp.ub) ||
+            !encode_q4_maps(s.down, 16, &mp.d, &mp.ds, &mp.db))
+            return cudaErrorInvalidValue;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(L.scratch);
+    a.hbuf = reinterpret_cast<float*>(ws);
+    a.act = reinterpret_cast<float*>(ws + (size_t)3 * M * H * 4);
+    a.h_last = stack_output(L);
+    a.bar = L.bar;
+    a.off_bar = p.off_bar;
+    a.off_misc = p.off_misc;
+    a.off_scr = p.off_scr;
+    a.off_xs = p.off_xs;
+    a.off_cs = p.off_cs;
+    a.off_xq = p.off_xq;
+    a.off_red = p.off_red;
+    a.off_ring = p.off_ring;
     const int grid = device_num_sms();
 
     auto go = [&](auto kernel) -> cudaError_t {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
         if (e != cudaSuccess) return e;
         int per_sm = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSThreads, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSThreads, p.smem);
         if (e != cudaSuccess) return e;
         if (per_sm < 1) return cudaErrorInvalidConfiguration;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kSThreads);
-        cfg.dynamicSmemBytes = smem;
+        cfg.dynamicSmemBytes = p.smem;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeCooperative;
@@ -618,11 +675,7 @@ cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream) {
         cfg.numAttrs = 1;
         return cudaLaunchKernelEx(&cfg, kernel, a);
     };
-    switch (ntn) {
-        case 1: return go(q4_stack_kernel<1>);
-        case 2: return go(q4_stack_kernel<2>);
-        default: return go(q4_stack_kernel<4>);
-    }
+    return p.ntn == 1 ? go(q4_stack_kernel<1>) : go(q4_stack_kernel<2>);
 }
 
 int stack_device_error(bool clear) { return tu_device_error(clear); }

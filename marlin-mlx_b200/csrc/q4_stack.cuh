@@ -1,4 +1,4 @@
-// q4_stack.cuh — launcher of the one-kernel Q4 decode step (persistent, cooperative).
+// q4_stack.cuh — launcher of the one-kernel Q4 layer stack of the decode step (persistent, cooperative).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -10,7 +10,7 @@
 namespace marlin {
 
 constexpr int kStackMaxLayers = 24;  // tensor maps travel as kernel parameters (<= 32 KB)
-constexpr int kStackMaxRows = 8;  // activation planes and the row buffer share shared memory with the ring
+constexpr int kStackMaxRows = 4;  // activation planes share shared memory with the ring
 
 struct StackLayer {
     const uint16_t* norm;  // post-attention RMSNorm weight (1 + w), bf16 [hidden]
@@ -23,20 +23,19 @@ struct StackLaunch {
     int64_t m, hidden, inter;
     int n_layers;
     const StackLayer* layers;
-    const uint16_t* final_norm;
     float eps;
-    const Q4Mat* lm;  // null: no lm_head phase (h_out receives the result)
-    int32_t* ids;
-    float* best;
-    float* h_out;     // optional [m, hidden] binary32: h before the final norm
-    unsigned* bar;    // 4 words, zero before the first launch (left zero)
-    unsigned long long* keys;  // [m], zero before the first launch (left zero)
+    float* h_out;     // optional [m, hidden] binary32 for the last layer's output (else in scratch)
+    unsigned* bar;    // control block of 64 words, zero before the first launch (left zero)
     void* scratch;    // >= stack_scratch_size bytes, 256-byte aligned (no initial contents needed)
 };
 
 bool stack_supported(int64_t m, int64_t hidden, int64_t inter, int n_layers);
 size_t stack_scratch_size(int64_t m, int64_t hidden, int64_t inter);
 cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream);
+// Where the last layer's output lands: h_out, or inside the scratch.
+inline float* stack_output(const StackLaunch& L) {
+    return L.h_out ? L.h_out : reinterpret_cast<float*>(L.scratch) + 2 * L.m * L.hidden;
+}
 int stack_device_error(bool clear);
 
 }  // namespace marlin

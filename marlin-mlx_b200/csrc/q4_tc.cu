@@ -267,7 +267,7 @@ template <class C>
 __global__ void __launch_bounds__(kLmThreads, 1) tc_lm_head_kernel(const __grid_constant__ TcLmArgs a) {
     using B = LmBuf<C>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const LmHeadLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G, S = a.S, M = (int)L.m;
@@ -500,7 +500,7 @@ struct TcUnitArgs {
 template <class C, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_unit_kernel(const __grid_constant__ TcUnitArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = (int)L.m, G = a.G, CL = a.CL;
