@@ -44,16 +44,17 @@ constexpr uint32_t kI8TwoPerSm = 110 * 1024;          // two CTAs per SM (PDL ov
 
 // ------------------------------------------------------------------------------------------------
 // one stage (4 groups) of one warp's 16 rows: y[j][0..1] row g, y[j][2..3] row g+8, columns
-// 8j + 2t + {0, 1} (lane = 4g + t)
+// 8j + 2t + {0, 1} (lane = 4g + t).  A stage of ROWS rows holds the packed lines [ROWS][128 B],
+// then the scales [ROWS][8 groups] and the biases [ROWS][8 groups].
 // ------------------------------------------------------------------------------------------------
-template <int NTN>
+template <int NTN, int ROWS = kI8Rows>
 __device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int ncols, int warp,
                                          int lane, float (&y)[NTN][4]) {
     // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * warp + g, r1 = r0 + 8;
-    const uint8_t* sc = st + kI8Packed;
-    const uint8_t* bi = sc + kI8Sb;
+    const uint8_t* sc = st + ROWS * 128;
+    const uint8_t* bi = sc + ROWS * 16;
     const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
     const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
     const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
@@ -269,10 +270,18 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
 // fused lm_head + argmax (persistent over 128-row vocabulary blocks)
 // ------------------------------------------------------------------------------------------------
 struct I8LmArgs {
-    CUtensorMap tw, ts, tb;
+    CUtensorMap tw, ts, tb;  // boxes of 128 rows
     LmHeadLaunch L;
     int G, S, nblocks, ncols;
     uint32_t off_bar, off_misc, off_keys, off_scr, off_xs, off_cs, off_xq, off_ring;
+};
+
+// lm_head stage: 16 W rows x 4 groups, loaded as 16 W / 128 boxes of 128 rows per tensor
+template <int W>
+struct LmStage {
+    static constexpr int kRows = 16 * W;
+    static constexpr uint32_t kBytes = kRows * (128 + 2 * 16);
+    static constexpr int kThreads = (W + 1) * 32;
 };
 
 __device__ __forceinline__ unsigned long long i8_logit_key(float v, int64_t idx) {
@@ -281,8 +290,9 @@ __device__ __forceinline__ unsigned long long i8_logit_key(float v, int64_t idx)
     return ((unsigned long long)o << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
 }
 
-template <int NTN>
-__global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_constant__ I8LmArgs a) {
+template <int NTN, int W>
+__global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(const __grid_constant__ I8LmArgs a) {
+    using ST = LmStage<W>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align_smem_1024(smem_raw);
     const LmHeadLaunch& L = a.L;
@@ -303,16 +313,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_
 
     auto issue = [&](int q) {
         const int bi = q / spb, gs = (q % spb) * kI8StageGroups;
-        const int64_t row0 = (int64_t)(blockIdx.x + (int64_t)bi * gridDim.x) * kI8Rows;
-        uint8_t* st = ring + (size_t)(q % S) * kI8StageBytes;
-        mbar_arrive_expect_tx(&full[q % S], kI8StageBytes);
-        i8_issue(st, &a.tw, &a.ts, &a.tb, gs, row0, 0, &full[q % S]);
+        const int64_t row0 = (int64_t)(blockIdx.x + (int64_t)bi * gridDim.x) * ST::kRows;
+        uint8_t* st = ring + (size_t)(q % S) * ST::kBytes;
+        mbar_arrive_expect_tx(&full[q % S], ST::kBytes);
+#pragma unroll
+        for (int h = 0; h < ST::kRows / kI8Rows; ++h) {
+            const int32_t y = (int32_t)(row0 + h * kI8Rows);
+            tma_load_2d(st + h * kI8Rows * 128, &a.tw, gs * 8, y, &full[q % S]);
+            tma_load_2d(st + ST::kRows * 128 + h * kI8Rows * 16, &a.ts, gs & ~7, y, &full[q % S]);
+            tma_load_2d(st + ST::kRows * 144 + h * kI8Rows * 16, &a.tb, gs & ~7, y, &full[q % S]);
+        }
     };
     if (tid == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kI8Warps);
+            mbar_init(&empty[s], W);
         }
         fence_mbar_init();
         prefetch_tmap(&a.tw);
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_
     pdl_launch_dependents();
     stage_x_i8(L.x, L.x_dtype, (int)L.w.k, L.norm_w, L.eps, 0, G, M, ncols, tx);
 
-    if (warp == kI8Warps) {
+    if (warp == W) {
         if (lane == 0) {
             int q = min(S, nst);
             for (; q < nst; ++q) {
@@ -347,13 +363,13 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_
         for (int q = 0; q < nst; ++q) {
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             const int sp = q % spb, gs = sp * kI8StageGroups;
-            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
+            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
 #pragma unroll
             for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q % S]);
             if (sp == spb - 1) {  // block finished: logits -> argmax keys (max over the warp's rows)
-                const int64_t rowa = (int64_t)(blockIdx.x + (int64_t)(q / spb) * gridDim.x) * kI8Rows + 16 * warp + g;
+                const int64_t rowa = (int64_t)(blockIdx.x + (int64_t)(q / spb) * gridDim.x) * ST::kRows + 16 * warp + g;
                 const int64_t rowb = rowa + 8;
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
@@ -393,7 +409,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8_lm_head_kernel(const __grid_
     __shared__ bool is_last;
     if (tid < M) {
         unsigned long long k = 0ull;
-        for (int w = 0; w < kI8Warps; ++w) k = ckeys[w * M + tid] > k ? ckeys[w * M + tid] : k;
+        for (int w = 0; w < W; ++w) k = ckeys[w * M + tid] > k ? ckeys[w * M + tid] : k;
         if (k) atomicMax(&L.keys[tid], k);
     }
     __threadfence();
@@ -480,22 +496,28 @@ uint32_t plan_i8_unit(const GemvLaunch& L, I8UnitArgs& a) {
     return 0;
 }
 
-uint32_t plan_i8_lm_head(const LmHeadLaunch& L, I8LmArgs& a) {
+// consumer warps of the lm_head kernel: 16 (256-row blocks) while the activation planes leave
+// room for at least three 40 KB stages, else 8
+int lm_warps(int64_t m) { return ntn_for(m) <= 4 ? 16 : 8; }
+
+uint32_t plan_i8_lm_head(const LmHeadLaunch& L, I8LmArgs& a, int W) {
     a.L = L;
     const int K = (int)L.w.k;
     a.G = K / kGroup;
     a.ncols = 8 * ntn_for(L.m);
-    a.nblocks = (int)((L.w.n + kI8Rows - 1) / kI8Rows);
+    const int rows = 16 * W;
+    const uint32_t stage = (uint32_t)rows * 160;
+    a.nblocks = (int)((L.w.n + rows - 1) / rows);
     for (int S = 12; S >= 2; --S) {
         uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.G, a.ncols, a.off_bar, a.off_misc, a.off_scr,
                                    a.off_xs, a.off_cs, S);
         a.off_keys = off;
-        off += align_up(kI8Warps * (uint32_t)L.m * 8, 128);
+        off += align_up((uint32_t)W * (uint32_t)L.m * 8, 128);
         a.off_xq = off;
         off += (uint32_t)a.G * a.ncols * 64;
         off = align_up(off, 1024);
         a.off_ring = off;
-        off += (uint32_t)S * kI8StageBytes + 1024;
+        off += (uint32_t)S * stage + 1024;
         if (off <= kI8SmemLimit) {
             a.S = S;
             return off;
@@ -537,16 +559,20 @@ cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream) {
 
 cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream) {
     I8LmArgs a{};
-    const uint32_t smem = plan_i8_lm_head(L, a);
+    const int W = lm_warps(L.m);
+    const uint32_t smem = plan_i8_lm_head(L, a, W);
     if (!smem) return cudaErrorInvalidConfiguration;
     if (!encode_q4_maps(L.w, kI8Rows, &a.tw, &a.ts, &a.tb)) return cudaErrorInvalidValue;
     const int grid = std::max(1, std::min(device_num_sms(), a.nblocks));
-    switch (a.ncols / 8) {
-        case 1: return launch_ex(i8_lm_head_kernel<1>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
-        case 2: return launch_ex(i8_lm_head_kernel<2>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
-        case 4: return launch_ex(i8_lm_head_kernel<4>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
-        default: return launch_ex(i8_lm_head_kernel<8>, a, grid, kI8Threads, 1, smem, L.pdl, stream);
+    if (W == 16) {
+        constexpr int T = LmStage<16>::kThreads;
+        switch (a.ncols / 8) {
+            case 1: return launch_ex(i8_lm_head_kernel<1, 16>, a, grid, T, 1, smem, L.pdl, stream);
+            case 2: return launch_ex(i8_lm_head_kernel<2, 16>, a, grid, T, 1, smem, L.pdl, stream);
+            default: return launch_ex(i8_lm_head_kernel<4, 16>, a, grid, T, 1, smem, L.pdl, stream);
+        }
     }
+    return launch_ex(i8_lm_head_kernel<8, 8>, a, grid, LmStage<8>::kThreads, 1, smem, L.pdl, stream);
 }
 
 int i8_device_error(bool clear) { return tu_device_error(clear); }
