@@ -285,8 +285,88 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
 // scratch for either the one-kernel step or the per-kernel composition.
 namespace {
 size_t step_zero_bytes(int64_t m) { return 256 + align16((size_t)m * 8 + 16); }
+size_t step_ssq_bytes(int64_t m, int64_t hidden) { return align16((size_t)((hidden + 127) / 128) * m * 4); }
+// h and act (binary32), then the activation planes handed between the integer-MMA kernels
 size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
-    return align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
+    size_t b = align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
+    if (m <= kI8MaxRows) b = (b + 255) / 256 * 256 + i8_planes_bytes(m, inter) + i8_planes_bytes(m, hidden) +
+                             step_ssq_bytes(m, hidden);
+    return b;
+}
+
+// The decode step on the integer-MMA kernels with the activations handed over as planes: each
+// kernel's epilogue writes the next kernel's operand (act planes; h * (1 + next norm weight) planes
+// with per-block sums of squares), so only the first gate/up launch stages from h0.
+int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t inter, int32_t n_layers,
+                       const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
+                       const marlin_q4_tensor* lm, int32_t* ids, float* best, float* h, uint8_t* scratch,
+                       void* lmws, cudaStream_t st) {
+    float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
+    uint8_t* pl = scratch + (align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4) + 255) / 256 * 256;
+    const XPlanes ap = i8_planes_at(pl, m, inter, nullptr, 0);
+    pl += i8_planes_bytes(m, inter);
+    float* ssq = reinterpret_cast<float*>(pl + i8_planes_bytes(m, hidden));
+    const XPlanes hp = i8_planes_at(pl, m, hidden, ssq, (int)((hidden + 127) / 128));
+    int rc;
+    const void* cur = h0;
+    int32_t cur_dtype = MARLIN_Q4_BF16;
+    for (int32_t l = 0; l < n_layers; ++l) {
+        const marlin_q4_layer& Ly = layers[l];
+        GemvLaunch G{};
+        G.x = cur;
+        G.x_dtype = cur_dtype;
+        G.m = m;
+        G.norm_w = Ly.post_attn_norm;
+        G.eps = eps;
+        G.w0 = view(&Ly.gate_proj);
+        G.w1 = view(&Ly.up_proj);
+        G.y = act;
+        G.y_dtype = MARLIN_Q4_F32;
+        G.ldy = inter;
+        G.epi = kEpiSwiglu;
+        G.pdl = g_pdl;
+        G.has_xin = l > 0;
+        G.xin = hp;
+        G.has_xout = true;
+        G.xout = ap;
+        if ((rc = cuda_status(launch_i8_gemv(G, st)))) return rc;
+        GemvLaunch D{};
+        D.x = act;
+        D.x_dtype = MARLIN_Q4_F32;
+        D.m = m;
+        D.w0 = view(&Ly.down_proj);
+        D.y = h;
+        D.y_dtype = MARLIN_Q4_F32;
+        D.ldy = hidden;
+        D.resid = cur;
+        D.resid_dtype = cur_dtype;
+        D.ldr = hidden;
+        D.epi = kEpiResid;
+        D.pdl = g_pdl;
+        D.has_xin = true;
+        D.xin = ap;
+        D.has_xout = true;
+        D.xout = hp;
+        D.out_norm = l + 1 < n_layers ? layers[l + 1].post_attn_norm : final_norm;
+        if ((rc = cuda_status(launch_i8_gemv(D, st)))) return rc;
+        cur = h;
+        cur_dtype = MARLIN_Q4_F32;
+    }
+    LmHeadLaunch Lh{};
+    Lh.x = h;
+    Lh.x_dtype = MARLIN_Q4_F32;
+    Lh.m = m;
+    Lh.norm_w = final_norm;
+    Lh.eps = eps;
+    Lh.w = view(lm);
+    Lh.keys = static_cast<unsigned long long*>(lmws);
+    Lh.counter = reinterpret_cast<unsigned int*>(Lh.keys + m);
+    Lh.ids = ids;
+    Lh.best = best;
+    Lh.pdl = g_pdl;
+    Lh.has_xin = true;
+    Lh.xin = hp;
+    return cuda_status(launch_i8_lm_head(Lh, st));
 }
 }  // namespace
 
@@ -352,6 +432,10 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     float* h = reinterpret_cast<float*>(scratch);
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
+    if (decode_path() == kPathI8 && uniform && m <= kI8MaxRows && i8_supported(hidden, m) &&
+        i8_supported(inter, m) && hidden % 128 == 0)
+        return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h, scratch,
+                                  lmws, st);
     const void* cur = h0;
     int32_t cur_dtype = MARLIN_Q4_BF16;
     for (int32_t l = 0; l < n_layers; ++l) {

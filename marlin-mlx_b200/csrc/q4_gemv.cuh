@@ -23,6 +23,23 @@ enum Epilogue : int {
     kEpiResid = 2,   // y[m, row] = resid[m, row] + out       (residual add, binary32)
 };
 
+// Activation rows handed from one integer-MMA decode kernel to the next in the operand form: the
+// producing kernel's epilogue writes them, the consuming kernel copies its K range into shared
+// memory instead of staging.  Per 64-group g of K and activation column c = 4 m + p (ncols =
+// 8 * ceil(m / 2) rounded to a power of two, padding columns zero):
+//   q[g][c][64]  s8 plane digits of the group, in the B-fragment byte order;
+//   xs[g][c]     64 * (sum of the group's values) on plane-0 columns, 0 elsewhere;
+//   xe[g][c]     2^e with e the group's exponent (|x| < 2^e), 0 on padding columns;
+//   ssq[b][m]    sums of squares of the raw rows per 128-row block b < nssq (a following RMSNorm
+//                takes its row factor from them); null when no RMSNorm follows.
+struct XPlanes {
+    uint8_t* q;
+    float* xs;
+    float* xe;
+    float* ssq;
+    int nssq;
+};
+
 struct GemvLaunch {
     const void* x;  // [m, k] activations (x_dtype)
     int x_dtype;
@@ -39,6 +56,12 @@ struct GemvLaunch {
     int64_t ldr;
     int epi;
     bool pdl;  // launch with programmatic stream serialization
+    // integer-MMA family only: activations taken from planes (x unused; norm_w then applies as the
+    // row factor from xin.ssq), and/or output rows also written as planes of y * (1 + out_norm)
+    // (y when out_norm is null; xout.ssq, when set, receives the sums of squares of y)
+    bool has_xin, has_xout;
+    XPlanes xin, xout;
+    const uint16_t* out_norm;
 };
 
 // Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default), tcgen05/TMEM, bf16
@@ -72,6 +95,8 @@ struct LmHeadLaunch {
     int32_t* ids;            // optional [m]: argmax ids (vocab_offset applied)
     float* best;             // optional [m]: winning logit
     bool pdl;
+    bool has_xin;            // integer-MMA family only: hidden state taken from planes (see XPlanes)
+    XPlanes xin;
 };
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream);

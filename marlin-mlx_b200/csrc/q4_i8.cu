@@ -29,6 +29,18 @@
 
 #include <algorithm>
 
+// Optional timeline hooks of the decode GEMV kernel, empty in the library build: I8_MARK_BEGIN()
+// at entry, I8_MARK(point) at phase boundaries (evaluated by thread 0 of each CTA).
+#ifndef I8_MARK_BEGIN
+#define I8_MARK_BEGIN()
+#endif
+#ifndef I8_MARK
+#define I8_MARK(k)
+#endif
+#ifndef I8_STAGE_MARK
+#define I8_STAGE_MARK(q)
+#endif
+
 namespace marlin {
 namespace {
 
@@ -79,10 +91,12 @@ __device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, con
             mma_s8_16832(c, a0, xv.x, xv.y);
             mma_s8_16832(e, a1, xv.z, xv.w);
             const float2 xs = *reinterpret_cast<const float2*>(t.xs + gl * ncols + 8 * j + 2 * tq);
-            y[j][0] = fmaf(sr0, (float)(c[0] + e[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(sr0, (float)(c[1] + e[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(sr1, (float)(c[2] + e[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(sr1, (float)(c[3] + e[3]), fmaf(br1, xs.y, y[j][3]));
+            const float xe = t.xe[gl * ncols + 8 * j + 2 * tq];  // both columns belong to one row
+            const float s0 = sr0 * xe, s1 = sr1 * xe;
+            y[j][0] = fmaf(s0, (float)(c[0] + e[0]), fmaf(br0, xs.x, y[j][0]));
+            y[j][1] = fmaf(s0, (float)(c[1] + e[1]), fmaf(br0, xs.y, y[j][1]));
+            y[j][2] = fmaf(s1, (float)(c[2] + e[2]), fmaf(br1, xs.x, y[j][2]));
+            y[j][3] = fmaf(s1, (float)(c[3] + e[3]), fmaf(br1, xs.y, y[j][3]));
         }
     }
 }
@@ -97,13 +111,112 @@ __device__ __forceinline__ void i8_issue(uint8_t* st, const CUtensorMap* tw, con
 }
 
 // ------------------------------------------------------------------------------------------------
+// activation planes handed between kernels (XPlanes)
+// ------------------------------------------------------------------------------------------------
+// Consumer side, one thread: bulk-copy groups [g0, g0 + ng) of the planes into shared memory.
+__device__ __forceinline__ void copy_planes_in(const XPlanes& P, int g0, int ng, int ncols, const I8X& t,
+                                               uint64_t* bar) {
+    const uint32_t qb = (uint32_t)ng * ncols * 64, fb = (uint32_t)ng * ncols * 4;
+    mbar_arrive_expect_tx(bar, qb + 2 * fb);
+    tma_bulk_g2s(t.xq, P.q + (size_t)g0 * ncols * 64, qb, bar);
+    tma_bulk_g2s(t.xs, P.xs + (size_t)g0 * ncols, fb, bar);
+    tma_bulk_g2s(t.xe, P.xe + (size_t)g0 * ncols, fb, bar);
+}
+
+// Consumer side, whole block: the plane weights cs and, when an RMSNorm applies, the row factors
+// r_m = 1/sqrt(sum(ssq blocks) / K + eps) (binary32, blocks summed in order).
+__device__ __forceinline__ void planes_factors(const XPlanes& P, const uint16_t* norm_w, float eps, int M, int K,
+                                               int ncols, const I8X& t) {
+    for (int c = threadIdx.x; c < ncols; c += blockDim.x) t.cs[c] = (c >> 2) < M ? pow2f(-6 - 7 * (c & 3)) : 0.f;
+    if (norm_w && (int)threadIdx.x < M) {
+        float s = 0.f;
+        for (int b = 0; b < P.nssq; ++b) s = __fadd_rn(s, P.ssq[(size_t)b * M + threadIdx.x]);
+        const float var = __fmul_rn(s, (float)(1.0 / (double)K));
+        t.rf[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Producer side, called by the `nthreads` epilogue threads (whole warps; two consecutive warps own
+// one 64-group): thread holds element k of group gi, value v[m] (the operand) and raw[m] (whose
+// squares feed P.ssq).  Per group: exponent from the group maximum, s8 digits as planes8, 64 x the
+// group sum on plane 0, 2^e on every plane column; padding columns zeroed.  P.ssq[slot][m] gets the
+// sum of squares over all `nthreads` rows (fixed order).  ep: shared scratch [nthreads/32][3][MS].
+template <int MS>
+__device__ __forceinline__ void write_planes(const XPlanes& P, int ncols, int M, int64_t gi, int k,
+                                             const float (&v)[MS], const float (&raw)[MS], float* ep, int wig,
+                                             int nthreads, int slot) {
+    const int lane = threadIdx.x & 31;
+    const bool with_ssq = P.ssq != nullptr;
+#pragma unroll
+    for (int m = 0; m < MS; ++m) {
+        if (m < M) {  // warp-uniform
+            const unsigned mx = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v[m])));
+            float sm = v[m], sq = with_ssq ? __fmul_rn(raw[m], raw[m]) : 0.f;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            if (with_ssq) {
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            }
+            if (lane == 0) {
+                ep[(wig * 3 + 0) * MS + m] = __uint_as_float(mx);
+                ep[(wig * 3 + 1) * MS + m] = sm;
+                ep[(wig * 3 + 2) * MS + m] = sq;
+            }
+        }
+    }
+    named_bar_sync(3, nthreads);
+    const int w0 = wig & ~1;
+    const size_t gbase = (size_t)gi * ncols;
+    const int pos = plane_pos(k);
+#pragma unroll
+    for (int m = 0; m < MS; ++m) {
+        if (m < M) {
+            const float gmax = fmaxf(ep[(w0 * 3) * MS + m], ep[((w0 + 1) * 3) * MS + m]);
+            const int e = row_exp(__float_as_uint(gmax));
+            const float qa = rintf(__fmul_rn(v[m], pow2f(13 - e)));
+            const int A = (int)qa;
+            const int B = __float2int_rn(__fmul_rn(fmaf(-qa, pow2f(e - 13), v[m]), pow2f(27 - e)));
+            const int i0 = (A + 64) >> 7, i2 = (B + 64) >> 7;
+            const int d[4] = {i0, A - (i0 << 7), i2, B - (i2 << 7)};
+#pragma unroll
+            for (int p = 0; p < 4; ++p) P.q[(gbase + 4 * m + p) * 64 + pos] = (uint8_t)(d[p] & 0xff);
+            if (k == 0) {
+                const float sg = ep[(w0 * 3 + 1) * MS + m] + ep[((w0 + 1) * 3 + 1) * MS + m];
+                const float pe = pow2f(e);
+                *reinterpret_cast<float4*>(P.xs + gbase + 4 * m) = make_float4(__fmul_rn(sg, 64.0f), 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(P.xe + gbase + 4 * m) = make_float4(pe, pe, pe, pe);
+            }
+        }
+    }
+    const int pad = ncols - 4 * M;  // padding columns: 16-byte stores spread over the group's 64 threads
+    for (int i = k; i < 4 * pad; i += 64)
+        *reinterpret_cast<uint4*>(P.q + (gbase + 4 * M + i / 4) * 64 + (i & 3) * 16) = make_uint4(0, 0, 0, 0);
+    for (int i = k; i < pad; i += 64) {
+        P.xs[gbase + 4 * M + i] = 0.f;
+        P.xe[gbase + 4 * M + i] = 0.f;
+    }
+    if (with_ssq && threadIdx.x == 0) {
+        for (int m = 0; m < M; ++m) {
+            float sq = 0.f;
+            for (int w = 0; w < nthreads / 32; ++w) sq = __fadd_rn(sq, ep[(w * 3 + 2) * MS + m]);
+            P.ssq[(size_t)slot * M + m] = sq;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // decode GEMV family: one 128-row block per thread-block cluster, K split over the cluster's CTAs
 // ------------------------------------------------------------------------------------------------
 struct I8UnitArgs {
     CUtensorMap tw0, ts0, tb0, tw1, ts1, tb1;  // w0 (gate / main) and w1 (up) maps
     GemvLaunch L;
     int G, CL, gpc, S, ncols;  // groups, cluster size, groups per CTA, ring stages, activation columns
-    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_red, off_xq, off_ring;
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_red, off_xq, off_ring, off_xe, off_ep;
 };
 
 // One instantiation per activation width serves all three epilogues (a run-time switch), so the
@@ -112,6 +225,7 @@ template <int NTN>
 __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_constant__ I8UnitArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align_smem_1024(smem_raw);
+    I8_MARK_BEGIN();
     constexpr int MS = 2 * NTN;  // activation rows per pass
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -131,7 +245,7 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
     uint8_t* ring = smem + a.off_ring;
     I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
            reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
-           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
+           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64), reinterpret_cast<float*>(smem + a.off_xe)};
 
     auto issue = [&](int q) {
         uint8_t* st = ring + (size_t)(q % S) * kI8StageBytes;
@@ -140,21 +254,49 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
         i8_issue(st, &a.tw0, &a.ts0, &a.tb0, gs, row0, 0, &full[q % S]);
         if (kSwiglu) i8_issue(st, &a.tw1, &a.ts1, &a.tb1, gs, row0, kHalf, &full[q % S]);
     };
+    uint64_t* xbar = full + 2 * S;  // planes copied in (has_xin)
     if (tid == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kI8Warps);
         }
+        mbar_init(xbar, 1);
         fence_mbar_init();
         prefetch_tmap(&a.tw0);
         // as much of this CTA's weight range as the ring holds, before the dependency wait
         for (int q = 0; q < min(S, nst); ++q) issue(q);
     }
+    // epilogue operands that do not wait for the math, read early by the leader's epilogue threads
+    // (small batches: held in registers through the main loop): the next RMSNorm weight (a weight,
+    // read before the dependency wait) and the residual rows (read right after it)
+    constexpr bool kEarly = MS <= 4;
+    const bool early = kEarly && rank == 0 && tid < kI8Rows && EPI == kEpiResid && row0 + tid < L.w0.n;
+    float wpre = 0.f, rpre[MS];
+#pragma unroll
+    for (int m = 0; m < MS; ++m) rpre[m] = 0.f;
+    if (early && L.has_xout && L.out_norm) wpre = bf16_bits_to_f32(L.out_norm[row0 + tid]);
     __syncthreads();
+    I8_MARK(1);
     pdl_wait();
+    I8_MARK(2);
     pdl_launch_dependents();
-    stage_x_i8(L.x, L.x_dtype, (int)L.w0.k, L.norm_w, L.eps, g0, ng, M, ncols, tx);
+    if (early) {
+#pragma unroll
+        for (int m = 0; m < MS; ++m)
+            if (m < M)
+                rpre[m] = L.resid_dtype == kBF16
+                              ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[(int64_t)m * L.ldr + row0 + tid])
+                              : static_cast<const float*>(L.resid)[(int64_t)m * L.ldr + row0 + tid];
+    }
+    if (L.has_xin) {
+        if (tid == kI8Warps * 32) copy_planes_in(L.xin, g0, ng, ncols, tx, xbar);
+        planes_factors(L.xin, L.norm_w, L.eps, M, (int)L.w0.k, ncols, tx);
+        __syncthreads();
+    } else {
+        stage_x_i8(L.x, L.x_dtype, (int)L.w0.k, L.norm_w, L.eps, g0, ng, M, ncols, tx);
+    }
+    I8_MARK(3);
 
     float y[NTN][4];
 #pragma unroll
@@ -167,10 +309,13 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
                 issue(q);
             }
             for (int r = max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
+            if (L.has_xin) drain_wait(xbar, 0u);
         }
     } else {
-        for (int q = 0; q < nst; ++q) {
+        const bool xin_ok = !L.has_xin || warp_wait(xbar, 0u, abort);
+        for (int q = 0; xin_ok && q < nst; ++q) {
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
+            I8_STAGE_MARK(q);
             const int gs = g0 + q * kI8StageGroups;
             i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, ncols, warp,
                           lane, y);
@@ -202,19 +347,25 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
                 }
             }
         }
+        I8_MARK(4);
     }
     if (CL > 1) cluster_sync_all();
     else __syncthreads();
+    I8_MARK(5);
     if (rank != 0 || tid >= kI8Rows) return;
 
     // leader epilogue: thread = block row lrow; out[m] = sum over the cluster's partials
     const int lrow = tid;
+    const bool row_factor = L.has_xin && L.norm_w;  // RMSNorm as a row factor on planes copied in
+    float* ep = reinterpret_cast<float*>(smem + a.off_ep);
     float o[MS];
 #pragma unroll
     for (int m = 0; m < MS; ++m) {
         o[m] = 0.f;
-        if (m < M)
+        if (m < M) {
             for (int r = 0; r < CL; ++r) o[m] += red[((size_t)r * kI8Rows + lrow) * MS + m];
+            if (row_factor) o[m] *= tx.rf[m];
+        }
     }
     if (kSwiglu) {
         // up rows (64..127) hand their outputs to the gate rows through shared memory
@@ -226,44 +377,61 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (lrow < kHalf) {
             const int64_t f = row0 + lrow;
-            if (f < L.w0.n) {
+            float av[MS];
 #pragma unroll
-                for (int m = 0; m < MS; ++m) {
-                    if (m < M) {
-                        const float gsum = o[m], u = xch[lrow * MS + m];
-                        if (L.y_dtype == kBF16) {
-                            const float gq = bf16_round(gsum), uq = bf16_round(u);
-                            const float sg = bf16_round(__fdividef(1.0f, 1.0f + expf(-gq)));
-                            const float r = bf16_round(bf16_round(sg * gq) * uq);
-                            static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + f] = (uint16_t)f32_to_bf16_bits(r);
-                        } else {
-                            const float sg = 1.0f / (1.0f + expf(-gsum));
-                            static_cast<float*>(L.y)[(int64_t)m * L.ldy + f] = (sg * gsum) * u;
-                        }
+            for (int m = 0; m < MS; ++m) {
+                av[m] = 0.f;
+                if (m < M && f < L.w0.n) {
+                    const float gsum = o[m], u = xch[lrow * MS + m];
+                    if (L.y_dtype == kBF16) {
+                        const float gq = bf16_round(gsum), uq = bf16_round(u);
+                        const float sg = bf16_round(__fdividef(1.0f, 1.0f + expf(-gq)));
+                        av[m] = bf16_round(bf16_round(sg * gq) * uq);
+                        static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + f] = (uint16_t)f32_to_bf16_bits(av[m]);
+                    } else {
+                        const float sg = 1.0f / (1.0f + expf(-gsum));
+                        av[m] = (sg * gsum) * u;
+                        static_cast<float*>(L.y)[(int64_t)m * L.ldy + f] = av[m];
                     }
                 }
             }
+            // one 64-group of the activation per block (kHalf = 64 rows per matrix)
+            I8_MARK(15);
+            if (L.has_xout) write_planes<MS>(L.xout, ncols, M, row0 / 64, lrow, av, av, ep, lrow >> 5, kHalf, block);
         }
+        I8_MARK(6);
         return;
     }
     const int64_t row = row0 + lrow;
-    if (row >= L.w0.n) return;
+    const bool live = row < L.w0.n;
+    float v[MS], u[MS];
+    const float wn = early ? wpre : (L.has_xout && L.out_norm && live) ? bf16_bits_to_f32(L.out_norm[row]) : 0.f;
 #pragma unroll
     for (int m = 0; m < MS; ++m) {
-        if (m < M) {
-            float v = o[m];
+        v[m] = u[m] = 0.f;
+        if (m < M && live) {
+            v[m] = o[m];
             if (EPI == kEpiResid) {
-                const float hv = L.resid_dtype == kBF16
-                                     ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[(int64_t)m * L.ldr + row])
-                                     : static_cast<const float*>(L.resid)[(int64_t)m * L.ldr + row];
-                v = hv + v;
+                const float hv =
+                    early ? rpre[m]
+                    : L.resid_dtype == kBF16
+                        ? bf16_bits_to_f32(static_cast<const uint16_t*>(L.resid)[(int64_t)m * L.ldr + row])
+                        : static_cast<const float*>(L.resid)[(int64_t)m * L.ldr + row];
+                v[m] = hv + v[m];
             }
-            if (L.y_dtype == kBF16)
-                static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + row] = (uint16_t)f32_to_bf16_bits(v);
-            else
-                static_cast<float*>(L.y)[(int64_t)m * L.ldy + row] = v;
+            if (L.y_dtype == kBF16) {
+                static_cast<uint16_t*>(L.y)[(int64_t)m * L.ldy + row] = (uint16_t)f32_to_bf16_bits(v[m]);
+                v[m] = bf16_round(v[m]);
+            } else {
+                static_cast<float*>(L.y)[(int64_t)m * L.ldy + row] = v[m];
+            }
+            u[m] = L.out_norm ? __fmul_rn(v[m], __fadd_rn(1.0f, wn)) : v[m];
         }
     }
+    // two 64-groups per 128-row block
+    I8_MARK(15);
+    if (L.has_xout) write_planes<MS>(L.xout, ncols, M, row / 64, lrow & 63, u, v, ep, lrow >> 5, kI8Rows, block);
+    I8_MARK(6);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -273,7 +441,7 @@ struct I8LmArgs {
     CUtensorMap tw, ts, tb;  // boxes of 128 rows
     LmHeadLaunch L;
     int G, S, nblocks, ncols;
-    uint32_t off_bar, off_misc, off_keys, off_scr, off_xs, off_cs, off_xq, off_ring;
+    uint32_t off_bar, off_misc, off_keys, off_scr, off_xs, off_cs, off_xq, off_ring, off_xe;
 };
 
 // lm_head stage: 16 W rows x 4 groups, loaded as 16 W / 128 boxes of 128 rows per tensor
@@ -309,7 +477,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     uint8_t* ring = smem + a.off_ring;
     I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
            reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
-           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
+           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64), reinterpret_cast<float*>(smem + a.off_xe)};
 
     auto issue = [&](int q) {
         const int bi = q / spb, gs = (q % spb) * kI8StageGroups;
@@ -330,6 +498,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
+        mbar_init(full + 2 * S, 1);
         fence_mbar_init();
         prefetch_tmap(&a.tw);
         prefetch_tmap(&a.ts);
@@ -339,7 +508,14 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     __syncthreads();
     pdl_wait();
     pdl_launch_dependents();
-    stage_x_i8(L.x, L.x_dtype, (int)L.w.k, L.norm_w, L.eps, 0, G, M, ncols, tx);
+    uint64_t* xbar = full + 2 * S;  // planes copied in (has_xin)
+    if (L.has_xin) {
+        if (tid == W * 32) copy_planes_in(L.xin, 0, G, ncols, tx, xbar);
+        planes_factors(L.xin, L.norm_w, L.eps, M, (int)L.w.k, ncols, tx);
+        __syncthreads();
+    } else {
+        stage_x_i8(L.x, L.x_dtype, (int)L.w.k, L.norm_w, L.eps, 0, G, M, ncols, tx);
+    }
 
     if (warp == W) {
         if (lane == 0) {
@@ -349,10 +525,13 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
                 issue(q);
             }
             for (int r = max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
+            if (L.has_xin) drain_wait(xbar, 0u);
         }
     } else {
         const int g = lane >> 2, tq = lane & 3;
-        const bool bf16_logits = L.x_dtype == kBF16 && !L.norm_w;
+        const bool bf16_logits = L.x_dtype == kBF16 && !L.norm_w && !L.has_xin;
+        const bool row_factor = L.has_xin && L.norm_w;
+        const bool xin_ok = !L.has_xin || warp_wait(xbar, 0u, abort);
         float y[NTN][4];
         unsigned long long best[NTN];
 #pragma unroll
@@ -360,7 +539,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
             y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
             best[j] = 0ull;
         }
-        for (int q = 0; q < nst; ++q) {
+        for (int q = 0; xin_ok && q < nst; ++q) {
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             const int sp = q % spb, gs = sp * kI8StageGroups;
             i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
@@ -378,6 +557,11 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
                     float lb = fmaf(cv.x, y[j][2], cv.y * y[j][3]);
                     la += __shfl_xor_sync(0xffffffffu, la, 1);
                     lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+                    if (row_factor) {
+                        const float rfm = tx.rf[min(2 * j + (tq >> 1), M - 1)];
+                        la *= rfm;
+                        lb *= rfm;
+                    }
                     if (bf16_logits) {
                         la = bf16_round(la);
                         lb = bf16_round(lb);
@@ -438,12 +622,14 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
 // ------------------------------------------------------------------------------------------------
 int ntn_for(int64_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
 
+size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
 // Shared-memory layout common to both kernels; returns the byte offset after the activations.
 uint32_t plan_common(int M, int K, bool normed, int ng, int ncols, uint32_t& off_bar, uint32_t& off_misc,
-                     uint32_t& off_scr, uint32_t& off_xs, uint32_t& off_cs, int S) {
+                     uint32_t& off_scr, uint32_t& off_xs, uint32_t& off_cs, uint32_t& off_xe, int S) {
     uint32_t off = 0;
     off_bar = off;
-    off += align_up(2u * (uint32_t)S * 8u, 128);
+    off += align_up((2u * (uint32_t)S + 1u) * 8u, 128);  // full[S], empty[S], planes copy-in
     off_misc = off;
     off += 128;  // abort flag + amax[M <= 16]
     off_scr = off;
@@ -452,6 +638,8 @@ uint32_t plan_common(int M, int K, bool normed, int ng, int ncols, uint32_t& off
     off += align_up((uint32_t)ng * ncols * 4, 128);
     off_cs = off;
     off += align_up((uint32_t)ncols * 4, 128);
+    off_xe = off;
+    off += align_up((uint32_t)ng * ncols * 4, 128);
     return off;
 }
 
@@ -478,9 +666,11 @@ uint32_t plan_i8_unit(const GemvLaunch& L, I8UnitArgs& a) {
     const int ms = 2 * ntn;
     for (int S = nst; S >= 2 || S == nst; --S) {
         uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.gpc, a.ncols, a.off_bar, a.off_misc, a.off_scr,
-                                   a.off_xs, a.off_cs, S);
+                                   a.off_xs, a.off_cs, a.off_xe, S);
         a.off_red = off;
         off += align_up((uint32_t)(CL + 1) * kI8Rows * ms * 4, 128);  // partials + SwiGLU exchange
+        a.off_ep = off;
+        off += align_up(4u * 3u * (uint32_t)ms * 4u, 128);  // epilogue plane statistics
         a.off_xq = off;
         off += (uint32_t)a.gpc * a.ncols * 64;
         off = align_up(off, 1024);
@@ -510,7 +700,7 @@ uint32_t plan_i8_lm_head(const LmHeadLaunch& L, I8LmArgs& a, int W) {
     a.nblocks = (int)((L.w.n + rows - 1) / rows);
     for (int S = 12; S >= 2; --S) {
         uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.G, a.ncols, a.off_bar, a.off_misc, a.off_scr,
-                                   a.off_xs, a.off_cs, S);
+                                   a.off_xs, a.off_cs, a.off_xe, S);
         a.off_keys = off;
         off += align_up((uint32_t)W * (uint32_t)L.m * 8, 128);
         a.off_xq = off;
@@ -576,5 +766,24 @@ cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream) {
 }
 
 int i8_device_error(bool clear) { return tu_device_error(clear); }
+
+int i8_ncols(int64_t m) { return 8 * ntn_for(m); }
+
+size_t i8_planes_bytes(int64_t m, int64_t k) {
+    const size_t g = (size_t)(k / kGroup), c = (size_t)i8_ncols(m);
+    return al256(g * c * 64) + 2 * al256(g * c * 4);
+}
+
+XPlanes i8_planes_at(void* base, int64_t m, int64_t k, float* ssq, int nssq) {
+    const size_t g = (size_t)(k / kGroup), c = (size_t)i8_ncols(m);
+    uint8_t* p = static_cast<uint8_t*>(base);
+    XPlanes P{};
+    P.q = p;
+    P.xs = reinterpret_cast<float*>(p + al256(g * c * 64));
+    P.xe = reinterpret_cast<float*>(p + al256(g * c * 64) + al256(g * c * 4));
+    P.ssq = ssq;
+    P.nssq = nssq;
+    return P;
+}
 
 }  // namespace marlin

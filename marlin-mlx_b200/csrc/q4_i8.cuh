@@ -21,4 +21,11 @@ cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream);
 // Device error word of this translation unit (see gemv_device_error).
 int i8_device_error(bool clear);
 
+// Activation columns of the integer-MMA kernels for m rows (4 planes per row, MMA tiles of 8).
+int i8_ncols(int64_t m);
+// Bytes of the q, xs and xe arrays of an XPlanes set for m rows of k features (256-byte aligned
+// pieces, q first), and the set laid out from `base` with the given ssq array.
+size_t i8_planes_bytes(int64_t m, int64_t k);
+XPlanes i8_planes_at(void* base, int64_t m, int64_t k, float* ssq, int nssq);
+
 }  // namespace marlin

@@ -8,6 +8,11 @@
 #include "q4_gemv.cuh"
 #include "q4_stage.cuh"
 
+// Optional timeline hook inside the activation staging (point 0..3), empty in the library build.
+#ifndef STAGE_MARK
+#define STAGE_MARK(k)
+#endif
+
 namespace marlin {
 namespace {
 
@@ -49,14 +54,28 @@ __device__ void norm_factors_team(Team& team, int dtype, int M, int K, float eps
 // (x0, x2, x4, x6, x1, x3, x5, x7): the order the B fragment of mma.m16n8k32 needs when the A
 // fragment is (q0, q2, q4, q6 | q1, q3, q5, q7) of one packed word.
 // ------------------------------------------------------------------------------------------------
+//
+// Fold.  With e the exponent of a group's planes (|x| < 2^e), x = 2^(e-6) sum_p 128^-p i_p, so per
+// weight row and 64-group, s * sum(q x) + b * sum(x) = 2^-6 sum_p 128^-p (s 2^e D_p) + b sum(x):
+// the kernels accumulate Y_p += (s * xe) * D_p + b * xs (xs = 64 sum(x) on plane-0 columns, 0 on
+// the others) and combine the planes once per output with cs = 2^(-6-7p).  Every scaling is by a
+// power of two, so the exponent may vary per group (planes written by the producing kernel) or be
+// one per row (planes staged here) with the same arithmetic.
 struct I8X {
     uint8_t* xq;          // [ng][ncols][64]
-    float* xs;            // [ng][ncols]: plane-0 columns hold sum_g(x) / c_m, the others 0
-    float* cs;            // [ncols]: c_m * 128^-p (0 for padding columns)
+    float* xs;            // [ng][ncols]: plane-0 columns hold 64 sum_g(x), the others 0
+    float* cs;            // [ncols]: 2^(-6-7p) (0 for padding columns)
     float* rf;            // [M] RMSNorm factors
     float* ssq;           // [M * K/8] RMSNorm scratch
     unsigned int* amax;   // [M] max |x| (binary32 bits) over the staged range
+    float* xe;            // [ng][ncols]: 2^e of the group's planes (0 for padding columns)
 };
+
+// byte offset of element k (0..63) of a group in its 64-byte plane row (B-fragment order)
+__device__ __forceinline__ int plane_pos(int k) {
+    const int j = k & 7;
+    return (k & ~7) + ((j & 1) ? 4 : 0) + (j >> 1);
+}
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
@@ -156,8 +175,12 @@ __device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, con
         }
     };
     load_chunk(0);
+    STAGE_MARK(0);
     if (tid < M) t.amax[tid] = 0u;
-    for (int i = tid; i < ng * ncols; i += nt) t.xs[i] = 0.f;
+    for (int i = tid; i < ng * ncols; i += nt) {
+        t.xs[i] = 0.f;
+        t.xe[i] = 0.f;
+    }
     const int pad = ncols - 4 * M;
     for (int i = tid; i < ng * pad * 4; i += nt) {
         const int gl = i / (pad * 4), rem = i % (pad * 4);
@@ -198,13 +221,10 @@ __device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, con
         }
     }
     team.sync();
+    STAGE_MARK(1);
     if (normed) norm_factors_team(team, dtype, M, K, eps, t.rf, t.ssq);  // ends with a barrier
-    for (int c = tid; c < ncols; c += nt) {
-        const int m = c >> 2, p = c & 3;
-        float mx = 0.f;
-        if (m < M) mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
-        t.cs[c] = m < M ? pow2f(row_exp(__float_as_uint(mx)) - 6 - 7 * p) : 0.f;
-    }
+    STAGE_MARK(2);
+    for (int c = tid; c < ncols; c += nt) t.cs[c] = (c >> 2) < M ? pow2f(-6 - 7 * (c & 3)) : 0.f;
 #pragma unroll 1
     for (int c = 0; c < nchunk; ++c) {
         if (nchunk > 1) load_chunk(c);
@@ -215,12 +235,12 @@ __device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, con
                 const int idx = base + lane;
                 const int m = idx < total_l ? idx / upr_l : 0, ul = idx < total_l ? idx % upr_l - u0 : -1;
                 const bool ok = idx < total_l && ul >= 0 && ul < ng * 8;
-                float s = 0.f, inv0 = 0.f;
+                float s = 0.f, pe = 0.f;
                 if (ok) {
                     if (normed) norm8(v[u], nw[u], t.rf[m]);
                     const float mx = normed ? __uint_as_float(t.amax[m]) * t.rf[m] * 1.001f : __uint_as_float(t.amax[m]);
                     const int e = row_exp(__float_as_uint(mx));
-                    inv0 = pow2f(6 - e);
+                    pe = pow2f(e);
                     uint32_t b[4][2];
                     planes8(v[u], e, b);
 #pragma unroll
@@ -234,7 +254,11 @@ __device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, con
                 s += __shfl_xor_sync(0xffffffffu, s, 1);
                 s += __shfl_xor_sync(0xffffffffu, s, 2);
                 s += __shfl_xor_sync(0xffffffffu, s, 4);
-                if (ok && (lane & 7) == 0) t.xs[(ul >> 3) * ncols + 4 * m] = __fmul_rn(s, inv0);
+                if (ok && (lane & 7) == 0) {
+                    const int o = (ul >> 3) * ncols + 4 * m;
+                    t.xs[o] = __fmul_rn(s, 64.0f);
+                    t.xe[o] = t.xe[o + 1] = t.xe[o + 2] = t.xe[o + 3] = pe;
+                }
             }
         }
     }

@@ -155,7 +155,7 @@ struct StackArgs {
     float* h_last;  // [M][H] the last layer's output
     float* act;     // [M][I]
     unsigned* bar;  // control block (zero on entry, left zero)
-    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring;
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring, off_xe;
 };
 
 // Phase A, one 8-group stage, consumer warp (tile t = gate/up, groups 2kp and 2kp + 1): the same
@@ -188,10 +188,12 @@ __device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const 
             mma_s8_16832(cc, a0, xv.x, xv.y);
             mma_s8_16832(ee, a1, xv.z, xv.w);
             const float2 xs = *reinterpret_cast<const float2*>(t.xs + gl * ncols + 8 * j + 2 * tq);
-            y[j][0] = fmaf(sr0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(sr0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(sr1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(sr1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
+            const float xe = t.xe[gl * ncols + 8 * j + 2 * tq];
+            const float s0 = sr0 * xe, s1 = sr1 * xe;
+            y[j][0] = fmaf(s0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
+            y[j][1] = fmaf(s0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
+            y[j][2] = fmaf(s1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
+            y[j][3] = fmaf(s1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
         }
     }
 }
@@ -201,7 +203,8 @@ __device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const 
 // 128-byte swizzle; scales [2 boxes][16 rows][8] at 8 KB, biases likewise at 8.5 KB.
 template <int NTN>
 __device__ __forceinline__ void stack_stage_b(const uint8_t* st, int s, const uint8_t* xqw, const float* xsw,
-                                              int ncols, int warp, int lane, float (&y)[NTN][4]) {
+                                              const float (&pe)[NTN], int ncols, int warp, int lane,
+                                              float (&y)[NTN][4]) {
     const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -225,17 +228,18 @@ __device__ __forceinline__ void stack_stage_b(const uint8_t* st, int s, const ui
             mma_s8_16832(cc, a0, xv.x, xv.y);
             mma_s8_16832(ee, a1, xv.z, xv.w);
             const float2 xs = *reinterpret_cast<const float2*>(xsw + lg * ncols + 8 * j + 2 * tq);
-            y[j][0] = fmaf(sr0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(sr0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(sr1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(sr1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
+            const float s0 = sr0 * pe[j], s1 = sr1 * pe[j];
+            y[j][0] = fmaf(s0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
+            y[j][1] = fmaf(s0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
+            y[j][2] = fmaf(s1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
+            y[j][3] = fmaf(s1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
         }
     }
 }
 
 // Phase B staging by one warp: its 2 * nsb local groups (local group lg = K group
 // 16 (lg >> 1) + 2 warp + (lg & 1)) of the M act rows as s8 planes against row exponents e[m]
-// from the global maxima, with the plane-0 sums / c_m.  Same byte layout as stage_x_i8_team.
+// from the global maxima, with 64 x the plane-0 sums.  Same byte layout as stage_x_i8_team.
 __device__ __forceinline__ void stage_b_warp(const float* act, int I, int M, int ncols, int nsb, int warp, int lane,
                                              const int (&e)[kStackMaxRows], uint8_t* xqw, float* xsw) {
     const int nlg = 2 * nsb;
@@ -285,7 +289,7 @@ __device__ __forceinline__ void stage_b_warp(const float* act, int I, int M, int
                 s += __shfl_xor_sync(0xffffffffu, s, 1);
                 s += __shfl_xor_sync(0xffffffffu, s, 2);
                 s += __shfl_xor_sync(0xffffffffu, s, 4);
-                if (un == 0) xsw[lg * ncols + 4 * m] = __fmul_rn(s, pow2f(6 - em));
+                if (un == 0) xsw[lg * ncols + 4 * m] = __fmul_rn(s, 64.0f);
             }
         }
     }
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
     uint8_t* ring = smem + a.off_ring;
     I8X tx{smem + a.off_xq, reinterpret_cast<float*>(smem + a.off_xs), reinterpret_cast<float*>(smem + a.off_cs),
            reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
-           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64)};
+           reinterpret_cast<unsigned int*>(smem + a.off_misc + 64), reinterpret_cast<float*>(smem + a.off_xe)};
     const int spa = a.GA / kSAGroups;  // stages per phase-A item
     const int nsb = a.nsb;             // stages per phase-B item
     const int na = a.items_a > cta ? (a.items_a - 1 - cta) / nb + 1 : 0;
@@ -502,12 +506,19 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
                 float* xsw = tx.xs + (size_t)warp * (2 * nsb) * ncols;
                 stage_b_warp(a.act, I, M, ncols, nsb, warp, lane, e, xqw, xsw);
                 STACK_MARK(l, 5);
-                float yb[NTN][4];
+                float yb[NTN][4], pe[NTN];
 #pragma unroll
-                for (int j = 0; j < NTN; ++j) yb[j][0] = yb[j][1] = yb[j][2] = yb[j][3] = 0.f;
+                for (int j = 0; j < NTN; ++j) {
+                    yb[j][0] = yb[j][1] = yb[j][2] = yb[j][3] = 0.f;
+                    const int m = 2 * j + (tq >> 1);
+                    int em = e[0];
+#pragma unroll
+                    for (int r = 1; r < kStackMaxRows; ++r) em = m == r ? e[r] : em;
+                    pe[j] = m < M ? pow2f(em) : 0.f;
+                }
                 for (int s = 0; s < nsb; ++s) {
                     const uint8_t* st = wait_stage();
-                    if (st) stack_stage_b<NTN>(st, s, xqw, xsw, ncols, warp, lane, yb);
+                    if (st) stack_stage_b<NTN>(st, s, xqw, xsw, pe, ncols, warp, lane, yb);
 #pragma unroll
                     for (int j = 0; j < NTN; ++j) hold_regs(yb[j]);
                     release_stage();
@@ -516,12 +527,9 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
                     const int m = 2 * j + (tq >> 1);
-                    int em = e[0];
-#pragma unroll
-                    for (int r = 1; r < kStackMaxRows; ++r) em = m == r ? e[r] : em;
                     const int p = 2 * (tq & 1);
-                    const float cx = m < M ? pow2f(em - 6 - 7 * p) : 0.f;
-                    const float cy = m < M ? pow2f(em - 13 - 7 * p) : 0.f;
+                    const float cx = m < M ? pow2f(-6 - 7 * p) : 0.f;
+                    const float cy = m < M ? pow2f(-13 - 7 * p) : 0.f;
                     float p0 = fmaf(cx, yb[j][0], cy * yb[j][1]);
                     float p1 = fmaf(cx, yb[j][2], cy * yb[j][3]);
                     p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
@@ -567,7 +575,7 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
 // Shared-memory plan of one launch; false when it does not fit.
 struct StackPlan {
     int ntn, ncols, S;
-    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring, smem;
+    uint32_t off_bar, off_misc, off_scr, off_xs, off_cs, off_xq, off_red, off_ring, off_xe, smem;
 };
 
 bool stack_plan(int64_t m, int64_t hidden, int64_t inter, StackPlan& p) {
@@ -587,6 +595,7 @@ bool stack_plan(int64_t m, int64_t hidden, int64_t inter, StackPlan& p) {
     p.off_scr = take((64 + (uint32_t)m * (uint32_t)(hidden / 8)) * 4, 16);
     p.off_cs = take(p.ncols * 4, 16);
     p.off_xs = take(std::max(GA, kSCons * nlg) * p.ncols * 4, 16);
+    p.off_xe = take(GA * p.ncols * 4, 16);
     p.off_xq = take(std::max(GA, kSCons * nlg) * p.ncols * 64, 128);
     p.off_red = take(std::max<uint32_t>(4 * kSAItems * 32, kSCons * 16) * MS * 4, 16);
     off = (off + 1023) / 1024 * 1024;
@@ -654,6 +663,7 @@ cudaError_t launch_stack(const StackLaunch& L, cudaStream_t stream) {
     a.off_xq = p.off_xq;
     a.off_red = p.off_red;
     a.off_ring = p.off_ring;
+    a.off_xe = p.off_xe;
     const int grid = device_num_sms();
 
     auto go = [&](auto kernel) -> cudaError_t {
