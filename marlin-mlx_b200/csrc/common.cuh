@@ -283,6 +283,13 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 //   a0: row g, k 4t..4t+3;  a1: row g+8, k 4t..4t+3;  a2: row g, k 16+4t..;  a3: row g+8, k 16+4t..
 //   b0: column g, k 4t..4t+3;  b1: column g, k 16+4t..
 //   d0, d1: row g, columns 2t, 2t+1;  d2, d3: row g+8, columns 2t, 2t+1.
+// As mma_s8_16832 with the A operand unsigned bytes (0..255).
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])

@@ -61,7 +61,7 @@ constexpr uint32_t kI8TwoPerSm = 110 * 1024;          // two CTAs per SM (PDL ov
 // ------------------------------------------------------------------------------------------------
 template <int NTN, int ROWS = kI8Rows>
 __device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int ncols, int warp,
-                                         int lane, float (&y)[NTN][4]) {
+                                         int lane, float (&y)[NTN][4], float (&yb)[NTN][2]) {
     // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * warp + g, r1 = r0 + 8;
@@ -80,23 +80,13 @@ __device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, con
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        const uint32_t a0[4] = {wa[q].x & kNib, wb[q].x & kNib, (wa[q].x >> 4) & kNib, (wb[q].x >> 4) & kNib};
-        const uint32_t a1[4] = {wa[q].y & kNib, wb[q].y & kNib, (wa[q].y >> 4) & kNib, (wb[q].y >> 4) & kNib};
         const float sr0 = sel_bf16(s0, q), sr1 = sel_bf16(s1, q), br0 = sel_bf16(b0, q), br1 = sel_bf16(b1, q);
         const int gl = gl0 + q;
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
             const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
-            int c[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};  // the two K-steps accumulate independently
-            mma_s8_16832(c, a0, xv.x, xv.y);
-            mma_s8_16832(e, a1, xv.z, xv.w);
-            const float2 xs = *reinterpret_cast<const float2*>(t.xs + gl * ncols + 8 * j + 2 * tq);
-            const float xe = t.xe[gl * ncols + 8 * j + 2 * tq];  // both columns belong to one row
-            const float s0 = sr0 * xe, s1 = sr1 * xe;
-            y[j][0] = fmaf(s0, (float)(c[0] + e[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(s0, (float)(c[1] + e[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(s1, (float)(c[2] + e[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(s1, (float)(c[3] + e[3]), fmaf(br1, xs.y, y[j][3]));
+            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);  // plane-0 column of the lane's row
+            i8_group(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
         }
     }
 }
@@ -127,7 +117,7 @@ __device__ __forceinline__ void copy_planes_in(const XPlanes& P, int g0, int ng,
 // r_m = 1/sqrt(sum(ssq blocks) / K + eps) (binary32, blocks summed in order).
 __device__ __forceinline__ void planes_factors(const XPlanes& P, const uint16_t* norm_w, float eps, int M, int K,
                                                int ncols, const I8X& t) {
-    for (int c = threadIdx.x; c < ncols; c += blockDim.x) t.cs[c] = (c >> 2) < M ? pow2f(-6 - 7 * (c & 3)) : 0.f;
+    for (int c = threadIdx.x; c < ncols; c += blockDim.x) t.cs[c] = (c >> 2) < M ? pow2f(-10 - 7 * (c & 3)) : 0.f;
     if (norm_w && (int)threadIdx.x < M) {
         float s = 0.f;
         for (int b = 0; b < P.nssq; ++b) s = __fadd_rn(s, P.ssq[(size_t)b * M + threadIdx.x]);
@@ -298,9 +288,9 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
     }
     I8_MARK(3);
 
-    float y[NTN][4];
+    float y[NTN][4], yb[NTN][2];
 #pragma unroll
-    for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+    for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
     if (warp == kI8Warps) {
         if (lane == 0) {
             int q = min(S, nst);
@@ -318,9 +308,12 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
             I8_STAGE_MARK(q);
             const int gs = g0 + q * kI8StageGroups;
             i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, ncols, warp,
-                          lane, y);
+                          lane, y, yb);
 #pragma unroll
-            for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
+            for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
+                hold_regs(y[j]);
+                hold_regs(yb[j]);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q % S]);
         }
@@ -330,10 +323,8 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
             const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
-            float p0 = fmaf(cv.x, y[j][0], cv.y * y[j][1]);
-            float p1 = fmaf(cv.x, y[j][2], cv.y * y[j][3]);
-            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+            const float2 pp = i8_combine(y[j], yb[j], cv, tq);
+            const float p0 = pp.x, p1 = pp.y;
             const int m = 2 * j + (tq >> 1);
             if ((tq & 1) == 0 && m < M) {
                 float* s0 = red + ((size_t)rank * kI8Rows + r0) * MS + m;
@@ -532,19 +523,23 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
         const bool bf16_logits = L.x_dtype == kBF16 && !L.norm_w && !L.has_xin;
         const bool row_factor = L.has_xin && L.norm_w;
         const bool xin_ok = !L.has_xin || warp_wait(xbar, 0u, abort);
-        float y[NTN][4];
+        float y[NTN][4], yb[NTN][2];
         unsigned long long best[NTN];
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
-            y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+            y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
             best[j] = 0ull;
         }
         for (int q = 0; xin_ok && q < nst; ++q) {
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             const int sp = q % spb, gs = sp * kI8StageGroups;
-            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y);
+            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y,
+                                     yb);
 #pragma unroll
-            for (int j = 0; j < NTN; ++j) hold_regs(y[j]);  // the stage's data is consumed before release
+            for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
+                hold_regs(y[j]);
+                hold_regs(yb[j]);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q % S]);
             if (sp == spb - 1) {  // block finished: logits -> argmax keys (max over the warp's rows)
@@ -553,10 +548,8 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
                     const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
-                    float la = fmaf(cv.x, y[j][0], cv.y * y[j][1]);
-                    float lb = fmaf(cv.x, y[j][2], cv.y * y[j][3]);
-                    la += __shfl_xor_sync(0xffffffffu, la, 1);
-                    lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+                    const float2 ll = i8_combine(y[j], yb[j], cv, tq);
+                    float la = ll.x, lb = ll.y;
                     if (row_factor) {
                         const float rfm = tx.rf[min(2 * j + (tq >> 1), M - 1)];
                         la *= rfm;
@@ -577,7 +570,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
                         ka = other > ka ? other : ka;
                     }
                     best[j] = ka > best[j] ? ka : best[j];
-                    y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
+                    y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
                 }
             }
         }

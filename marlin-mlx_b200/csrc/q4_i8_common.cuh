@@ -56,11 +56,13 @@ __device__ void norm_factors_team(Team& team, int dtype, int M, int K, float eps
 // ------------------------------------------------------------------------------------------------
 //
 // Fold.  With e the exponent of a group's planes (|x| < 2^e), x = 2^(e-6) sum_p 128^-p i_p, so per
-// weight row and 64-group, s * sum(q x) + b * sum(x) = 2^-6 sum_p 128^-p (s 2^e D_p) + b sum(x):
-// the kernels accumulate Y_p += (s * xe) * D_p + b * xs (xs = 64 sum(x) on plane-0 columns, 0 on
-// the others) and combine the planes once per output with cs = 2^(-6-7p).  Every scaling is by a
-// power of two, so the exponent may vary per group (planes written by the producing kernel) or be
-// one per row (planes staged here) with the same arithmetic.
+// weight row and 64-group, s * sum(q x) + b * sum(x) = 2^-6 sum_p 128^-p (s 2^e D_p) + b sum(x).
+// The codes enter two MMAs without shifting: the even elements as q (w & 0x0F0F0F0F) and the odd
+// ones as 16 q (w & 0xF0F0F0F0, unsigned bytes), so 16 D_p = 16 D_even + D_odd' exactly.  The
+// kernels accumulate Y_p += (s * xe) * 16 D_p and, per row, Yb += b * xs (xs = 64 sum(x), held on
+// the plane-0 columns), and combine once per output: sum_p cs_p Y_p + 2^-6 Yb with
+// cs = 2^(-10-7p).  Every scaling is by a power of two, so the exponent may vary per group (planes
+// written by the producing kernel) or be one per row (planes staged here) with the same arithmetic.
 struct I8X {
     uint8_t* xq;          // [ng][ncols][64]
     float* xs;            // [ng][ncols]: plane-0 columns hold 64 sum_g(x), the others 0
@@ -70,6 +72,37 @@ struct I8X {
     unsigned int* amax;   // [M] max |x| (binary32 bits) over the staged range
     float* xe;            // [ng][ncols]: 2^e of the group's planes (0 for padding columns)
 };
+
+// One 64-group of a warp's 16-row weight tile against activation column tile j (see Fold): wa, wb
+// the lane's packed words 2t, 2t + 1 of rows g and g + 8; xv the lane's 16 plane bytes (elements
+// 16t..16t+15 of column g, evens then odds per 8); sr/br the rows' scales and biases; xe and x0
+// the group's 2^e and 64 sum(x) for the lane's activation row.  y: rows g, g+8 x columns 2t, 2t+1.
+__device__ __forceinline__ void i8_group(uint2 wa, uint2 wb, uint4 xv, float sr0, float sr1, float br0, float br1,
+                                         float xe, float x0, float (&y)[4], float (&yb)[2]) {
+    const uint32_t lo[4] = {wa.x & kNib, wb.x & kNib, wa.y & kNib, wb.y & kNib};
+    const uint32_t hi[4] = {wa.x & ~kNib, wb.x & ~kNib, wa.y & ~kNib, wb.y & ~kNib};
+    int c[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
+    mma_u8s8_16832(c, lo, xv.x, xv.z);  // even elements
+    mma_u8s8_16832(e, hi, xv.y, xv.w);  // odd elements, times 16
+    const float s0 = sr0 * xe, s1 = sr1 * xe;
+    y[0] = fmaf(s0, (float)(16 * c[0] + e[0]), y[0]);
+    y[1] = fmaf(s0, (float)(16 * c[1] + e[1]), y[1]);
+    y[2] = fmaf(s1, (float)(16 * c[2] + e[2]), y[2]);
+    y[3] = fmaf(s1, (float)(16 * c[3] + e[3]), y[3]);
+    yb[0] = fmaf(br0, x0, yb[0]);
+    yb[1] = fmaf(br1, x0, yb[1]);
+}
+
+// The outputs of a lane after the K loop: rows g (.x) and g + 8 (.y) of activation row
+// m = 2j + (t >> 1), summed over the lane pair (t, t ^ 1) that holds the row's four planes.
+__device__ __forceinline__ float2 i8_combine(const float (&y)[4], const float (&yb)[2], float2 cv, int tq) {
+    const float bw = (tq & 1) ? 0.f : 0.015625f;  // 2^-6 Yb, added once per pair
+    float p0 = fmaf(bw, yb[0], fmaf(cv.x, y[0], cv.y * y[1]));
+    float p1 = fmaf(bw, yb[1], fmaf(cv.x, y[2], cv.y * y[3]));
+    p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+    p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+    return make_float2(p0, p1);
+}
 
 // byte offset of element k (0..63) of a group in its 64-byte plane row (B-fragment order)
 __device__ __forceinline__ int plane_pos(int k) {
@@ -224,7 +257,7 @@ __device__ void stage_x_i8_team(Team& team, const void* x, int dtype, int K, con
     STAGE_MARK(1);
     if (normed) norm_factors_team(team, dtype, M, K, eps, t.rf, t.ssq);  // ends with a barrier
     STAGE_MARK(2);
-    for (int c = tid; c < ncols; c += nt) t.cs[c] = (c >> 2) < M ? pow2f(-6 - 7 * (c & 3)) : 0.f;
+    for (int c = tid; c < ncols; c += nt) t.cs[c] = (c >> 2) < M ? pow2f(-10 - 7 * (c & 3)) : 0.f;
 #pragma unroll 1
     for (int c = 0; c < nchunk; ++c) {
         if (nchunk > 1) load_chunk(c);

@@ -164,7 +164,7 @@ struct StackArgs {
 // per row with 128-byte swizzle; scales [32 rows][8] at 8 KB, biases [32 rows][8] at 8.5 KB.
 template <int NTN>
 __device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const I8X& t, int ncols, int tile, int kp,
-                                              int lane, float (&y)[NTN][4]) {
+                                              int lane, float (&y)[NTN][4], float (&yb)[NTN][2]) {
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * tile + g, r1 = r0 + 8;
 #pragma unroll
@@ -178,22 +178,12 @@ __device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const 
         const float sr1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + r1 * 16 + 2 * q));
         const float br0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + r0 * 16 + 2 * q));
         const float br1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + r1 * 16 + 2 * q));
-        const uint32_t a0[4] = {wa.x & kNib, wb.x & kNib, (wa.x >> 4) & kNib, (wb.x >> 4) & kNib};
-        const uint32_t a1[4] = {wa.y & kNib, wb.y & kNib, (wa.y >> 4) & kNib, (wb.y >> 4) & kNib};
         const int gl = gl0 + q;
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
             const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
-            int cc[4] = {0, 0, 0, 0}, ee[4] = {0, 0, 0, 0};
-            mma_s8_16832(cc, a0, xv.x, xv.y);
-            mma_s8_16832(ee, a1, xv.z, xv.w);
-            const float2 xs = *reinterpret_cast<const float2*>(t.xs + gl * ncols + 8 * j + 2 * tq);
-            const float xe = t.xe[gl * ncols + 8 * j + 2 * tq];
-            const float s0 = sr0 * xe, s1 = sr1 * xe;
-            y[j][0] = fmaf(s0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(s0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(s1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(s1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
+            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);
+            i8_group(wa, wb, xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
         }
     }
 }
@@ -204,7 +194,7 @@ __device__ __forceinline__ void stack_stage_a(const uint8_t* st, int gl0, const 
 template <int NTN>
 __device__ __forceinline__ void stack_stage_b(const uint8_t* st, int s, const uint8_t* xqw, const float* xsw,
                                               const float (&pe)[NTN], int ncols, int warp, int lane,
-                                              float (&y)[NTN][4]) {
+                                              float (&y)[NTN][4], float (&yb)[NTN][2]) {
     const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -218,21 +208,11 @@ __device__ __forceinline__ void stack_stage_b(const uint8_t* st, int s, const ui
         const float sr1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + so + (g + 8) * 16));
         const float br0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + so + g * 16));
         const float br1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(st + kSPacked + 512 + so + (g + 8) * 16));
-        const uint32_t a0[4] = {wa.x & kNib, wb.x & kNib, (wa.x >> 4) & kNib, (wb.x >> 4) & kNib};
-        const uint32_t a1[4] = {wa.y & kNib, wb.y & kNib, (wa.y >> 4) & kNib, (wb.y >> 4) & kNib};
         const int lg = 2 * s + e;
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
             const uint4 xv = *reinterpret_cast<const uint4*>(xqw + ((size_t)(lg * ncols + 8 * j + g) * 64 + 16 * tq));
-            int cc[4] = {0, 0, 0, 0}, ee[4] = {0, 0, 0, 0};
-            mma_s8_16832(cc, a0, xv.x, xv.y);
-            mma_s8_16832(ee, a1, xv.z, xv.w);
-            const float2 xs = *reinterpret_cast<const float2*>(xsw + lg * ncols + 8 * j + 2 * tq);
-            const float s0 = sr0 * pe[j], s1 = sr1 * pe[j];
-            y[j][0] = fmaf(s0, (float)(cc[0] + ee[0]), fmaf(br0, xs.x, y[j][0]));
-            y[j][1] = fmaf(s0, (float)(cc[1] + ee[1]), fmaf(br0, xs.y, y[j][1]));
-            y[j][2] = fmaf(s1, (float)(cc[2] + ee[2]), fmaf(br1, xs.x, y[j][2]));
-            y[j][3] = fmaf(s1, (float)(cc[3] + ee[3]), fmaf(br1, xs.y, y[j][3]));
+            i8_group(wa, wb, xv, sr0, sr1, br0, br1, pe[j], xsw[lg * ncols + 8 * j + 4 * (tq >> 1)], y[j], yb[j]);
         }
     }
 }
@@ -428,19 +408,23 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
             // ---- phase A: x = RMSNorm(h) as s8 planes, then all of this CTA's 16-feature items
             stage_x_i8_team(team, hin, hin_dtype, H, a.norm_w[l], a.eps, 0, a.GA, M, ncols, tx);
             STACK_MARK(l, 1);
-            float y[kSAItems][NTN][4];
+            float y[kSAItems][NTN][4], ya[kSAItems][NTN][2];
 #pragma unroll
             for (int i = 0; i < kSAItems; ++i)
 #pragma unroll
-                for (int j = 0; j < NTN; ++j) y[i][j][0] = y[i][j][1] = y[i][j][2] = y[i][j][3] = 0.f;
+                for (int j = 0; j < NTN; ++j)
+                    y[i][j][0] = y[i][j][1] = y[i][j][2] = y[i][j][3] = ya[i][j][0] = ya[i][j][1] = 0.f;
 #pragma unroll
             for (int i = 0; i < kSAItems; ++i) {
                 if (i < na) {
                     for (int s = 0; s < spa; ++s) {
                         const uint8_t* st = wait_stage();
-                        if (st) stack_stage_a<NTN>(st, kSAGroups * s, tx, ncols, tile, kp, lane, y[i]);
+                        if (st) stack_stage_a<NTN>(st, kSAGroups * s, tx, ncols, tile, kp, lane, y[i], ya[i]);
 #pragma unroll
-                        for (int j = 0; j < NTN; ++j) hold_regs(y[i][j]);  // consumed before release
+                        for (int j = 0; j < NTN; ++j) {  // consumed before release
+                            hold_regs(y[i][j]);
+                            hold_regs(ya[i][j]);
+                        }
                         release_stage();
                     }
                 }
@@ -453,10 +437,8 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
 #pragma unroll
                     for (int j = 0; j < NTN; ++j) {
                         const float2 cv = *reinterpret_cast<const float2*>(tx.cs + 8 * j + 2 * tq);
-                        float p0 = fmaf(cv.x, y[i][j][0], cv.y * y[i][j][1]);
-                        float p1 = fmaf(cv.x, y[i][j][2], cv.y * y[i][j][3]);
-                        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-                        p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+                        const float2 pp = i8_combine(y[i][j], ya[i][j], cv, tq);
+                        const float p0 = pp.x, p1 = pp.y;
                         const int m = 2 * j + (tq >> 1);
                         if ((tq & 1) == 0 && m < M) {
                             float* r = red + ((size_t)(kp * kSAItems + i) * 32 + 16 * tile + g) * MS + m;
@@ -506,10 +488,10 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
                 float* xsw = tx.xs + (size_t)warp * (2 * nsb) * ncols;
                 stage_b_warp(a.act, I, M, ncols, nsb, warp, lane, e, xqw, xsw);
                 STACK_MARK(l, 5);
-                float yb[NTN][4], pe[NTN];
+                float yb[NTN][4], ybb[NTN][2], pe[NTN];
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
-                    yb[j][0] = yb[j][1] = yb[j][2] = yb[j][3] = 0.f;
+                    yb[j][0] = yb[j][1] = yb[j][2] = yb[j][3] = ybb[j][0] = ybb[j][1] = 0.f;
                     const int m = 2 * j + (tq >> 1);
                     int em = e[0];
 #pragma unroll
@@ -518,9 +500,12 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
                 }
                 for (int s = 0; s < nsb; ++s) {
                     const uint8_t* st = wait_stage();
-                    if (st) stack_stage_b<NTN>(st, s, xqw, xsw, pe, ncols, warp, lane, yb);
+                    if (st) stack_stage_b<NTN>(st, s, xqw, xsw, pe, ncols, warp, lane, yb, ybb);
 #pragma unroll
-                    for (int j = 0; j < NTN; ++j) hold_regs(yb[j]);
+                    for (int j = 0; j < NTN; ++j) {
+                        hold_regs(yb[j]);
+                        hold_regs(ybb[j]);
+                    }
                     release_stage();
                 }
                 STACK_MARK(l, 6);
@@ -528,12 +513,10 @@ __global__ void __launch_bounds__(kSThreads, 1) q4_stack_kernel(const __grid_con
                 for (int j = 0; j < NTN; ++j) {
                     const int m = 2 * j + (tq >> 1);
                     const int p = 2 * (tq & 1);
-                    const float cx = m < M ? pow2f(-6 - 7 * p) : 0.f;
-                    const float cy = m < M ? pow2f(-13 - 7 * p) : 0.f;
-                    float p0 = fmaf(cx, yb[j][0], cy * yb[j][1]);
-                    float p1 = fmaf(cx, yb[j][2], cy * yb[j][3]);
-                    p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-                    p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+                    const float cx = m < M ? pow2f(-10 - 7 * p) : 0.f;
+                    const float cy = m < M ? pow2f(-17 - 7 * p) : 0.f;
+                    const float2 pp = i8_combine(yb[j], ybb[j], make_float2(cx, cy), tq);
+                    const float p0 = pp.x, p1 = pp.y;
                     if ((tq & 1) == 0 && m < M) {
                         red[((size_t)warp * 16 + g) * MS + m] = p0;
                         red[((size_t)warp * 16 + g + 8) * MS + m] = p1;
