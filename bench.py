@@ -6,8 +6,9 @@
 Workload (the metric's decode tokens/s): one greedy decode step = 24 x [RMSNorm
 (1+w) -> Q4 SwiGLU MLP 2048<->6144 -> residual] -> final RMSNorm -> Q4 lm_head 248320x2048 -> argmax,
 seeded synthetic weights (N(0,0.02) via the seeded generator) and embeddings (N(0,1)), batch B
-(default 1).  At N > 1 the step is tensor-parallel (column/row-split MLP + NCCL all-reduce per
-layer, vocabulary-sharded lm_head with a max-merge of packed keys): strong scaling.
+(default 1).  At N > 1 the step is tensor-parallel (column/row-split MLP, vocabulary-sharded
+lm_head): the per-layer all-reduce and the argmax merge run inside the kernels over NVLink peer
+memory (marlin_q4_tp_decode_step): strong scaling.
 
 `value` is tokens/s of the whole job from CUDA events around K CUDA-graph replays (weights stream
 795.7 MB per step, > 126 MB L2: every step reads HBM).  `e2e` repeats the measurement through the
@@ -128,7 +129,7 @@ def build_model(mq, tp_rank: int, tp: int):
         d = mq.quantize_weight(mq.synth_bf16((H, I), 1002 + 4 * l, 0.0, 0.02))
         nw = mq.synth_bf16((H,), 1003 + 4 * l, 0.1, 0.02)
         layer = mq.Layer(nw, g, u, d)
-        layers.append(tpmod.shard_layer(layer, tp_rank, tp) if tp > 1 else layer)
+        layers.append(tpmod.shard_layer(layer, tp_rank, tp, k_multiple=512) if tp > 1 else layer)
     lm = mq.quantize_weight(mq.synth_bf16((V, H), 2000, 0.0, 0.02))
     off = 0
     if tp > 1:
@@ -187,7 +188,8 @@ def run_ours(args):
     h0 = mq.synth_bf16((B, H), 3000, 0.0, 1.0)
 
     if world > 1:
-        step = tpmod.TPDecodeStep(layers, fn, lm, off, B)
+        # exchanges inside the kernels over NVLink peer memory (no collective call per step)
+        step = tpmod.FusedTPDecodeStep(layers, fn, lm, off, B)
     else:
         step = mq.DecodeStep(layers, fn, lm, B)
 
@@ -383,7 +385,7 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_baseline_from_device(layers, fn, lm, h0, B, args.cpu_seconds)
 
-    launches = args.steps * (2 * L + 1) if world == 1 else args.steps * (3 * L + 3)
+    launches = args.steps * (2 * L + 1)  # per step: gate/up and down per layer, then the lm_head
     line = {
         "metric": "Q4 MLP+lm_head decode tokens/s (24-layer Q4 SwiGLU MLP stack + Q4 lm_head + argmax)",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -413,6 +415,7 @@ def run_ours(args):
     if extras:
         line["extras"] = extras
     if world > 1:
+        step.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

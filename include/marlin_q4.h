@@ -183,12 +183,40 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
  * persistent cooperative kernel (all SMs, software grid barriers between the gate/up and down
  * phases of each layer) before the lm_head kernel.
  * workspace: >= marlin_q4_decode_step_workspace_size bytes, 256-byte aligned, zero-filled before
- * the first call (its head is left zeroed by every call). */
+ * the first call (its head is left zeroed by every call); one workspace serves one (m, hidden,
+ * intermediate) shape; zero it again before using it for another. */
 int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
                           const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
                           const marlin_q4_tensor* lm, int32_t* ids, float* best, float* h_out,
                           void* workspace, size_t workspace_bytes, void* stream);
 size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate);
+
+/* ---- tensor-parallel decode step (no counterpart in the reference, which runs on one device) -----
+ * The decode step of marlin_q4_decode_step over weights sharded across tp_size GPUs of one box, one
+ * process per GPU: gate_proj/up_proj split by output rows, down_proj by input columns (its K may
+ * carry zero padding up to a multiple of 512 beyond the rank's gate/up rows: zero codes, scales and
+ * biases), the lm_head by vocabulary rows starting at vocab_offset.  The per-layer all-reduce of
+ * the down_proj partial rows and the argmax merge happen inside the kernels over NVLink: every rank
+ * stores its partial rows and keys into every rank's exchange buffer and waits (bounded, about 2 s,
+ * then records a device error) for the others' flags; sums run in rank order, so every rank holds
+ * the same h and ids.  exchange[r]: rank r's exchange buffer as mapped in this process (the own one
+ * from marlin_q4_device_alloc, the others from marlin_q4_ipc_open_handle), each
+ * marlin_q4_tp_exchange_size bytes, zero before the first call and left zero.  All ranks must call
+ * the step the same number of times.  m <= 16, hidden a multiple of 512, down_proj K a multiple of
+ * 512.  workspace as for marlin_q4_decode_step with intermediate = down_proj K. */
+int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
+                             const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
+                             const marlin_q4_tensor* lm_shard, int64_t vocab_offset, int32_t* ids, float* best,
+                             float* h_out, int32_t tp_rank, int32_t tp_size, void* const* exchange, void* workspace,
+                             size_t workspace_bytes, void* stream);
+size_t marlin_q4_tp_exchange_size(int64_t m, int64_t hidden, int32_t tp);
+/* Zero-filled device memory for an exchange buffer (cudaMalloc: its IPC handle covers exactly it). */
+int marlin_q4_device_alloc(size_t bytes, void** ptr);
+int marlin_q4_device_free(void* ptr);
+/* CUDA IPC of an exchange buffer between the ranks' processes: handle = 64 bytes. */
+int marlin_q4_ipc_get_handle(const void* ptr, void* handle);
+int marlin_q4_ipc_open_handle(const void* handle, void** ptr);
+int marlin_q4_ipc_close_handle(void* ptr);
 
 /* ---- synthetic inputs (benchmark / test support; no counterpart in the reference) ----------------
  * out[i] = bf16(mean + sigma * z_i), z_i a seeded Irwin-Hall(12) variate (mean 0, sd 1), the same

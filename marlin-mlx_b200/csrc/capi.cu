@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 
 namespace marlin {
 namespace {
@@ -297,10 +298,30 @@ size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
 // The decode step on the integer-MMA kernels with the activations handed over as planes: each
 // kernel's epilogue writes the next kernel's operand (act planes; h * (1 + next norm weight) planes
 // with per-block sums of squares), so only the first gate/up launch stages from h0.
+// Exchange buffer of the tensor-parallel step (TpExchange), per rank.
+struct TpLayout {
+    size_t part, flag, keys, kflag, total;
+};
+TpLayout tp_layout(int64_t m, int64_t hidden, int tp) {
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    TpLayout t{};
+    size_t off = 0;
+    t.part = off;
+    off += al((size_t)2 * tp * m * hidden * 4);
+    t.flag = off;
+    off += al((size_t)2 * (hidden / 128) * tp * 4);
+    t.keys = off;
+    off += al((size_t)tp * m * 8);
+    t.kflag = off;
+    off += al((size_t)tp * 4);
+    t.total = off;
+    return t;
+}
+
 int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t inter, int32_t n_layers,
                        const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
                        const marlin_q4_tensor* lm, int32_t* ids, float* best, float* h, uint8_t* scratch,
-                       void* lmws, cudaStream_t st) {
+                       void* lmws, cudaStream_t st, const TpExchange* tpx = nullptr, int64_t vocab_offset = 0) {
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     uint8_t* pl = scratch + (align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4) + 255) / 256 * 256;
     const XPlanes ap = i8_planes_at(pl, m, inter, nullptr, 0);
@@ -348,6 +369,10 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
         D.has_xout = true;
         D.xout = hp;
         D.out_norm = l + 1 < n_layers ? layers[l + 1].post_attn_norm : final_norm;
+        if (tpx) {
+            D.tp = *tpx;
+            D.tp.parity = l & 1;
+        }
         if ((rc = cuda_status(launch_i8_gemv(D, st)))) return rc;
         cur = h;
         cur_dtype = MARLIN_Q4_F32;
@@ -366,6 +391,8 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
     Lh.pdl = g_pdl;
     Lh.has_xin = true;
     Lh.xin = hp;
+    Lh.vocab_offset = vocab_offset;
+    if (tpx) Lh.tp = *tpx;
     return cuda_status(launch_i8_lm_head(Lh, st));
 }
 }  // namespace
@@ -449,6 +476,94 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     }
     return marlin_q4_lm_head_argmax(cur, cur_dtype, m, final_norm, eps, lm, 0, ids, best, nullptr, lmws,
                                     marlin_q4_lm_head_workspace_size(m), st);
+}
+
+// ---- tensor-parallel decode step ------------------------------------------------------------------
+size_t marlin_q4_tp_exchange_size(int64_t m, int64_t hidden, int32_t tp) {
+    if (m <= 0 || hidden <= 0 || tp < 1) return 0;
+    return tp_layout(m, hidden, tp).total;
+}
+
+int marlin_q4_device_alloc(size_t bytes, void** ptr) {
+    if (!ptr || !bytes) return MARLIN_Q4_ERR_ARG;
+    *ptr = nullptr;
+    if (cudaMalloc(ptr, bytes) != cudaSuccess) return cuda_status(cudaErrorMemoryAllocation);
+    if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return MARLIN_Q4_ERR_CUDA;
+    }
+    return MARLIN_Q4_OK;
+}
+
+int marlin_q4_device_free(void* ptr) { return cuda_status(cudaFree(ptr)); }
+
+int marlin_q4_ipc_get_handle(const void* ptr, void* handle) {
+    if (!ptr || !handle) return MARLIN_Q4_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return cuda_status(e);
+    std::memcpy(handle, &h, sizeof(h));
+    return MARLIN_Q4_OK;
+}
+
+int marlin_q4_ipc_open_handle(const void* handle, void** ptr) {
+    if (!handle || !ptr) return MARLIN_Q4_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int marlin_q4_ipc_close_handle(void* ptr) { return cuda_status(cudaIpcCloseMemHandle(ptr)); }
+
+int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
+                             const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
+                             const marlin_q4_tensor* lm_shard, int64_t vocab_offset, int32_t* ids, float* best,
+                             float* h_out, int32_t tp_rank, int32_t tp_size, void* const* exchange, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    int rc;
+    if (!h0 || m <= 0 || hidden <= 0 || n_layers < 1 || !layers || !final_norm || !ids || !exchange)
+        return MARLIN_Q4_ERR_ARG;
+    if (tp_size < 1 || tp_size > kTpMax || tp_rank < 0 || tp_rank >= tp_size || vocab_offset < 0)
+        return MARLIN_Q4_ERR_ARG;
+    if (!aligned(h0, 16) || !aligned(final_norm, 16) || (h_out && !aligned(h_out, 16))) return MARLIN_Q4_ERR_ALIGN;
+    if ((rc = check_tensor(lm_shard))) return rc;
+    if (lm_shard->k != hidden || vocab_offset + lm_shard->n > 0xffffffffLL) return MARLIN_Q4_ERR_SHAPE;
+    // the down shard may carry zero K padding beyond its gate/up rows (its K a multiple of 512)
+    const int64_t inter = layers[0].down_proj.k;
+    for (int32_t l = 0; l < n_layers; ++l) {
+        const marlin_q4_layer& L = layers[l];
+        if (!L.post_attn_norm) return MARLIN_Q4_ERR_ARG;
+        if (!aligned(L.post_attn_norm, 16)) return MARLIN_Q4_ERR_ALIGN;
+        if ((rc = check_tensor(&L.gate_proj)) || (rc = check_tensor(&L.up_proj)) || (rc = check_tensor(&L.down_proj)))
+            return rc;
+        if (L.gate_proj.k != hidden || L.up_proj.k != hidden || L.up_proj.n != L.gate_proj.n ||
+            L.down_proj.n != hidden || L.down_proj.k != inter || L.gate_proj.n > inter || L.gate_proj.n % 64)
+            return MARLIN_Q4_ERR_SHAPE;
+    }
+    if (m > kI8MaxRows || hidden % 128 || !i8_supported(hidden, m) || !i8_supported(inter, m))
+        return MARLIN_Q4_ERR_UNSUPPORTED;
+    if (!workspace || !aligned(workspace, 256) ||
+        workspace_bytes < marlin_q4_decode_step_workspace_size(m, hidden, inter))
+        return MARLIN_Q4_ERR_WORKSPACE;
+    const TpLayout lay = tp_layout(m, hidden, tp_size);
+    TpExchange X{};
+    X.tp = tp_size;
+    X.rank = tp_rank;
+    X.nblk = (int)(hidden / 128);
+    for (int r = 0; r < tp_size; ++r) {
+        uint8_t* b = static_cast<uint8_t*>(exchange[r]);
+        if (!b || !aligned(b, 256)) return MARLIN_Q4_ERR_ARG;
+        X.part[r] = reinterpret_cast<float*>(b + lay.part);
+        X.flag[r] = reinterpret_cast<unsigned*>(b + lay.flag);
+        X.keys[r] = reinterpret_cast<unsigned long long*>(b + lay.keys);
+        X.kflag[r] = reinterpret_cast<unsigned*>(b + lay.kflag);
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint8_t* scratch = ws + step_zero_bytes(m);
+    float* h = h_out ? h_out : reinterpret_cast<float*>(scratch);
+    return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm_shard, ids, best, h, scratch,
+                              ws + 256, static_cast<cudaStream_t>(stream), &X, vocab_offset);
 }
 
 int marlin_q4_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float sigma, void* stream) {

@@ -40,6 +40,22 @@ struct XPlanes {
     int nssq;
 };
 
+// Cross-GPU exchange of the tensor-parallel decode step (plain peer loads/stores over NVLink, no
+// multicast).  Every rank owns one exchange buffer; part/flag/keys/kflag hold the device addresses
+// of all ranks' buffers in this process (the own one at [rank], the others IPC-mapped):
+//   part[r]   [2 parities][tp sources][m][hidden] binary32 partial rows of down_proj,
+//   flag[r]   [2 parities][hidden / 128 blocks][tp sources] arrival flags (1 = written, reset to 0
+//             by the owner once read),
+//   keys[r]   [tp sources][m] packed argmax keys, kflag[r] [tp sources] their arrival flags.
+constexpr int kTpMax = 8;
+struct TpExchange {
+    int tp, rank, parity, nblk;
+    float* part[kTpMax];
+    unsigned* flag[kTpMax];
+    unsigned long long* keys[kTpMax];
+    unsigned* kflag[kTpMax];
+};
+
 struct GemvLaunch {
     const void* x;  // [m, k] activations (x_dtype)
     int x_dtype;
@@ -62,6 +78,9 @@ struct GemvLaunch {
     bool has_xin, has_xout;
     XPlanes xin, xout;
     const uint16_t* out_norm;
+    // kEpiResid with tp.tp > 1: the partial rows are summed over the ranks (exchange) before the
+    // residual add
+    TpExchange tp;
 };
 
 // Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default), tcgen05/TMEM, bf16
@@ -97,6 +116,7 @@ struct LmHeadLaunch {
     bool pdl;
     bool has_xin;            // integer-MMA family only: hidden state taken from planes (see XPlanes)
     XPlanes xin;
+    TpExchange tp;           // tp.tp > 1: the final keys are max-merged over the ranks (exchange)
 };
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream);

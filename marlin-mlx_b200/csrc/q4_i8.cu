@@ -200,6 +200,49 @@ __device__ __forceinline__ void write_planes(const XPlanes& P, int ncols, int M,
 }
 
 // ------------------------------------------------------------------------------------------------
+// tensor-parallel exchange (see TpExchange)
+// ------------------------------------------------------------------------------------------------
+// The 128 epilogue threads of block `block` (thread = row `row` of the block): o[m] holds this
+// rank's partial of the row; on return it holds the sum over all ranks in rank order (the same
+// bits on every rank).  Each rank writes its partial rows into every rank's buffer, then raises
+// its flag there (system-scope release after a system fence); it waits (bounded) for all ranks'
+// flags of the block in its own buffer, sums, and resets those flags once every thread has read.
+template <int MS>
+__device__ __forceinline__ void tp_allreduce_rows(const TpExchange& X, int M, int64_t H, int64_t row, bool live,
+                                                  int block, float (&o)[MS]) {
+    const int tid = threadIdx.x, tp = X.tp, P = X.parity;
+    if (live) {
+        for (int p = 0; p < tp; ++p) {
+            float* dst = X.part[p] + ((size_t)(P * tp + X.rank) * M) * H + row;
+#pragma unroll
+            for (int m = 0; m < MS; ++m)
+                if (m < M) dst[(size_t)m * H] = o[m];
+        }
+    }
+    named_bar_sync(3, kI8Rows);
+    const size_t fo = ((size_t)P * X.nblk + block) * tp;
+    if (tid == 0) {
+        __threadfence_system();
+        for (int p = 0; p < tp; ++p) st_release_sys(X.flag[p] + fo + X.rank, 1u);
+    }
+    if (tid < tp) wait_flag_sys(X.flag[X.rank] + fo + tid);
+    named_bar_sync(3, kI8Rows);
+    if (live) {
+        const volatile float* src = X.part[X.rank] + ((size_t)P * tp * M) * H + row;
+#pragma unroll
+        for (int m = 0; m < MS; ++m) {
+            if (m < M) {
+                float v = 0.f;
+                for (int r = 0; r < tp; ++r) v += src[((size_t)r * M + m) * H];
+                o[m] = v;
+            }
+        }
+    }
+    named_bar_sync(3, kI8Rows);
+    if (tid < tp) X.flag[X.rank][fo + tid] = 0u;
+}
+
+// ------------------------------------------------------------------------------------------------
 // decode GEMV family: one 128-row block per thread-block cluster, K split over the cluster's CTAs
 // ------------------------------------------------------------------------------------------------
 struct I8UnitArgs {
@@ -395,6 +438,7 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
     }
     const int64_t row = row0 + lrow;
     const bool live = row < L.w0.n;
+    if (L.tp.tp > 1) tp_allreduce_rows<MS>(L.tp, M, L.w0.n, row, live, block, o);
     float v[MS], u[MS];
     const float wn = early ? wpre : (L.has_xout && L.out_norm && live) ? bf16_bits_to_f32(L.out_norm[row]) : 0.f;
 #pragma unroll
@@ -598,8 +642,31 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     __syncthreads();
     if (is_last) {
         __threadfence();
+        unsigned long long k = 0ull;
+        if (tid < M) k = atomicExch(&L.keys[tid], 0ull);
+        if (L.tp.tp > 1) {
+            // max-merge of the ranks' keys: write ours everywhere, wait for all, reduce in order
+            const TpExchange& X = L.tp;
+            if (tid < M)
+                for (int p = 0; p < X.tp; ++p) X.keys[p][(size_t)X.rank * M + tid] = k;
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence_system();
+                for (int p = 0; p < X.tp; ++p) st_release_sys(X.kflag[p] + X.rank, 1u);
+            }
+            if (tid < X.tp) wait_flag_sys(X.kflag[X.rank] + tid);
+            __syncthreads();
+            if (tid < M) {
+                const volatile unsigned long long* ks = X.keys[X.rank];
+                for (int r = 0; r < X.tp; ++r) {
+                    const unsigned long long kr = ks[(size_t)r * M + tid];
+                    k = kr > k ? kr : k;
+                }
+            }
+            __syncthreads();
+            if (tid < X.tp) X.kflag[X.rank][tid] = 0u;
+        }
         if (tid < M) {
-            const unsigned long long k = atomicExch(&L.keys[tid], 0ull);
             if (L.keys_out) L.keys_out[tid] = k;
             const uint32_t o = (uint32_t)(k >> 32);
             const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;

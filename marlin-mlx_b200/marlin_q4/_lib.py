@@ -58,6 +58,14 @@ SIGNATURES = {
     "marlin_q4_decode_step": (ctypes.c_int, [_vp, _i64, _i64, _i32, _PL, _vp, _f32, _PT, _vp, _vp, _vp,
                                              _vp, _sz, _vp]),
     "marlin_q4_decode_step_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "marlin_q4_tp_decode_step": (ctypes.c_int, [_vp, _i64, _i64, _i32, _vp, _vp, _f32, _vp, _i64, _vp, _vp, _vp, _i32,
+                                                _i32, _vp, _vp, _sz, _vp]),
+    "marlin_q4_tp_exchange_size": (_sz, [_i64, _i64, _i32]),
+    "marlin_q4_device_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "marlin_q4_device_free": (ctypes.c_int, [_vp]),
+    "marlin_q4_ipc_get_handle": (ctypes.c_int, [_vp, _vp]),
+    "marlin_q4_ipc_open_handle": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "marlin_q4_ipc_close_handle": (ctypes.c_int, [_vp]),
     "marlin_q4_synth_bf16": (ctypes.c_int, [_vp, _i64, _u64, _f32, _f32, _vp]),
 }
 
