@@ -197,12 +197,14 @@ size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t i
  * carry zero padding up to a multiple of 512 beyond the rank's gate/up rows: zero codes, scales and
  * biases), the lm_head by vocabulary rows starting at vocab_offset.  The per-layer all-reduce of
  * the down_proj partial rows and the argmax merge happen inside the kernels over NVLink: every rank
- * stores its partial rows and keys into every rank's exchange buffer and waits (bounded, about 2 s,
- * then records a device error) for the others' flags; sums run in rank order, so every rank holds
- * the same h and ids.  exchange[r]: rank r's exchange buffer as mapped in this process (the own one
+ * stores its partial rows and keys, each value tagged with the step and layer in one 8-byte word,
+ * into every rank's exchange buffer and waits (bounded, about 2 s, then records a device error) for
+ * the others' words to carry the expected tag; sums run in rank order, so every rank holds the same
+ * h and ids.  exchange[r]: rank r's exchange buffer as mapped in this process (the own one
  * from marlin_q4_device_alloc, the others from marlin_q4_ipc_open_handle), each
- * marlin_q4_tp_exchange_size bytes, zero before the first call and left zero.  All ranks must call
- * the step the same number of times.  m <= 16, hidden a multiple of 512, down_proj K a multiple of
+ * marlin_q4_tp_exchange_size bytes, zero before the first call (it then holds the rank's step
+ * counter and the last values exchanged).  All ranks must call the step the same number of times,
+ * at most 120 layers.  m <= 16, hidden a multiple of 512, down_proj K a multiple of
  * 512.  workspace as for marlin_q4_decode_step with intermediate = down_proj K. */
 int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
                              const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,

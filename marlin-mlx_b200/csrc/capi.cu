@@ -300,20 +300,18 @@ size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
 // with per-block sums of squares), so only the first gate/up launch stages from h0.
 // Exchange buffer of the tensor-parallel step (TpExchange), per rank.
 struct TpLayout {
-    size_t part, flag, keys, kflag, total;
+    size_t part, keys, step, total;
 };
 TpLayout tp_layout(int64_t m, int64_t hidden, int tp) {
     auto al = [](size_t v) { return (v + 255) / 256 * 256; };
     TpLayout t{};
     size_t off = 0;
     t.part = off;
-    off += al((size_t)2 * tp * m * hidden * 4);
-    t.flag = off;
-    off += al((size_t)2 * (hidden / 128) * tp * 4);
+    off += al((size_t)2 * tp * m * hidden * 8);
     t.keys = off;
-    off += al((size_t)tp * m * 8);
-    t.kflag = off;
-    off += al((size_t)tp * 4);
+    off += al((size_t)tp * m * 2 * 8);
+    t.step = off;
+    off += 256;
     t.total = off;
     return t;
 }
@@ -372,6 +370,7 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
         if (tpx) {
             D.tp = *tpx;
             D.tp.parity = l & 1;
+            D.tp.layer = l;
         }
         if ((rc = cuda_status(launch_i8_gemv(D, st)))) return rc;
         cur = h;
@@ -547,18 +546,17 @@ int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int3
         workspace_bytes < marlin_q4_decode_step_workspace_size(m, hidden, inter))
         return MARLIN_Q4_ERR_WORKSPACE;
     const TpLayout lay = tp_layout(m, hidden, tp_size);
+    if (n_layers > 120) return MARLIN_Q4_ERR_UNSUPPORTED;  // exchange tags hold the layer in 7 bits
     TpExchange X{};
     X.tp = tp_size;
     X.rank = tp_rank;
-    X.nblk = (int)(hidden / 128);
     for (int r = 0; r < tp_size; ++r) {
         uint8_t* b = static_cast<uint8_t*>(exchange[r]);
         if (!b || !aligned(b, 256)) return MARLIN_Q4_ERR_ARG;
-        X.part[r] = reinterpret_cast<float*>(b + lay.part);
-        X.flag[r] = reinterpret_cast<unsigned*>(b + lay.flag);
+        X.part[r] = reinterpret_cast<unsigned long long*>(b + lay.part);
         X.keys[r] = reinterpret_cast<unsigned long long*>(b + lay.keys);
-        X.kflag[r] = reinterpret_cast<unsigned*>(b + lay.kflag);
     }
+    X.step = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(exchange[tp_rank]) + lay.step);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     uint8_t* scratch = ws + step_zero_bytes(m);
     float* h = h_out ? h_out : reinterpret_cast<float*>(scratch);

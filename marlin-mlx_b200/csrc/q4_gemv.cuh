@@ -41,19 +41,21 @@ struct XPlanes {
 };
 
 // Cross-GPU exchange of the tensor-parallel decode step (plain peer loads/stores over NVLink, no
-// multicast).  Every rank owns one exchange buffer; part/flag/keys/kflag hold the device addresses
-// of all ranks' buffers in this process (the own one at [rank], the others IPC-mapped):
-//   part[r]   [2 parities][tp sources][m][hidden] binary32 partial rows of down_proj,
-//   flag[r]   [2 parities][hidden / 128 blocks][tp sources] arrival flags (1 = written, reset to 0
-//             by the owner once read),
-//   keys[r]   [tp sources][m] packed argmax keys, kflag[r] [tp sources] their arrival flags.
+// multicast, no flags or fences): every value travels as one 8-byte word, (tag << 32) | bits, so a
+// reader that sees the expected tag also sees the value (aligned 64-bit stores are single-copy
+// atomic).  Tags are (step << 7) + slot + 1 with `step` a per-rank counter that every rank advances
+// once per decode step (the lm_head's last CTA), so consecutive uses of a word carry different tags.
+// Every rank owns one exchange buffer; part/keys hold the device addresses of all ranks' buffers in
+// this process (the own one at [rank], the others IPC-mapped):
+//   part[r]   [2 parities][tp sources][m][hidden] words: partial rows of down_proj (binary32 bits),
+//   keys[r]   [tp sources][m][2] words: the low and high halves of the packed argmax keys,
+//   step      this rank's step counter (in its own buffer).
 constexpr int kTpMax = 8;
 struct TpExchange {
-    int tp, rank, parity, nblk;
-    float* part[kTpMax];
-    unsigned* flag[kTpMax];
+    int tp, rank, parity, layer;
+    unsigned long long* part[kTpMax];
     unsigned long long* keys[kTpMax];
-    unsigned* kflag[kTpMax];
+    unsigned* step;
 };
 
 struct GemvLaunch {

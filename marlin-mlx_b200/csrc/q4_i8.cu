@@ -202,44 +202,58 @@ __device__ __forceinline__ void write_planes(const XPlanes& P, int ncols, int M,
 // ------------------------------------------------------------------------------------------------
 // tensor-parallel exchange (see TpExchange)
 // ------------------------------------------------------------------------------------------------
-// The 128 epilogue threads of block `block` (thread = row `row` of the block): o[m] holds this
-// rank's partial of the row; on return it holds the sum over all ranks in rank order (the same
-// bits on every rank).  Each rank writes its partial rows into every rank's buffer, then raises
-// its flag there (system-scope release after a system fence); it waits (bounded) for all ranks'
-// flags of the block in its own buffer, sums, and resets those flags once every thread has read.
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait for the word at p to carry `tag`; returns its low 32 bits (0 after a timeout, which
+// is recorded as a device error).
+__device__ __forceinline__ uint32_t wait_word(const unsigned long long* p, uint32_t tag) {
+    unsigned long long w = ld_word_sys(p);
+    if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+    const unsigned long long t0 = cycles_now();
+    for (uint32_t it = 0;; ++it) {
+        w = ld_word_sys(p);
+        if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+        if ((it & 63u) == 63u && cycles_now() - t0 > kWaitCycles) {
+            record_device_error(kDevErrMbarTimeout);
+            return 0u;
+        }
+    }
+}
+__device__ __forceinline__ uint32_t tp_tag(const TpExchange& X, int slot) {
+    return (*reinterpret_cast<volatile unsigned*>(X.step) << 7) + (uint32_t)slot + 1u;
+}
+
+// One epilogue thread per output row: o[m] holds this rank's partial of the row; on return it holds
+// the sum over all ranks in rank order (the same bits on every rank).  The thread stores its tagged
+// partials into every rank's buffer, then reads each source's word for its row from its own buffer
+// once the tag matches.  No barrier: each thread waits only for the words of its own row.
 template <int MS>
 __device__ __forceinline__ void tp_allreduce_rows(const TpExchange& X, int M, int64_t H, int64_t row, bool live,
-                                                  int block, float (&o)[MS]) {
-    const int tid = threadIdx.x, tp = X.tp, P = X.parity;
-    if (live) {
-        for (int p = 0; p < tp; ++p) {
-            float* dst = X.part[p] + ((size_t)(P * tp + X.rank) * M) * H + row;
+                                                  float (&o)[MS]) {
+    if (!live) return;
+    const int tp = X.tp, P = X.parity;
+    const uint32_t tag = tp_tag(X, X.layer);
+    for (int p = 0; p < tp; ++p) {
+        unsigned long long* dst = X.part[p] + ((size_t)(P * tp + X.rank) * M) * H + row;
 #pragma unroll
-            for (int m = 0; m < MS; ++m)
-                if (m < M) dst[(size_t)m * H] = o[m];
+        for (int m = 0; m < MS; ++m)
+            if (m < M) st_word_sys(dst + (size_t)m * H, ((unsigned long long)tag << 32) | __float_as_uint(o[m]));
+    }
+    const unsigned long long* src = X.part[X.rank] + ((size_t)P * tp * M) * H + row;
+#pragma unroll
+    for (int m = 0; m < MS; ++m) {
+        if (m < M) {
+            float v = 0.f;
+            for (int r = 0; r < tp; ++r) v += __uint_as_float(wait_word(src + ((size_t)r * M + m) * H, tag));
+            o[m] = v;
         }
     }
-    named_bar_sync(3, kI8Rows);
-    const size_t fo = ((size_t)P * X.nblk + block) * tp;
-    if (tid == 0) {
-        __threadfence_system();
-        for (int p = 0; p < tp; ++p) st_release_sys(X.flag[p] + fo + X.rank, 1u);
-    }
-    if (tid < tp) wait_flag_sys(X.flag[X.rank] + fo + tid);
-    named_bar_sync(3, kI8Rows);
-    if (live) {
-        const volatile float* src = X.part[X.rank] + ((size_t)P * tp * M) * H + row;
-#pragma unroll
-        for (int m = 0; m < MS; ++m) {
-            if (m < M) {
-                float v = 0.f;
-                for (int r = 0; r < tp; ++r) v += src[((size_t)r * M + m) * H];
-                o[m] = v;
-            }
-        }
-    }
-    named_bar_sync(3, kI8Rows);
-    if (tid < tp) X.flag[X.rank][fo + tid] = 0u;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -438,7 +452,7 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
     }
     const int64_t row = row0 + lrow;
     const bool live = row < L.w0.n;
-    if (L.tp.tp > 1) tp_allreduce_rows<MS>(L.tp, M, L.w0.n, row, live, block, o);
+    if (L.tp.tp > 1) tp_allreduce_rows<MS>(L.tp, M, L.w0.n, row, live, o);
     float v[MS], u[MS];
     const float wn = early ? wpre : (L.has_xout && L.out_norm && live) ? bf16_bits_to_f32(L.out_norm[row]) : 0.f;
 #pragma unroll
@@ -645,26 +659,25 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
         unsigned long long k = 0ull;
         if (tid < M) k = atomicExch(&L.keys[tid], 0ull);
         if (L.tp.tp > 1) {
-            // max-merge of the ranks' keys: write ours everywhere, wait for all, reduce in order
+            // max-merge of the ranks' keys: tagged halves to every rank, then each rank's from the own buffer
             const TpExchange& X = L.tp;
-            if (tid < M)
-                for (int p = 0; p < X.tp; ++p) X.keys[p][(size_t)X.rank * M + tid] = k;
-            __syncthreads();
-            if (tid == 0) {
-                __threadfence_system();
-                for (int p = 0; p < X.tp; ++p) st_release_sys(X.kflag[p] + X.rank, 1u);
-            }
-            if (tid < X.tp) wait_flag_sys(X.kflag[X.rank] + tid);
-            __syncthreads();
+            const uint32_t tag = tp_tag(X, 126);
             if (tid < M) {
-                const volatile unsigned long long* ks = X.keys[X.rank];
+                const unsigned long long th = (unsigned long long)tag << 32;
+                for (int p = 0; p < X.tp; ++p) {
+                    unsigned long long* d = X.keys[p] + ((size_t)X.rank * M + tid) * 2;
+                    st_word_sys(d, th | (k & 0xffffffffull));
+                    st_word_sys(d + 1, th | (k >> 32));
+                }
                 for (int r = 0; r < X.tp; ++r) {
-                    const unsigned long long kr = ks[(size_t)r * M + tid];
+                    const unsigned long long* sw = X.keys[X.rank] + ((size_t)r * M + tid) * 2;
+                    const unsigned long long kr = (unsigned long long)wait_word(sw, tag) |
+                                                  ((unsigned long long)wait_word(sw + 1, tag) << 32);
                     k = kr > k ? kr : k;
                 }
             }
-            __syncthreads();
-            if (tid < X.tp) X.kflag[X.rank][tid] = 0u;
+            __syncthreads();  // every thread of this CTA has read this step's words
+            if (tid == 0) *reinterpret_cast<volatile unsigned*>(X.step) = *reinterpret_cast<volatile unsigned*>(X.step) + 1u;
         }
         if (tid < M) {
             if (L.keys_out) L.keys_out[tid] = k;
