@@ -371,28 +371,6 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
-// ---- system-scope flags for cross-GPU exchanges (plain peer memory) -----------------------------
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Bounded wait until *p == 1 (written by another GPU); false after kWaitCycles (error recorded).
-__device__ __forceinline__ bool wait_flag_sys(const unsigned* p) {
-    if (ld_acquire_sys(p) == 1u) return true;
-    const unsigned long long t0 = cycles_now();
-    for (uint32_t it = 0;; ++it) {
-        if (ld_acquire_sys(p) == 1u) return true;
-        if ((it & 63u) == 63u && cycles_now() - t0 > kWaitCycles) {
-            record_device_error(kDevErrMbarTimeout);
-            return false;
-        }
-    }
-}
-
 __device__ __forceinline__ void st_cluster_f32(const float* local_ptr, uint32_t rank, float v) {
     uint32_t raddr;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(local_ptr)), "r"(rank));
