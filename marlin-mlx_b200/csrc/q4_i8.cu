@@ -60,8 +60,9 @@ constexpr uint32_t kI8TwoPerSm = 110 * 1024;          // two CTAs per SM (PDL ov
 // then the scales [ROWS][8 groups] and the biases [ROWS][8 groups].
 // ------------------------------------------------------------------------------------------------
 template <int NTN, int ROWS = kI8Rows>
-__device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int ncols, int warp,
-                                         int lane, float (&y)[NTN][4], float (&yb)[NTN][2]) {
+__device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int warp, int lane,
+                                         float (&y)[NTN][4], float (&yb)[NTN][2]) {
+    constexpr int ncols = 8 * NTN;  // activation columns (compile-time, so plane addresses fold)
     // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * warp + g, r1 = r0 + 8;
@@ -276,7 +277,8 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
     constexpr int MS = 2 * NTN;  // activation rows per pass
     const GemvLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int M = (int)L.m, CL = a.CL, S = a.S, ncols = a.ncols;
+    const int M = (int)L.m, CL = a.CL, S = a.S;
+    constexpr int ncols = 8 * NTN;  // == a.ncols
     const uint32_t rank = CL > 1 ? cluster_rank() : 0u;
     const int block = blockIdx.x / CL;
     const int g0 = (int)rank * a.gpc, ng = min(a.gpc, a.G - g0);
@@ -364,8 +366,8 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             I8_STAGE_MARK(q);
             const int gs = g0 + q * kI8StageGroups;
-            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, ncols, warp,
-                          lane, y, yb);
+            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, warp, lane,
+                          y, yb);
 #pragma unroll
             for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
                 hold_regs(y[j]);
@@ -514,7 +516,8 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     uint8_t* smem = align_smem_1024(smem_raw);
     const LmHeadLaunch& L = a.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = a.G, S = a.S, M = (int)L.m, ncols = a.ncols;
+    const int G = a.G, S = a.S, M = (int)L.m;
+    constexpr int ncols = 8 * NTN;  // == a.ncols
     const int spb = G / kI8StageGroups;  // stages per block
     const int my_blocks =
         a.nblocks > (int)blockIdx.x ? (a.nblocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -591,8 +594,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
         for (int q = 0; xin_ok && q < nst; ++q) {
             if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
             const int sp = q % spb, gs = sp * kI8StageGroups;
-            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, ncols, warp, lane, y,
-                                     yb);
+            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, warp, lane, y, yb);
 #pragma unroll
             for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
                 hold_regs(y[j]);
