@@ -362,19 +362,24 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
         }
     } else {
         const bool xin_ok = !L.has_xin || warp_wait(xbar, 0u, abort);
+        int slot = 0;  // ring position of stage q, kept as a counter (no division per stage)
+        uint32_t ph = 0u;
         for (int q = 0; xin_ok && q < nst; ++q) {
-            if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
+            if (!warp_wait(&full[slot], ph, abort)) break;
             I8_STAGE_MARK(q);
             const int gs = g0 + q * kI8StageGroups;
-            i8_stage<NTN>(ring + (size_t)(q % S) * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, warp, lane,
-                          y, yb);
+            i8_stage<NTN>(ring + (size_t)slot * kI8StageBytes, (gs & 7) * 2, q * kI8StageGroups, tx, warp, lane, y, yb);
 #pragma unroll
             for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
                 hold_regs(y[j]);
                 hold_regs(yb[j]);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[q % S]);
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == S) {
+                slot = 0;
+                ph ^= 1u;
+            }
         }
         // planes -> one partial per (row, activation row), into the leader's slot for this rank
         const int g = lane >> 2, tq = lane & 3;
@@ -591,19 +596,27 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
             y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
             best[j] = 0ull;
         }
+        int slot = 0, sp = 0, bi = 0;  // ring position, stage within the block, block (counters)
+        uint32_t ph = 0u;
         for (int q = 0; xin_ok && q < nst; ++q) {
-            if (!warp_wait(&full[q % S], (uint32_t)((q / S) & 1), abort)) break;
-            const int sp = q % spb, gs = sp * kI8StageGroups;
-            i8_stage<NTN, ST::kRows>(ring + (size_t)(q % S) * ST::kBytes, (gs & 7) * 2, gs, tx, warp, lane, y, yb);
+            if (!warp_wait(&full[slot], ph, abort)) break;
+            const int gs = sp * kI8StageGroups;
+            i8_stage<NTN, ST::kRows>(ring + (size_t)slot * ST::kBytes, (gs & 7) * 2, gs, tx, warp, lane, y, yb);
 #pragma unroll
             for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
                 hold_regs(y[j]);
                 hold_regs(yb[j]);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[q % S]);
-            if (sp == spb - 1) {  // block finished: logits -> argmax keys (max over the warp's rows)
-                const int64_t rowa = (int64_t)(blockIdx.x + (int64_t)(q / spb) * gridDim.x) * ST::kRows + 16 * warp + g;
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == S) {
+                slot = 0;
+                ph ^= 1u;
+            }
+            if (++sp == spb) {  // block finished: logits -> argmax keys (max over the warp's rows)
+                sp = 0;
+                const int64_t rowa = (int64_t)(blockIdx.x + (int64_t)bi * gridDim.x) * ST::kRows + 16 * warp + g;
+                ++bi;
                 const int64_t rowb = rowa + 8;
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
