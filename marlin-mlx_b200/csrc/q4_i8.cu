@@ -536,19 +536,21 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
            reinterpret_cast<float*>(smem + a.off_scr), reinterpret_cast<float*>(smem + a.off_scr) + 64,
            reinterpret_cast<unsigned int*>(smem + a.off_misc + 64), reinterpret_cast<float*>(smem + a.off_xe)};
 
-    auto issue = [&](int q) {
-        const int bi = q / spb, gs = (q % spb) * kI8StageGroups;
+    // stage at ring slot `slot`: stage sp of this CTA's block bi
+    auto issue_at = [&](int slot, int sp, int bi) {
+        const int gs = sp * kI8StageGroups;
         const int64_t row0 = (int64_t)(blockIdx.x + (int64_t)bi * gridDim.x) * ST::kRows;
-        uint8_t* st = ring + (size_t)(q % S) * ST::kBytes;
-        mbar_arrive_expect_tx(&full[q % S], ST::kBytes);
+        uint8_t* st = ring + (size_t)slot * ST::kBytes;
+        mbar_arrive_expect_tx(&full[slot], ST::kBytes);
 #pragma unroll
         for (int h = 0; h < ST::kRows / kI8Rows; ++h) {
             const int32_t y = (int32_t)(row0 + h * kI8Rows);
-            tma_load_2d(st + h * kI8Rows * 128, &a.tw, gs * 8, y, &full[q % S]);
-            tma_load_2d(st + ST::kRows * 128 + h * kI8Rows * 16, &a.ts, gs & ~7, y, &full[q % S]);
-            tma_load_2d(st + ST::kRows * 144 + h * kI8Rows * 16, &a.tb, gs & ~7, y, &full[q % S]);
+            tma_load_2d(st + h * kI8Rows * 128, &a.tw, gs * 8, y, &full[slot]);
+            tma_load_2d(st + ST::kRows * 128 + h * kI8Rows * 16, &a.ts, gs & ~7, y, &full[slot]);
+            tma_load_2d(st + ST::kRows * 144 + h * kI8Rows * 16, &a.tb, gs & ~7, y, &full[slot]);
         }
     };
+    auto issue = [&](int q) { issue_at(q % S, q % spb, q / spb); };
     if (tid == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
@@ -577,9 +579,19 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     if (warp == W) {
         if (lane == 0) {
             int q = min(S, nst);
+            int slot = q % S, sp = q % spb, bi = q / spb;  // counters from here on
+            uint32_t ph = (uint32_t)(((q / S) - 1) & 1);
             for (; q < nst; ++q) {
-                if (!thread_wait(&empty[q % S], (uint32_t)(((q / S) - 1) & 1), abort)) break;
-                issue(q);
+                if (!thread_wait(&empty[slot], ph, abort)) break;
+                issue_at(slot, sp, bi);
+                if (++slot == S) {
+                    slot = 0;
+                    ph ^= 1u;
+                }
+                if (++sp == spb) {
+                    sp = 0;
+                    ++bi;
+                }
             }
             for (int r = max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
             if (L.has_xin) drain_wait(xbar, 0u);
