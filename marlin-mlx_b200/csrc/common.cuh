@@ -86,6 +86,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but a thread whose phase is not complete sleeps until it completes (or about
+// 1 ms passes) instead of returning at once, so waiting warps leave the issue slots to the others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -307,12 +321,14 @@ __device__ __forceinline__ void hold_regs(const float (&v)[N]) {
 
 // ---- waits shared by the warp-specialised kernels ------------------------------------------------
 // Bounded wait that also ends early once another role has aborted (timeout recorded on device).
-// Every lane acquires the barrier; the exit is warp-uniform.
+// Every lane acquires the barrier; the exit is warp-uniform.  kSleep: wait with mbar_try_wait_sleep.
+template <bool kSleep = false>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
     const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0;; ++it) {
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0)) return true;
+        const bool ok = kSleep ? mbar_try_wait_sleep(bar, parity) : mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ok ? 1 : 0)) return true;
         if ((it & 63u) == 63u) {
             int stop = 0;
             if ((threadIdx.x & 31) == 0) {
@@ -329,11 +345,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 // Single-thread bounded wait (producer / MMA issuer).
+template <bool kSleep = false>
 __device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0; it < (1u << 28); ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (kSleep ? mbar_try_wait_sleep(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 63u) {
             if (*abort) return false;
             if (cycles_now() - t0 > kWaitCycles) {

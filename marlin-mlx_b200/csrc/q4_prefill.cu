@@ -11,15 +11,18 @@
 // consumer is done: X tiles [128 x 64] bf16 (128-byte swizzle; released by the MMA commit),
 // packed words [256 rows x 8 words] (released by the dequant warps) and scales/biases
 // [256 rows x 8 groups] (one entry per 8 groups).  Warp roles:
-//   * warp 0: lane 0 feeds the X ring, lane 1 the weight and scale/bias rings;
-//   * warps 2-9, thread = weight row: dequantize one group into bf16 W[256 x 64] in shared
-//     memory, K-major with 128-byte swizzle (the tcgen05 operand layout): per pair of codes one
-//     LOP3 (128 + q as bf16, exact), one FMA removing the 128 (exact) and one FMA q s + b (bf16x2,
-//     a single rounding), then PRMTs restore natural K order; double-buffered;
+//   * warp 5 (one thread) feeds the X ring, warp 9 (one thread) the weight and scale/bias rings
+//     (separate warps: two producer loops in one warp serialise each other's waits);
+//   * sixteen warps, two teams of eight taking alternate K steps, thread = weight row: dequantize one
+//     group into bf16 W[256 x 64] in shared memory, K-major with 128-byte swizzle (the tcgen05
+//     operand layout): per pair of codes one LOP3 (128 + q as bf16, exact), one FMA removing the
+//     128 (exact) and one FMA q s + b (bf16x2, a single rounding), then PRMTs restore natural K
+//     order; three buffers (two for 256-row tiles), so a team's fence and waits overlap the other
+//     team's work;
 //   * warp 1 (one thread): tcgen05.mma kind::f16 (bf16), M=128 N=256 K=16, A = X and B = W from
 //     shared memory, D in TMEM (two 256-column accumulators, so the epilogue of one tile overlaps
 //     the MMAs of the next);
-//   * warps 10-13: epilogue — tcgen05.ld the accumulator (lane = activation row), then store
+//   * warps 12-15: epilogue — tcgen05.ld the accumulator (lane = activation row), then store
 //     (bf16 / binary32), SwiGLU of a gate/up tile pair (128 gate + 128 up rows per tile) or a
 //     residual add.
 // Every wait is bounded (2 s): on timeout the kernel records a device error and drains.
@@ -30,32 +33,51 @@
 
 #include <algorithm>
 
+// Optional timeline hook, empty in the library build: PF_MARK(warp, lane, point, index) at phase
+// boundaries of the MMA, dequant and epilogue loops (index = the CTA's running step or tile).
+#ifndef PF_MARK
+#define PF_MARK(w, l, k, i)
+#endif
+
 namespace marlin {
 namespace {
 
 constexpr int kPM = 128;                      // activation rows per MMA (M, TMEM lanes)
 constexpr int kPN = 256;                      // weight rows per tile (MMA N)
-constexpr int kPSW = 6;                       // packed-word ring stages
-constexpr int kPNB = 2;                       // dequantized W buffers
 constexpr uint32_t kPA = kPM * 128;           // X box: 128 rows x 64 bf16
 constexpr uint32_t kPW = kPN * 32;            // packed words: 256 rows x 8 words
 constexpr uint32_t kPSB = kPN * 16;           // scales (or biases): 256 rows x 8 groups
 constexpr uint32_t kPB = kPN * 128;           // dequantized W: 256 rows x 64 bf16
-constexpr int kPDeqWarps = 16;                // two threads per weight row
-constexpr int kPThreads = (2 + kPDeqWarps + 4) * 32;  // producers, MMA, dequant, epilogue
+constexpr int kPTeamWarps = 8;                // one dequant team: one thread per weight row
+constexpr int kPDeqWarps = 2 * kPTeamWarps;   // two teams, alternate K steps
+// Warp roles by warp index; warp w issues on SM sub-partition w % 4.  The MMA issuer (one thread that
+// must keep the tensor pipe fed) shares its sub-partition with the two producers and one epilogue
+// warp, which mostly sleep on barriers, and only two of the sixteen dequant warps; the other
+// sub-partitions take one epilogue warp and four or five dequant warps each.
+constexpr int kPWarpMma = 1, kPWarpX = 5, kPWarpW = 9;
+constexpr int kPEpi0 = 12;                    // epilogue warps 12-15: TMEM lane quarters 0-3
+constexpr int kPThreads = (4 + kPDeqWarps + 3) * 32;
+
+// dequant warp index 0..15 of a warp that has no other role
+__device__ __forceinline__ int deq_index(int warp) {
+    return warp - (warp > kPWarpMma) - (warp > kPWarpX) - (warp > kPWarpW) - (warp > kPEpi0 ? min(warp, kPEpi0 + 4) - kPEpi0 : 0);
+}
 constexpr uint32_t kPTmemCols = 512;
+constexpr bool kPSleep = true;                // waiting threads sleep on the mbarrier (no spinning)
 
 // Shared-memory plan for MH activation-row halves per tile (M = 128 MH): MH = 1 double-buffers the
 // accumulator across tiles; MH = 2 uses both 256-column accumulators for one 256-row tile and so
-// dequantizes each weight tile once for twice the MMA work.
+// dequantizes each weight tile once for twice the MMA work (its epilogue then stalls the MMAs).
 template <int MH>
 struct PPlan {
-    static constexpr int SX = MH == 1 ? 5 : 3;  // X ring stages
+    static constexpr int SX = MH == 1 ? 4 : 3;  // X ring stages
+    static constexpr int SW = 6;                // packed-word ring stages
+    static constexpr int NB = MH == 1 ? 3 : 2;  // dequantized W buffers
     static constexpr uint32_t XSTAGE = MH * kPA;
     static constexpr uint32_t OFF_W = SX * XSTAGE;
-    static constexpr uint32_t OFF_SB = OFF_W + kPSW * kPW;
+    static constexpr uint32_t OFF_SB = OFF_W + SW * kPW;
     static constexpr uint32_t OFF_B = OFF_SB + 2 * 2 * kPSB;
-    static constexpr uint32_t OFF_BAR = OFF_B + kPNB * kPB;
+    static constexpr uint32_t OFF_BAR = OFF_B + NB * kPB;
     static constexpr uint32_t SMEM = 1024 + OFF_BAR + 512;
 };
 
@@ -98,6 +120,24 @@ __device__ __forceinline__ float swiglu_bf16(float g, float u) {
     return bf16_round(bf16_round(sg * gq) * uq);
 }
 
+// bf16x2 of (lo, hi), each rounded to nearest even
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// swiglu_bf16 of two adjacent outputs, as bf16x2 (the first in the low half).  The same roundings:
+// g, u and the sigmoid rounded to bf16 by cvt; each product of two bf16 values is exact in binary32,
+// so one bf16 multiply (an FMA with -0) rounds it as bf16_round does.
+__device__ __forceinline__ uint32_t swiglu_bf16x2(float g0, float g1, float u0, float u1) {
+    constexpr uint32_t kNegZero2 = 0x80008000u;
+    const uint32_t gq = cvt_bf16x2(g0, g1), uq = cvt_bf16x2(u0, u1);
+    const float a0 = bf16_bits_to_f32(gq & 0xffffu), a1 = bf16_bits_to_f32(gq >> 16);
+    const uint32_t sq = cvt_bf16x2(__fdividef(1.0f, 1.0f + expf(-a0)), __fdividef(1.0f, 1.0f + expf(-a1)));
+    return bf16x2_fma(bf16x2_fma(sq, gq, kNegZero2), uq, kNegZero2);
+}
+
 // Ring position: slot and round advance together.
 struct RingPos {
     int slot = 0, round = 0;
@@ -125,22 +165,21 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::OFF_BAR);
     uint64_t* xfull = bars;               // [SX]
     uint64_t* xempty = xfull + P::SX;     // [SX] MMA commit
-    uint64_t* wfull = xempty + P::SX;     // [kPSW]
-    uint64_t* wempty = wfull + kPSW;      // [kPSW] 8 dequant warps
-    uint64_t* sbfull = wempty + kPSW;     // [2]
-    uint64_t* sbempty = sbfull + 2;       // [2] 8 dequant warps
-    uint64_t* bfull = sbempty + 2;        // [kPNB] 8 dequant warps
-    uint64_t* bfree = bfull + kPNB;       // [kPNB] MMA commit
-    uint64_t* dfull = bfree + kPNB;       // [2]
+    uint64_t* wfull = xempty + P::SX;     // [SW]
+    uint64_t* wempty = wfull + P::SW;     // [SW] the warps of one dequant team
+    uint64_t* sbfull = wempty + P::SW;    // [2]
+    uint64_t* sbempty = sbfull + 2;       // [2] all dequant warps
+    uint64_t* bfull = sbempty + 2;        // [NB] the warps of one dequant team
+    uint64_t* bfree = bfull + P::NB;      // [NB] MMA commit
+    uint64_t* dfull = bfree + P::NB;      // [2]
     uint64_t* dempty = dfull + 2;         // [2] 4 epilogue warps (per accumulator; per half when MH == 2)
     uint64_t* fin = dempty + 2;           // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int ntiles_total = a.mtiles * a.ntiles;
     const int my_tiles = ntiles_total > (int)blockIdx.x ? (ntiles_total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nsb = (G + 7) / 8;  // scale/bias entries per tile
 
-    if (warp == 1) {
+    if (warp == kPWarpMma) {
         tmem_alloc(tmem_slot, kPTmemCols);
         tmem_relinquish();
     }
@@ -150,9 +189,9 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             mbar_init(&xfull[s], 1);
             mbar_init(&xempty[s], 1);
         }
-        for (int s = 0; s < kPSW; ++s) {
+        for (int s = 0; s < P::SW; ++s) {
             mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], kPDeqWarps);
+            mbar_init(&wempty[s], kPTeamWarps);
         }
         for (int j = 0; j < 2; ++j) {
             mbar_init(&sbfull[j], 1);
@@ -160,8 +199,8 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             mbar_init(&dfull[j], 1);
             mbar_init(&dempty[j], 4);
         }
-        for (int j = 0; j < kPNB; ++j) {
-            mbar_init(&bfull[j], kPDeqWarps);
+        for (int j = 0; j < P::NB; ++j) {
+            mbar_init(&bfull[j], kPTeamWarps);
             mbar_init(&bfree[j], 1);
         }
         mbar_init(fin, 1);
@@ -180,7 +219,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
         nt = t / a.mtiles;
     };
 
-    if (warp == 0) {
+    if (warp == kPWarpX) {
         if (lane == 0) {  // X tiles
             prefetch_tmap(&a.tx);
             RingPos p;
@@ -190,7 +229,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 int mt, nt;
                 tile_coords(lt, mt, nt);
                 for (int g = 0; g < G; ++g) {
-                    if (p.round > 0 && !thread_wait(&xempty[p.slot], (uint32_t)((p.round - 1) & 1), abort)) {
+                    if (p.round > 0 && !thread_wait<kPSleep>(&xempty[p.slot], (uint32_t)((p.round - 1) & 1), abort)) {
                         ok = false;
                         break;
                     }
@@ -204,7 +243,9 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 }
             }
             for (int q = max(0, issued - P::SX); q < issued; ++q) drain_wait(&xfull[q % P::SX], (uint32_t)((q / P::SX) & 1));
-        } else if (lane == 1) {  // packed words, scales / biases
+        }
+    } else if (warp == kPWarpW) {
+        if (lane == 0) {  // packed words, scales / biases
             prefetch_tmap(&a.tw0);
             prefetch_tmap(&a.ts0);
             prefetch_tmap(&a.tb0);
@@ -218,7 +259,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 for (int g = 0; g < G; ++g) {
                     if ((g & 7) == 0) {
                         const int se = e & 1;
-                        if (e >= 2 && !thread_wait(&sbempty[se], (uint32_t)(((e >> 1) - 1) & 1), abort)) {
+                        if (e >= 2 && !thread_wait<kPSleep>(&sbempty[se], (uint32_t)(((e >> 1) - 1) & 1), abort)) {
                             ok = false;
                             break;
                         }
@@ -235,7 +276,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                         }
                         ++e;
                     }
-                    if (p.round > 0 && !thread_wait(&wempty[p.slot], (uint32_t)((p.round - 1) & 1), abort)) {
+                    if (p.round > 0 && !thread_wait<kPSleep>(&wempty[p.slot], (uint32_t)((p.round - 1) & 1), abort)) {
                         ok = false;
                         break;
                     }
@@ -248,35 +289,44 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                         tma_load_2d(sw, &a.tw0, g * 8, row0, &wfull[p.slot]);
                     }
                     ++issued;
-                    p.next(kPSW);
+                    p.next(P::SW);
                 }
             }
-            for (int q = max(0, issued - kPSW); q < issued; ++q) drain_wait(&wfull[q % kPSW], (uint32_t)((q / kPSW) & 1));
+            for (int q = max(0, issued - P::SW); q < issued; ++q) drain_wait(&wfull[q % P::SW], (uint32_t)((q / P::SW) & 1));
             for (int q = max(0, e - 2); q < e; ++q) drain_wait(&sbfull[q & 1], (uint32_t)((q >> 1) & 1));
         }
-    } else if (warp == 1) {
+    } else if (warp == kPWarpMma) {
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_bf16(kPM, kPN);
+            // operand descriptors of the ring bases; a stage, half or K slice at byte offset o adds
+            // o >> 4 to the start-address field (addresses stay below 2^18, so the field never carries)
+            const uint64_t xd0 = umma_desc_sw128(xring), bd0 = umma_desc_sw128(bbuf);
             RingPos px, pb;
             bool ok = true;
             for (int lt = 0; lt < my_tiles && ok; ++lt) {
                 // MH == 1: accumulators alternate between tiles; MH == 2: both belong to every tile, and
                 // half h is reused as soon as the epilogue has drained it (checked before its first MMA)
                 const int acc = MH == 1 ? (lt & 1) : 0;
-                if (MH == 1 && lt >= 2 && !thread_wait(&dempty[acc], (uint32_t)(((lt >> 1) - 1) & 1), abort)) break;
+                if (MH == 1 && lt >= 2 && !thread_wait<kPSleep>(&dempty[acc], (uint32_t)(((lt >> 1) - 1) & 1), abort)) break;
                 for (int g = 0; g < G; ++g) {
-                    if (!thread_wait(&xfull[px.slot], (uint32_t)(px.round & 1), abort) ||
-                        !thread_wait(&bfull[pb.slot], (uint32_t)(pb.round & 1), abort)) {
+                    PF_MARK(warp, lane, 0, lt * G + g);
+                    if (!thread_wait<kPSleep>(&xfull[px.slot], (uint32_t)(px.round & 1), abort)) {
                         ok = false;
                         break;
                     }
+                    PF_MARK(warp, lane, 1, lt * G + g);
+                    if (!thread_wait<kPSleep>(&bfull[pb.slot], (uint32_t)(pb.round & 1), abort)) {
+                        ok = false;
+                        break;
+                    }
+                    PF_MARK(warp, lane, 2, lt * G + g);
                     tc_fence_after();
-                    const uint8_t* xa = xring + (size_t)px.slot * P::XSTAGE;
-                    const uint8_t* wb = bbuf + (size_t)pb.slot * kPB;
+                    const uint64_t xd = xd0 + (uint64_t)(((uint32_t)px.slot * P::XSTAGE) >> 4);
+                    const uint64_t bd = bd0 + (uint64_t)(((uint32_t)pb.slot * kPB) >> 4);
 #pragma unroll
                     for (int h = 0; h < MH; ++h) {
                         if (MH == 2 && g == 0 && lt >= 1) {
-                            if (!thread_wait(&dempty[h], (uint32_t)((lt - 1) & 1), abort)) {
+                            if (!thread_wait<kPSleep>(&dempty[h], (uint32_t)((lt - 1) & 1), abort)) {
                                 ok = false;
                                 break;
                             }
@@ -284,61 +334,80 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                         }
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            umma_smem_a(tmem + (acc + h) * kPN, umma_desc_sw128(xa + h * kPA + 32 * k),
-                                        umma_desc_sw128(wb + 32 * k), idesc, g > 0 || k > 0);
+                            umma_smem_a(tmem + (acc + h) * kPN, xd + (uint64_t)((h * kPA + 32 * k) >> 4),
+                                        bd + (uint64_t)(2 * k), idesc, g > 0 || k > 0);
                     }
                     if (!ok) break;
+                    PF_MARK(warp, lane, 3, lt * G + g);
                     umma_commit(&xempty[px.slot]);
                     umma_commit(&bfree[pb.slot]);
                     if (g == G - 1) umma_commit(&dfull[acc]);
                     px.next(P::SX);
-                    pb.next(kPNB);
+                    pb.next(P::NB);
                 }
             }
             umma_commit(fin);  // every MMA issued above completes before TMEM is released
             drain_wait(fin, 0);
         }
-    } else if (warp < 2 + kPDeqWarps) {
-        // dequant: two threads per weight row n, four packed words each
-        const int t = tid - 64, n = t >> 1, half = t & 1;
-        uint32_t uoff[4];  // 128-byte swizzle: 16-byte unit u of row n sits at (u ^ (n & 7)) * 16
-#pragma unroll
-        for (int i = 0; i < 4; ++i) uoff[i] = (uint32_t)(n * 128 + (((4 * half + i) ^ (n & 7)) << 4));
-        RingPos pw, pb;
+    } else if (warp < kPEpi0 || warp >= kPEpi0 + 4) {
+        // dequant: team tm takes the K steps of its parity (the two teams work on consecutive steps at
+        // once); one thread per weight row n, its eight packed words of the group
+        const int dw = deq_index(warp);
+        const int tm = dw / kPTeamWarps;
+        const int n = (dw % kPTeamWarps) * 32 + lane;
+        const uint32_t rx = (uint32_t)(n & 7);  // 128-byte swizzle: 16-byte unit u of row n at (u ^ (n & 7)) * 16
+        RingPos pw, pb;                         // positions of the CTA's running K step
+        if (tm) {
+            pw.next(P::SW);
+            pb.next(P::NB);
+        }
         int e = 0;
         bool ok = true;
         for (int lt = 0; lt < my_tiles && ok; ++lt) {
-            for (int g = 0; g < G; ++g) {
+            for (int g = tm; g < G; g += 2) {  // G % 8 == 0: the parity of g is the parity of the step
                 const int se = e & 1;
-                if ((g & 7) == 0 && !warp_wait(&sbfull[se], (uint32_t)((e >> 1) & 1), abort)) {
+                PF_MARK(warp, lane, 0, lt * G + g);
+                if ((g & 7) == tm && !warp_wait<kPSleep>(&sbfull[se], (uint32_t)((e >> 1) & 1), abort)) {
                     ok = false;
                     break;
                 }
-                if (!warp_wait(&wfull[pw.slot], (uint32_t)(pw.round & 1), abort) ||
-                    (pb.round > 0 && !warp_wait(&bfree[pb.slot], (uint32_t)((pb.round - 1) & 1), abort))) {
+                if (!warp_wait<kPSleep>(&wfull[pw.slot], (uint32_t)(pw.round & 1), abort)) {
                     ok = false;
                     break;
                 }
-                const uint4 wq = *reinterpret_cast<const uint4*>(wring + (size_t)pw.slot * kPW + n * 32 + half * 16);
+                PF_MARK(warp, lane, 1, lt * G + g);
+                if (pb.round > 0 && !warp_wait<kPSleep>(&bfree[pb.slot], (uint32_t)((pb.round - 1) & 1), abort)) {
+                    ok = false;
+                    break;
+                }
+                PF_MARK(warp, lane, 2, lt * G + g);
+                const uint8_t* ws = wring + (size_t)pw.slot * kPW + n * 32;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(ws);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(ws + 16);
                 const uint8_t* sb = sbring + se * 2 * kPSB + n * 16 + (g & 7) * 2;
                 const uint32_t sbits = *reinterpret_cast<const uint16_t*>(sb);
                 const uint32_t bbits = *reinterpret_cast<const uint16_t*>(sb + kPSB);
                 const uint32_t s2 = sbits | (sbits << 16), b2 = bbits | (bbits << 16);
-                uint8_t* out = bbuf + (size_t)pb.slot * kPB;
-                *reinterpret_cast<uint4*>(out + uoff[0]) = dequant_word(wq.x, s2, b2);
-                *reinterpret_cast<uint4*>(out + uoff[1]) = dequant_word(wq.y, s2, b2);
-                *reinterpret_cast<uint4*>(out + uoff[2]) = dequant_word(wq.z, s2, b2);
-                *reinterpret_cast<uint4*>(out + uoff[3]) = dequant_word(wq.w, s2, b2);
+                uint8_t* out = bbuf + (size_t)pb.slot * kPB + n * 128;
+                const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    *reinterpret_cast<uint4*>(out + ((u ^ rx) << 4)) = dequant_word(wv[u], s2, b2);
+                PF_MARK(warp, lane, 3, lt * G + g);
                 fence_proxy_async_smem();  // generic stores -> visible to the tensor core
                 __syncwarp();
+                PF_MARK(warp, lane, 4, lt * G + g);
+                const bool last = (g & 7) == 6 + tm;  // the team's last step on this scale/bias entry
                 if (lane == 0) {
                     mbar_arrive(&wempty[pw.slot]);  // the packed words are consumed (dequantized and stored)
                     mbar_arrive(&bfull[pb.slot]);
-                    if ((g & 7) == 7 || g == G - 1) mbar_arrive(&sbempty[se]);
+                    if (last) mbar_arrive(&sbempty[se]);
                 }
-                if ((g & 7) == 7 || g == G - 1) ++e;
-                pw.next(kPSW);
-                pb.next(kPNB);
+                if (last) ++e;
+                pw.next(P::SW);
+                pw.next(P::SW);
+                pb.next(P::NB);
+                pb.next(P::NB);
             }
         }
     } else {
@@ -350,7 +419,9 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
         for (int lt = 0; lt < my_tiles; ++lt) {
             const int acc = MH == 1 ? (lt & 1) : 0;
             const int use = MH == 1 ? (lt >> 1) : lt;
-            if (!warp_wait(&dfull[acc], (uint32_t)(use & 1), abort)) break;
+            PF_MARK(warp, lane, 0, lt);
+            if (!warp_wait<kPSleep>(&dfull[acc], (uint32_t)(use & 1), abort)) break;
+            PF_MARK(warp, lane, 1, lt);
             tc_fence_after();
             int mt, nt;
             tile_coords(lt, mt, nt);
@@ -367,6 +438,18 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                         uint32_t u0[16];
                         tmem_ld16(dcol + kPN / 2 + c0, u0);
                         tmem_wait_ld();
+                        if (ybf && row_ok && a.vec && (int64_t)nt * ncols + c0 + 16 <= a.N) {
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                pk[i] = swiglu_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]),
+                                                      __uint_as_float(u0[2 * i]), __uint_as_float(u0[2 * i + 1]));
+                            uint4* yp = reinterpret_cast<uint4*>(static_cast<uint16_t*>(L.y) + m * L.ldy +
+                                                                 (int64_t)nt * ncols + c0);
+                            yp[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            yp[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            continue;
+                        }
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             const float g0 = __uint_as_float(r0[i]), x0 = __uint_as_float(u0[i]);
@@ -441,12 +524,13 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&dempty[MH == 1 ? acc : h]);  // this accumulator half is drained
+                PF_MARK(warp, lane, 2 + h, lt);
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kPTmemCols);
     }
