@@ -310,12 +310,11 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 if (MH == 1 && lt >= 2 && !thread_wait<kPSleep>(&dempty[acc], (uint32_t)(((lt >> 1) - 1) & 1), abort)) break;
                 for (int g = 0; g < G; ++g) {
                     PF_MARK(warp, lane, 0, lt * G + g);
-                    if (!thread_wait<kPSleep>(&xfull[px.slot], (uint32_t)(px.round & 1), abort)) {
-                        ok = false;
-                        break;
-                    }
-                    PF_MARK(warp, lane, 1, lt * G + g);
-                    if (!thread_wait<kPSleep>(&bfull[pb.slot], (uint32_t)(pb.round & 1), abort)) {
+                    // both polls in flight at once (the common case: both stages are ready)
+                    const bool xr = mbar_try_wait(&xfull[px.slot], (uint32_t)(px.round & 1));
+                    const bool br = mbar_try_wait(&bfull[pb.slot], (uint32_t)(pb.round & 1));
+                    if (!(xr && br) && (!thread_wait<kPSleep>(&xfull[px.slot], (uint32_t)(px.round & 1), abort) ||
+                                        !thread_wait<kPSleep>(&bfull[pb.slot], (uint32_t)(pb.round & 1), abort))) {
                         ok = false;
                         break;
                     }
