@@ -22,7 +22,8 @@
 //   * warp 1 (one thread): tcgen05.mma kind::f16 (bf16), M=128 N=256 K=16, A = X and B = W from
 //     shared memory, D in TMEM (two 256-column accumulators, so the epilogue of one tile overlaps
 //     the MMAs of the next);
-//   * warps 12-15: epilogue — tcgen05.ld the accumulator (lane = activation row), then store
+//   * warps 12-15 and 23-26, two per TMEM lane quarter (each half of the columns): epilogue —
+//     tcgen05.ld the accumulator (lane = activation row), then store
 //     (bf16 / binary32), SwiGLU of a gate/up tile pair (128 gate + 128 up rows per tile) or a
 //     residual add.
 // Every wait is bounded (2 s): on timeout the kernel records a device error and drains.
@@ -51,12 +52,14 @@ constexpr uint32_t kPB = kPN * 128;           // dequantized W: 256 rows x 64 bf
 constexpr int kPTeamWarps = 8;                // one dequant team: one thread per weight row
 constexpr int kPDeqWarps = 2 * kPTeamWarps;   // two teams, alternate K steps
 // Warp roles by warp index; warp w issues on SM sub-partition w % 4.  The MMA issuer (one thread that
-// must keep the tensor pipe fed) shares its sub-partition with the two producers and one epilogue
-// warp, which mostly sleep on barriers, and only two of the sixteen dequant warps; the other
-// sub-partitions take one epilogue warp and four or five dequant warps each.
+// must keep the tensor pipe fed) shares its sub-partition with the two producers and two epilogue
+// warps, which mostly sleep on barriers, and only two of the sixteen dequant warps; the other
+// sub-partitions take two epilogue warps and four or five dequant warps each.
 constexpr int kPWarpMma = 1, kPWarpX = 5, kPWarpW = 9;
 constexpr int kPEpi0 = 12;                    // epilogue warps 12-15: TMEM lane quarters 0-3
-constexpr int kPThreads = (4 + kPDeqWarps + 3) * 32;
+constexpr int kPEpi1 = 23;                    // second epilogue set 23-26 (quarters 3, 0, 1, 2)
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = (4 + kPDeqWarps + 3 + 4) * 32;
 
 // dequant warp index 0..15 of a warp that has no other role
 __device__ __forceinline__ int deq_index(int warp) {
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             mbar_init(&sbfull[j], 1);
             mbar_init(&sbempty[j], kPDeqWarps);
             mbar_init(&dfull[j], 1);
-            mbar_init(&dempty[j], 4);
+            mbar_init(&dempty[j], kPEpiWarps);
         }
         for (int j = 0; j < P::NB; ++j) {
             mbar_init(&bfull[j], kPTeamWarps);
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
             umma_commit(fin);  // every MMA issued above completes before TMEM is released
             drain_wait(fin, 0);
         }
-    } else if (warp < kPEpi0 || warp >= kPEpi0 + 4) {
+    } else if (warp < kPEpi0 || (warp >= kPEpi0 + 4 && warp < kPEpi1)) {
         // dequant: team tm takes the K steps of its parity (the two teams work on consecutive steps at
         // once); one thread per weight row n, its eight packed words of the group
         const int dw = deq_index(warp);
@@ -429,7 +432,8 @@ __global__ void __launch_bounds__(kPThreads, 1) q4_prefill_kernel(const __grid_c
                 const bool row_ok = m < a.M;
                 const uint32_t dcol = lane_base + (acc + h) * kPN;
                 const int ncols = swiglu ? kPN / 2 : kPN;
-                for (int c0 = 0; c0 < ncols; c0 += 16) {
+                const int cbeg = warp >= kPEpi1 ? ncols / 2 : 0;  // two warps per lane quarter split the columns
+                for (int c0 = cbeg; c0 < cbeg + ncols / 2; c0 += 16) {
                     uint32_t r0[16];
                     float v[16];
                     tmem_ld16(dcol + c0, r0);
