@@ -66,7 +66,8 @@ const char* marlin_q4_version(void);
 const char* marlin_q4_status_string(int status);
 /* cudaError_t of the last failed launch in this thread (0 if none). */
 int marlin_q4_last_cuda_error(void);
-/* Device-side error word of the current device (0 = none; 1 = a bounded wait timed out).
+/* Device-side error word of the current device (0 = none; 1 = a bounded wait timed out; 3 = an
+ * embedding id out of range).
  * Synchronous: copies the word to the host.  clear != 0 resets it to 0. */
 int marlin_q4_device_error(int clear);
 /* Programmatic dependent launch (kernels prefetch weights while their predecessor finishes).
@@ -219,6 +220,14 @@ int marlin_q4_device_free(void* ptr);
 int marlin_q4_ipc_get_handle(const void* ptr, void* handle);
 int marlin_q4_ipc_open_handle(const void* handle, void** ptr);
 int marlin_q4_ipc_close_handle(void* ptr);
+
+/* ---- embedding rows from the tied Q4 table -------------------------------------------------------
+ * MarlinModel::embed_tokens (src/model/marlin.cpp:63-65: mx::take(embed_tokens, ids, 0)) served from
+ * the quantized lm_head it is tied to (src/model/weights.cpp:180-194, :207) instead of a separate
+ * bf16 table: out[i, :] = bf16(scale * q + bias) of row ids[i], each element the exact value
+ * rounded once (round to nearest even).  ids: int32 [m] on the device; out: bf16 [m, table->k],
+ * 16-byte aligned.  An id outside [0, table->n) yields a zero row and device error 3. */
+int marlin_q4_embed(const int32_t* ids, int64_t m, const marlin_q4_tensor* table, uint16_t* out, void* stream);
 
 /* ---- synthetic inputs (benchmark / test support; no counterpart in the reference) ----------------
  * out[i] = bf16(mean + sigma * z_i), z_i a seeded Irwin-Hall(12) variate (mean 0, sd 1), the same

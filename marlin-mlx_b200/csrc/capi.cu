@@ -136,11 +136,13 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
     const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0),
-              v_pf = prefill_device_error(clear != 0), v_st = stack_device_error(clear != 0);
+              v_pf = prefill_device_error(clear != 0), v_st = stack_device_error(clear != 0),
+              v_mi = misc_device_error(clear != 0);
     if (!v) v = v_tc;
     if (!v) v = v_i8;
     if (!v) v = v_pf;
     if (!v) v = v_st;
+    if (!v) v = v_mi;
     if (v < 0) return cuda_status(cudaGetLastError());
     return v;
 }
@@ -168,6 +170,15 @@ int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_
     const Q4Mat v = view(w);
     return gemv_passes(x, x_dtype, m, nullptr, 0.f, v, v, kEpiStore, y, x_dtype, w->n, nullptr, 0, 0,
                        static_cast<cudaStream_t>(stream));
+}
+
+int marlin_q4_embed(const int32_t* ids, int64_t m, const marlin_q4_tensor* table, uint16_t* out, void* stream) {
+    int rc = check_tensor(table);
+    if (rc) return rc;
+    if (!ids || !out || m <= 0) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(ids, 4) || !aligned(out, 16)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_embed_q4(ids, m, table->weight, table->scales, table->biases, table->n, table->k, out,
+                                       static_cast<cudaStream_t>(stream)));
 }
 
 int marlin_q4_rms_norm(const void* x, int32_t x_dtype, const uint16_t* weight, int64_t m, int64_t h, float eps,

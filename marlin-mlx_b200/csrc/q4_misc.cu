@@ -1,5 +1,7 @@
-// q4_misc.cu — Q4 quantize/pack, standalone RMSNorm, and the seeded synthetic-input generator.
+// q4_misc.cu — Q4 quantize/pack, standalone RMSNorm, the Q4 embedding gather, and the seeded
+// synthetic-input generator.
 #include "common.cuh"
+#include "q4_host.cuh"
 #include "q4_misc.cuh"
 
 namespace marlin {
@@ -149,6 +151,33 @@ __global__ void residual_add_kernel(const void* __restrict__ h, int dtype, const
     }
 }
 
+// Rows `ids` of a Q4 table dequantized to bf16, out[i, :] = bf16(s q + b) per element with one
+// rounding of the exact value (the operand the prefill GEMM builds): the embedding lookup
+// MarlinModel::embed_tokens (src/model/marlin.cpp:63-65, mx::take of the embedding table) served
+// from the tied, quantized lm_head instead of a separate bf16 table.  One CTA per row; each thread
+// turns packed words into 16-byte row segments.  An id outside [0, n) writes a zero row and records
+// kDevErrBadIndex.
+__global__ void __launch_bounds__(256) embed_q4_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ wq,
+                                                       const uint16_t* __restrict__ scales,
+                                                       const uint16_t* __restrict__ biases, int64_t n, int64_t k,
+                                                       uint16_t* __restrict__ out) {
+    const int64_t i = blockIdx.x;
+    const int32_t id = ids[i];
+    const bool ok = id >= 0 && id < n;
+    if (!ok && threadIdx.x == 0) record_device_error(kDevErrBadIndex);
+    const int64_t words = k / 8, groups = k / 64;
+    uint4* orow = reinterpret_cast<uint4*>(out + i * k);
+    for (int64_t w = threadIdx.x; w < words; w += blockDim.x) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (ok) {
+            const int64_t g = (int64_t)id * groups + w / 8;
+            const uint32_t sb = scales[g], bb = biases[g];
+            v = dequant_word(wq[(int64_t)id * words + w], sb | (sb << 16), bb | (bb << 16));
+        }
+        orow[w] = v;
+    }
+}
+
 int sm_count() {
     static int n = 0;
     if (!n) {
@@ -186,6 +215,15 @@ cudaError_t launch_residual_add(const void* h, int dtype, const float* y, int64_
     residual_add_kernel<<<(unsigned)blocks, 256, 0, stream>>>(h, dtype, y, n, out);
     return cudaGetLastError();
 }
+
+cudaError_t launch_embed_q4(const int32_t* ids, int64_t m, const uint32_t* wq, const uint16_t* scales,
+                            const uint16_t* biases, int64_t n, int64_t k, uint16_t* out, cudaStream_t stream) {
+    if (m <= 0) return cudaSuccess;
+    embed_q4_kernel<<<(unsigned)m, 256, 0, stream>>>(ids, wq, scales, biases, n, k, out);
+    return cudaGetLastError();
+}
+
+int misc_device_error(bool clear) { return tu_device_error(clear); }
 
 cudaError_t launch_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float sigma, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;

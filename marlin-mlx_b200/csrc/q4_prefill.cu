@@ -92,31 +92,6 @@ struct PrefillArgs {
     int vec;               // 1: y (and resid) rows allow 16-byte vector access at 16-column steps
 };
 
-__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// Eight codes of one packed word -> eight bf16 weights s*q + b in natural K order (4 registers).
-// LOP3 gives the pair (128 + q_i, 128 + q_i+4) as bf16 (exact), one FMA removes the 128 and one
-// FMA forms q s + b with a single rounding; PRMTs regroup the pairs into K order 0..7.
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2, uint32_t b2) {
-    constexpr uint32_t kOne2 = 0x3F803F80u, kNeg128 = 0xC300C300u, kMagic = 0x43004300u;
-    uint32_t p[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t v = lop3_and_or(w >> (4 * i), 0x000F000Fu, kMagic);
-        p[i] = bf16x2_fma(bf16x2_fma(v, kOne2, kNeg128), s2, b2);  // (w_i, w_i+4)
-    }
-    uint4 o;
-    o.x = __byte_perm(p[0], p[1], 0x5410);  // (w0, w1)
-    o.y = __byte_perm(p[2], p[3], 0x5410);  // (w2, w3)
-    o.z = __byte_perm(p[0], p[1], 0x7632);  // (w4, w5)
-    o.w = __byte_perm(p[2], p[3], 0x7632);  // (w6, w7)
-    return o;
-}
-
 __device__ __forceinline__ float swiglu_bf16(float g, float u) {
     const float gq = bf16_round(g), uq = bf16_round(u);
     const float sg = bf16_round(__fdividef(1.0f, 1.0f + expf(-gq)));

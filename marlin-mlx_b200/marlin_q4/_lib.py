@@ -66,6 +66,7 @@ SIGNATURES = {
     "marlin_q4_ipc_get_handle": (ctypes.c_int, [_vp, _vp]),
     "marlin_q4_ipc_open_handle": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "marlin_q4_ipc_close_handle": (ctypes.c_int, [_vp]),
+    "marlin_q4_embed": (ctypes.c_int, [_vp, _i64, _PT, _vp, _vp]),
     "marlin_q4_synth_bf16": (ctypes.c_int, [_vp, _i64, _u64, _f32, _f32, _vp]),
 }
 

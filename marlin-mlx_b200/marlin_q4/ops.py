@@ -191,6 +191,32 @@ def lm_head_argmax(hidden: torch.Tensor, lm: QuantizedTensor, norm_weight: torch
     return ids, best
 
 
+def next_token_after_prefill(hidden: torch.Tensor, lm: QuantizedTensor, norm_weight: torch.Tensor | None = None,
+                             eps: float = 1e-6, workspace: LmHeadWorkspace | None = None):
+    """Greedy token that starts the decode loop after a prefill of S rows.
+
+    The reference runs lm_head over all S rows of the prefill hidden state (src/core/engine.cpp:64)
+    and sample_token keeps only the last position (src/sampling/sampler.cpp:10-15); only that row's
+    logits matter, so this runs the final norm + fused lm_head/argmax on the last row alone (one
+    GEMV over the 248K-row head instead of an S-row GEMM).  hidden: [S, H] or [1, S, H].
+    Returns (ids int32 [1], best float32 [1])."""
+    h2 = hidden.reshape(-1, hidden.shape[-1])
+    return lm_head_argmax(h2[-1:], lm, norm_weight, eps, workspace=workspace)
+
+
+def embed_q4(ids: torch.Tensor, table: QuantizedTensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Embedding rows from the tied Q4 table (marlin_q4_embed): bf16(s*q + b) of rows `ids`."""
+    _cuda(ids, "ids")
+    assert ids.dtype == torch.int32
+    m = ids.numel()
+    if out is None:
+        out = torch.empty((m, table.k), dtype=torch.bfloat16, device=ids.device)
+    tc = table.c()
+    check(_lib.load().marlin_q4_embed(ids.data_ptr(), m, ctypes.byref(tc), out.data_ptr(), _stream()),
+          "marlin_q4_embed")
+    return out
+
+
 def decode_keys(keys: torch.Tensor):
     m = keys.numel()
     ids = torch.empty(m, dtype=torch.int32, device=keys.device)
@@ -236,6 +262,30 @@ class DecodeStep:
             ctypes.byref(self.c_lm), self.ids.data_ptr(), self.best.data_ptr(), self.h.data_ptr(), self.ws.data_ptr(),
             self.ws_bytes, _stream()), "marlin_q4_decode_step")
         return self.ids, self.best, self.h
+
+
+class GreedyLoop:
+    """run_decode_loop's greedy path (src/core/engine.cpp:79-94) on the device: per token, the
+    embedding rows of the current ids from the tied Q4 table (embed_q4), one DecodeStep, and its ids
+    fed back, with no host synchronisation between tokens (the reference syncs every step, :80).
+    Every kernel of one token is stream-ordered, so a caller may capture tokens in a CUDA graph."""
+
+    def __init__(self, layers: list[Layer], final_norm: torch.Tensor, lm: QuantizedTensor, m: int,
+                 eps: float = 1e-6):
+        self.step = DecodeStep(layers, final_norm, lm, m, eps)
+        self.lm = lm
+        self.h0 = torch.empty((m, lm.k), dtype=torch.bfloat16, device=final_norm.device)
+
+    def __call__(self, ids0: torch.Tensor, n_tokens: int) -> torch.Tensor:
+        """ids0: int32 [m] on the device.  Returns int32 [n_tokens, m]: the ids of each step."""
+        out = torch.empty((n_tokens, ids0.numel()), dtype=torch.int32, device=ids0.device)
+        cur = ids0
+        for t in range(n_tokens):
+            embed_q4(cur, self.lm, out=self.h0)
+            ids, _, _ = self.step(self.h0)
+            out[t].copy_(ids)
+            cur = out[t]
+        return out
 
 
 def synth_bf16(shape, seed: int, mean: float = 0.0, sigma: float = 1.0, device="cuda") -> torch.Tensor:
