@@ -30,7 +30,8 @@
 #include <algorithm>
 
 // Optional timeline hooks of the decode GEMV kernel, empty in the library build: I8_MARK_BEGIN()
-// at entry, I8_MARK(point) at phase boundaries (evaluated by thread 0 of each CTA).
+// at entry, I8_MARK(point) at phase boundaries (evaluated by thread 0 of each CTA), I8_STAGE_MARK(q)
+// when stage q of the ring is ready.
 #ifndef I8_MARK_BEGIN
 #define I8_MARK_BEGIN()
 #endif
@@ -362,6 +363,7 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
         }
     } else {
         const bool xin_ok = !L.has_xin || warp_wait(xbar, 0u, abort);
+        I8_MARK(14);
         int slot = 0;  // ring position of stage q, kept as a counter (no division per stage)
         uint32_t ph = 0u;
         for (int q = 0; xin_ok && q < nst; ++q) {
