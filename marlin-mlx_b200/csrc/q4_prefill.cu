@@ -17,7 +17,7 @@
 //     group into bf16 W[256 x 64] in shared memory, K-major with 128-byte swizzle (the tcgen05
 //     operand layout): per pair of codes one LOP3 (128 + q as bf16, exact), one FMA removing the
 //     128 (exact) and one FMA q s + b (bf16x2, a single rounding), then PRMTs restore natural K
-//     order; three buffers (two for 256-row tiles), so a team's fence and waits overlap the other
+//     order; three buffers, so a team's fence and waits overlap the other
 //     team's work;
 //   * warp 1 (one thread): tcgen05.mma kind::f16 (bf16), M=128 N=256 K=16, A = X and B = W from
 //     shared memory, D in TMEM (two 256-column accumulators, so the epilogue of one tile overlaps
@@ -73,9 +73,9 @@ constexpr bool kPSleep = true;                // waiting threads sleep on the mb
 // dequantizes each weight tile once for twice the MMA work (its epilogue then stalls the MMAs).
 template <int MH>
 struct PPlan {
-    static constexpr int SX = MH == 1 ? 4 : 3;  // X ring stages
+    static constexpr int SX = MH == 1 ? 4 : 2;  // X ring stages
     static constexpr int SW = 6;                // packed-word ring stages
-    static constexpr int NB = MH == 1 ? 3 : 2;  // dequantized W buffers
+    static constexpr int NB = 3;                // dequantized W buffers
     static constexpr uint32_t XSTAGE = MH * kPA;
     static constexpr uint32_t OFF_W = SX * XSTAGE;
     static constexpr uint32_t OFF_SB = OFF_W + SW * kPW;
