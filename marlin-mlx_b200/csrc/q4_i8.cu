@@ -424,6 +424,7 @@ __global__ void __launch_bounds__(kI8Threads, 2) i8_unit_kernel(const __grid_con
             if (row_factor) o[m] *= tx.rf[m];
         }
     }
+    I8_MARK(16);
     if (kSwiglu) {
         // up rows (64..127) hand their outputs to the gate rows through shared memory
         float* xch = red + (size_t)CL * kI8Rows * MS;
