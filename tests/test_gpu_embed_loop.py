@@ -88,3 +88,44 @@ def test_next_token_after_prefill_is_last_row_argmax():
     assert ids.shape == (1,)
     assert int(ids[0]) == int(all_ids[-1]) and float(best[0]) == float(all_best[-1])
     assert mq.device_error() == 0
+
+
+def test_greedy_token_in_cuda_graph():
+    """One token of the loop (embedding from the fed-back ids, the step, the ids copied back)
+    captured once and replayed equals the eager loop token for token."""
+    H, I, V, m, T = 512, 1024, 2048, 2, 5
+    layers = []
+    for l in range(2):
+        layers.append(mq.Layer(mq.synth_bf16((H,), 873 + 4 * l, 0.1, 0.02),
+                               mq.quantize_weight(mq.synth_bf16((I, H), 870 + 4 * l, 0.0, 0.02)),
+                               mq.quantize_weight(mq.synth_bf16((I, H), 871 + 4 * l, 0.0, 0.02)),
+                               mq.quantize_weight(mq.synth_bf16((H, I), 872 + 4 * l, 0.0, 0.02))))
+    lm = mq.quantize_weight(mq.synth_bf16((V, H), 890, 0.0, 0.02))
+    fn = mq.synth_bf16((H,), 891, 0.1, 0.02)
+    ids0 = torch.tensor([11, 1999], dtype=torch.int32, device="cuda")
+    want = mq.GreedyLoop(layers, fn, lm, m)(ids0, T)
+    loop = mq.GreedyLoop(layers, fn, lm, m)
+    cur = ids0.clone()
+
+    def token():
+        mq.embed_q4(cur, lm, out=loop.h0)
+        ids, _, _ = loop.step(loop.h0)
+        cur.copy_(ids)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        token()  # warm-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    cur.copy_(ids0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        token()
+    cur.copy_(ids0)
+    got = []
+    for _ in range(T):
+        g.replay()
+        got.append(cur.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(torch.stack(got), want)
+    assert mq.device_error() == 0
