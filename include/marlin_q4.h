@@ -179,7 +179,8 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
  * (src/sampling/sampler.cpp:15).  h0: bf16 [m, hidden] embedding rows.  ids [m]; best [m]
  * (optional); h_out: binary32 [m, hidden] hidden state before the final norm (optional).
  * n_layers >= 1.
- * Runs as two kernels per layer plus the lm_head; with MARLIN_Q4_PATH_ONEKERNEL (m <= 4, hidden a
+ * Runs as two kernels per layer plus the lm_head (more than 16 rows: in consecutive 16-row chunks,
+ * each a full step; rows are independent); with MARLIN_Q4_PATH_ONEKERNEL (m <= 4, hidden a
  * multiple of 512, intermediate of 1024, at most 24 layers of equal shape) the layers run as one
  * persistent cooperative kernel (all SMs, software grid barriers between the gate/up and down
  * phases of each layer) before the lm_head kernel.

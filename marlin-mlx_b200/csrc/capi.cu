@@ -301,8 +301,10 @@ size_t step_ssq_bytes(int64_t m, int64_t hidden) { return align16((size_t)((hidd
 // h and act (binary32), then the activation planes handed between the integer-MMA kernels
 size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
     size_t b = align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
-    if (m <= kI8MaxRows) b = (b + 255) / 256 * 256 + i8_planes_bytes(m, inter) + i8_planes_bytes(m, hidden) +
-                             step_ssq_bytes(m, hidden);
+    if (m <= kI8MaxRows)
+        b = (b + 255) / 256 * 256 + i8_planes_bytes(m, inter) + i8_planes_bytes(m, hidden) + step_ssq_bytes(m, hidden);
+    else  // h for all rows, then the scratch of one chunk of kI8MaxRows rows (the step runs in row chunks)
+        b = std::max(b, align16((size_t)m * hidden * 4) + step_compose_bytes(kI8MaxRows, hidden, inter));
     return b;
 }
 
@@ -473,6 +475,20 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
         i8_supported(inter, m) && hidden % 128 == 0)
         return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h, scratch,
                                   lmws, st);
+    if (decode_path() == kPathI8 && uniform && i8_supported(hidden, kI8MaxRows) &&
+        i8_supported(inter, kI8MaxRows) && hidden % 128 == 0) {
+        // more rows than one plane hand-off serves: the rows are independent (per-row norm, GEMV and
+        // argmax), so the step runs on consecutive chunks of kI8MaxRows rows, stream-ordered, each
+        // chunk in the scratch after h
+        uint8_t* cs = scratch + align16((size_t)m * hidden * 4);
+        for (int64_t r0 = 0; r0 < m; r0 += kI8MaxRows) {
+            const int64_t mc = std::min<int64_t>(kI8MaxRows, m - r0);
+            if ((rc = decode_step_planes(h0 + r0 * hidden, mc, hidden, inter, n_layers, layers, final_norm, eps, lm,
+                                         ids + r0, best ? best + r0 : nullptr, h + r0 * hidden, cs, lmws, st)))
+                return rc;
+        }
+        return MARLIN_Q4_OK;
+    }
     const void* cur = h0;
     int32_t cur_dtype = MARLIN_Q4_BF16;
     for (int32_t l = 0; l < n_layers; ++l) {

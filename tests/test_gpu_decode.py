@@ -1,8 +1,9 @@
 """GPU parity: the full Q4 decode stack (config 5) — 24 x [RMSNorm(1+w) -> Q4 MLP -> residual] ->
 final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
 
-Both forms of the step are checked: the per-kernel composition (default) and the one persistent
-cooperative kernel ("onekernel" family, m <= 8, grid barriers between phases)."""
+Both forms of the step are checked: the per-kernel composition (default; above 16 rows it runs in
+16-row chunks) and the one persistent cooperative kernel ("onekernel" family, grid barriers between
+phases; rows it does not take fall back to the single-op kernels)."""
 import numpy as np
 import pytest
 import torch
@@ -37,7 +38,7 @@ def family(request):
     mq.set_decode_path("i8")
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 12, 16])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 12, 16, 20, 32])
 def test_decode_step_matches_oracle(oracle, model, family, m):
     layers, hl, lm, hlm, fn, hfn = model
     step = mq.DecodeStep(layers, fn, lm, m)
