@@ -66,28 +66,28 @@ const char* marlin_q4_version(void);
 const char* marlin_q4_status_string(int status);
 /* cudaError_t of the last failed launch in this thread (0 if none). */
 int marlin_q4_last_cuda_error(void);
-/* Device-side error word of the current device (0 = none; 1 = a bounded wait timed out; 3 = an
- * embedding id out of range).
- * Synchronous: copies the word to the host.  clear != 0 resets it to 0. */
+/* Device-side error word of the current device (0 = none; 1 = a bounded wait timed out, on this
+ * GPU's own copies or on a peer's exchange words; 3 = an embedding id out of range).
+ * Synchronous: copies the word to the host.  clear != 0 resets it to 0.  While the word is set,
+ * the exchange waits of marlin_q4_tp_decode_step return at once (see there): clear it before the
+ * next step once the ranks are known to be in step again. */
 int marlin_q4_device_error(int clear);
+/* Bound of each wait for a peer GPU's exchange word in marlin_q4_tp_decode_step, in SM clock
+ * cycles (process-wide, read when a step is issued; a step captured in a CUDA graph keeps the
+ * value it was captured with).  0 restores the default, 4e9 cycles (about 2 s at 2 GHz). */
+void marlin_q4_set_wait_limit_cycles(uint64_t cycles);
 /* Programmatic dependent launch (kernels prefetch weights while their predecessor finishes).
  * Enabled by default; enable = 0 launches every kernel with plain stream ordering. */
 void marlin_q4_set_pdl(int enable);
-/* Decode kernel family (process-wide; every family computes the same function, within the float
- * tolerance, and each is tested against the CPU checker):
+/* Decode kernel family (process-wide; both compute the same function, within the float tolerance,
+ * and each is tested against the CPU checker):
  *   MARLIN_Q4_PATH_I8MMA   (default) integer tensor-core MMAs on the raw codes and 4 s8 activation
  *                          planes, exact int32 accumulation (k % 512 == 0, m <= 16 per launch);
- *   MARLIN_Q4_PATH_TCGEN05 5th-generation tensor cores: bf16 codes in TMEM, tcgen05.mma
- *                          (k % 512 == 0, m * planes <= 32);
- *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0);
- *   MARLIN_Q4_PATH_ONEKERNEL the integer-MMA kernels, and the layers of marlin_q4_decode_step as one
- *                          persistent cooperative kernel (m <= 4, at most 24 equal layers).
- * Shapes a family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns MARLIN_Q4_ERR_ARG
- * for an unknown path. */
+ *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0).
+ * Shapes the integer-MMA family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns
+ * MARLIN_Q4_ERR_ARG for an unknown path. */
 #define MARLIN_Q4_PATH_I8MMA 0
-#define MARLIN_Q4_PATH_TCGEN05 1
 #define MARLIN_Q4_PATH_BF16MMA 2
-#define MARLIN_Q4_PATH_ONEKERNEL 3
 int marlin_q4_set_decode_path(int path);
 
 /* ---- quantize --------------------------------------------------------------------------------
@@ -107,6 +107,16 @@ int marlin_q4_quantize(const uint16_t* w, int64_t n, int64_t k, int32_t group_si
  * exact up to binary32 accumulation.  gate_up_swiglu and matmul_residual dispatch the same way. */
 int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, void* y,
                      void* stream);
+
+/* The same product with a binary32 result whatever x's dtype: the partial of a projection whose
+ * input features are split across GPUs (the tensor-parallel down_proj of mlp_forward,
+ * src/model/marlin.cpp:34), which the ranks sum before it is rounded to the activation dtype.
+ * Dispatches like marlin_q4_matmul (bf16 x above 16 rows: the tcgen05 GEMM). */
+int marlin_q4_matmul_f32(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, float* y,
+                         void* stream);
+/* out[i] = bf16(x[i]) (round to nearest even): the summed binary32 partials back in the activation
+ * dtype mlp_forward returns for bf16 x (src/model/marlin.cpp:31-35). */
+int marlin_q4_cast_bf16(const float* x, int64_t count, uint16_t* out, void* stream);
 
 /* ---- RMSNorm -------------------------------------------------------------------------------------
  * Replaces rms_norm (src/model/marlin.cpp:12-16): x * rsqrt(mean(x^2) + eps) * (1 + w), evaluated
@@ -155,16 +165,16 @@ size_t marlin_q4_lm_head_workspace_size(int64_t m);
 
 /* marlin_q4_lm_head_argmax without a workspace argument.  No counterpart in the reference: it
  * exists for callers that cannot allocate or own device scratch for this call, such as a binding
- * that replaces MarlinModel::lm_head + sample_token (src/model/marlin.cpp:161-169,
- * src/sampling/sampler.cpp:14-16), whose call shape carries no buffer, or a runtime that must not
- * call cudaMalloc (a device-wide synchronisation) inside its decode loop.  Same arguments and
- * results as marlin_q4_lm_head_argmax otherwise.
- * The keys live in one library-owned device array per device (zeroed at module load, left zeroed
- * by every call); nothing is allocated.  m > MARLIN_Q4_LM_HEAD_STATIC_MAX_ROWS returns
- * MARLIN_Q4_ERR_UNSUPPORTED.  All calls on one device share that array: calls that can overlap in
- * time (different streams, unordered host threads) race and return wrong ids, so keep them on one
- * stream.  The first call on each device looks the array up (cudaGetSymbolAddress) and must be made
- * outside stream capture. */
+ * that replaces the lm_head + greedy sampling pair, whose call shape carries no buffer, or a
+ * runtime that must not call cudaMalloc (a device-wide synchronisation) inside its decode loop.
+ * Same arguments and results as marlin_q4_lm_head_argmax otherwise.
+ * The keys live in one library-owned device array per device; each call first clears the part it
+ * uses (cudaMemsetAsync on the caller's stream), so a call never depends on what an earlier call,
+ * even an aborted one, left there.  Nothing is allocated.  m > MARLIN_Q4_LM_HEAD_STATIC_MAX_ROWS
+ * returns MARLIN_Q4_ERR_UNSUPPORTED.  All calls on one device share that array: calls that can
+ * overlap in time (different streams, unordered host threads) race and return wrong ids, so keep
+ * them on one stream.  The first call on each device (and the first after the device's context has
+ * been reset) looks the array up (cudaGetSymbolAddress) and must be made outside stream capture. */
 #define MARLIN_Q4_LM_HEAD_STATIC_MAX_ROWS 64
 int marlin_q4_lm_head_argmax_static(const void* hidden, int32_t dtype, int64_t m, const uint16_t* norm_weight,
                                     float eps, const marlin_q4_tensor* lm, int64_t vocab_offset, int32_t* ids,
@@ -180,10 +190,7 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
  * (optional); h_out: binary32 [m, hidden] hidden state before the final norm (optional).
  * n_layers >= 1.
  * Runs as two kernels per layer plus the lm_head (more than 16 rows: in consecutive 16-row chunks,
- * each a full step; rows are independent); with MARLIN_Q4_PATH_ONEKERNEL (m <= 4, hidden a
- * multiple of 512, intermediate of 1024, at most 24 layers of equal shape) the layers run as one
- * persistent cooperative kernel (all SMs, software grid barriers between the gate/up and down
- * phases of each layer) before the lm_head kernel.
+ * each a full step; rows are independent).
  * workspace: >= marlin_q4_decode_step_workspace_size bytes, 256-byte aligned, zero-filled before
  * the first call (its head is left zeroed by every call); one workspace serves one (m, hidden,
  * intermediate) shape; zero it again before using it for another. */
@@ -206,13 +213,19 @@ size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t i
  * from marlin_q4_device_alloc, the others from marlin_q4_ipc_open_handle), each
  * marlin_q4_tp_exchange_size bytes, zero before the first call (it then holds the rank's step
  * counter and the last values exchanged).  All ranks must call the step the same number of times,
- * at most 120 layers.  m <= 16, hidden a multiple of 512, down_proj K a multiple of
- * 512.  workspace as for marlin_q4_decode_step with intermediate = down_proj K. */
+ * at most 120 layers.  hidden a multiple of 512, down_proj K a multiple of 512; more than 16 rows
+ * run as consecutive 16-row chunks, each a full step with its own exchanges.  workspace as for
+ * marlin_q4_decode_step with intermediate = down_proj K.
+ * A peer that stops writing (a dead rank): the first wait that runs out (marlin_q4_set_wait_limit_cycles)
+ * sets device error 1 and every later exchange wait returns at once, so the step still completes,
+ * its ids and h void; the host reads marlin_q4_device_error after the step.  The workspace keeps its
+ * zero invariant through such a step. */
 int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
                              const marlin_q4_layer* layers, const uint16_t* final_norm, float eps,
                              const marlin_q4_tensor* lm_shard, int64_t vocab_offset, int32_t* ids, float* best,
                              float* h_out, int32_t tp_rank, int32_t tp_size, void* const* exchange, void* workspace,
                              size_t workspace_bytes, void* stream);
+/* Bytes of one rank's exchange buffer (rows beyond 16 reuse the 16-row layout chunk by chunk). */
 size_t marlin_q4_tp_exchange_size(int64_t m, int64_t hidden, int32_t tp);
 /* Zero-filled device memory for an exchange buffer (cudaMalloc: its IPC handle covers exactly it). */
 int marlin_q4_device_alloc(size_t bytes, void** ptr);

@@ -8,8 +8,6 @@
 #include "q4_gemv.cuh"
 #include "q4_i8.cuh"
 #include "q4_prefill.cuh"
-#include "q4_stack.cuh"
-#include "q4_tc.cuh"
 #include "q4_misc.cuh"
 
 #include <algorithm>
@@ -21,6 +19,7 @@ namespace {
 
 thread_local int t_last_cuda_error = 0;
 bool g_pdl = true;
+unsigned long long g_peer_wait_cycles = kPeerWaitDefaultCycles;
 
 int cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return MARLIN_Q4_OK;
@@ -135,19 +134,20 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
-    const int v_tc = tc_device_error(clear != 0), v_i8 = i8_device_error(clear != 0),
-              v_pf = prefill_device_error(clear != 0), v_st = stack_device_error(clear != 0),
+    const int v_i8 = i8_device_error(clear != 0), v_pf = prefill_device_error(clear != 0),
               v_mi = misc_device_error(clear != 0);
-    if (!v) v = v_tc;
     if (!v) v = v_i8;
     if (!v) v = v_pf;
-    if (!v) v = v_st;
     if (!v) v = v_mi;
     if (v < 0) return cuda_status(cudaGetLastError());
     return v;
 }
 
 void marlin_q4_set_pdl(int enable) { g_pdl = enable != 0; }
+
+void marlin_q4_set_wait_limit_cycles(uint64_t cycles) {
+    g_peer_wait_cycles = cycles ? (unsigned long long)cycles : kPeerWaitDefaultCycles;
+}
 
 int marlin_q4_set_decode_path(int path) {
     return set_decode_path(path) ? MARLIN_Q4_OK : MARLIN_Q4_ERR_ARG;
@@ -170,6 +170,24 @@ int marlin_q4_matmul(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_
     const Q4Mat v = view(w);
     return gemv_passes(x, x_dtype, m, nullptr, 0.f, v, v, kEpiStore, y, x_dtype, w->n, nullptr, 0, 0,
                        static_cast<cudaStream_t>(stream));
+}
+
+int marlin_q4_matmul_f32(const void* x, int32_t x_dtype, int64_t m, const marlin_q4_tensor* w, float* y,
+                         void* stream) {
+    int rc = check_tensor(w);
+    if (rc) return rc;
+    if ((rc = check_act16(x, x_dtype))) return rc;
+    if ((rc = check_act(y, MARLIN_Q4_F32))) return rc;
+    if (m <= 0) return MARLIN_Q4_ERR_ARG;
+    const Q4Mat v = view(w);
+    return gemv_passes(x, x_dtype, m, nullptr, 0.f, v, v, kEpiStore, y, MARLIN_Q4_F32, w->n, nullptr, 0, 0,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int marlin_q4_cast_bf16(const float* x, int64_t count, uint16_t* out, void* stream) {
+    if (!x || !out || count <= 0) return MARLIN_Q4_ERR_ARG;
+    if (!aligned(x, 4) || !aligned(out, 2)) return MARLIN_Q4_ERR_ALIGN;
+    return cuda_status(launch_cast_bf16(x, count, out, static_cast<cudaStream_t>(stream)));
 }
 
 int marlin_q4_embed(const int32_t* ids, int64_t m, const marlin_q4_tensor* table, uint16_t* out, void* stream) {
@@ -292,9 +310,8 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
                                           static_cast<cudaStream_t>(stream)));
 }
 
-// Workspace of marlin_q4_decode_step: a zero-invariant head (grid-barrier words and the argmax keys,
-// zero before the first call and left zero by every call, whichever kernels run) followed by
-// scratch for either the one-kernel step or the per-kernel composition.
+// Workspace of marlin_q4_decode_step: a zero-invariant head (the argmax keys and CTA counter, zero
+// before the first call and left zero by every call) followed by the step's scratch.
 namespace {
 size_t step_zero_bytes(int64_t m) { return 256 + align16((size_t)m * 8 + 16); }
 size_t step_ssq_bytes(int64_t m, int64_t hidden) { return align16((size_t)((hidden + 127) / 128) * m * 4); }
@@ -411,8 +428,7 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
 
 size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate) {
     if (m <= 0 || hidden <= 0 || intermediate <= 0) return 0;
-    return step_zero_bytes(m) + std::max(step_compose_bytes(m, hidden, intermediate),
-                                         stack_scratch_size(m, hidden, intermediate));
+    return step_zero_bytes(m) + step_compose_bytes(m, hidden, intermediate);
 }
 
 int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t n_layers,
@@ -446,28 +462,6 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     uint8_t* scratch = ws + step_zero_bytes(m);
     void* lmws = ws + 256;  // keys + counter, zero-invariant
-    if (decode_path() == kPathOneKernel && uniform && stack_supported(m, hidden, inter, n_layers)) {
-        // all layers as one persistent kernel, then the fused lm_head + argmax
-        StackLayer sl[kStackMaxLayers];
-        for (int32_t l = 0; l < n_layers; ++l)
-            sl[l] = StackLayer{layers[l].post_attn_norm, view(&layers[l].gate_proj), view(&layers[l].up_proj),
-                               view(&layers[l].down_proj)};
-        StackLaunch S{};
-        S.h0 = h0;
-        S.h0_dtype = MARLIN_Q4_BF16;
-        S.m = m;
-        S.hidden = hidden;
-        S.inter = inter;
-        S.n_layers = n_layers;
-        S.layers = sl;
-        S.eps = eps;
-        S.h_out = h_out;
-        S.bar = reinterpret_cast<unsigned*>(ws);
-        S.scratch = scratch;
-        if ((rc = cuda_status(launch_stack(S, st)))) return rc;
-        return marlin_q4_lm_head_argmax(stack_output(S), MARLIN_Q4_F32, m, final_norm, eps, lm, 0, ids, best, nullptr,
-                                        lmws, marlin_q4_lm_head_workspace_size(m), st);
-    }
     float* h = reinterpret_cast<float*>(scratch);
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
@@ -507,7 +501,7 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
 // ---- tensor-parallel decode step ------------------------------------------------------------------
 size_t marlin_q4_tp_exchange_size(int64_t m, int64_t hidden, int32_t tp) {
     if (m <= 0 || hidden <= 0 || tp < 1) return 0;
-    return tp_layout(m, hidden, tp).total;
+    return tp_layout(std::min<int64_t>(m, kI8MaxRows), hidden, tp).total;
 }
 
 int marlin_q4_device_alloc(size_t bytes, void** ptr) {
@@ -567,16 +561,20 @@ int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int3
             L.down_proj.n != hidden || L.down_proj.k != inter || L.gate_proj.n > inter || L.gate_proj.n % 64)
             return MARLIN_Q4_ERR_SHAPE;
     }
-    if (m > kI8MaxRows || hidden % 128 || !i8_supported(hidden, m) || !i8_supported(inter, m))
-        return MARLIN_Q4_ERR_UNSUPPORTED;
+    // more than kI8MaxRows rows run as consecutive chunks of kI8MaxRows rows, each a full step with
+    // its own exchanges (the step counter advances once per chunk on every rank, so the tags of one
+    // chunk never match another's); the exchange layout is that of one chunk
+    const int64_t mc = std::min<int64_t>(m, kI8MaxRows);
+    if (hidden % 128 || !i8_supported(hidden, mc) || !i8_supported(inter, mc)) return MARLIN_Q4_ERR_UNSUPPORTED;
     if (!workspace || !aligned(workspace, 256) ||
         workspace_bytes < marlin_q4_decode_step_workspace_size(m, hidden, inter))
         return MARLIN_Q4_ERR_WORKSPACE;
-    const TpLayout lay = tp_layout(m, hidden, tp_size);
+    const TpLayout lay = tp_layout(mc, hidden, tp_size);
     if (n_layers > 120) return MARLIN_Q4_ERR_UNSUPPORTED;  // exchange tags hold the layer in 7 bits
     TpExchange X{};
     X.tp = tp_size;
     X.rank = tp_rank;
+    X.wait_cycles = g_peer_wait_cycles;
     for (int r = 0; r < tp_size; ++r) {
         uint8_t* b = static_cast<uint8_t*>(exchange[r]);
         if (!b || !aligned(b, 256)) return MARLIN_Q4_ERR_ARG;
@@ -587,8 +585,20 @@ int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int3
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     uint8_t* scratch = ws + step_zero_bytes(m);
     float* h = h_out ? h_out : reinterpret_cast<float*>(scratch);
-    return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm_shard, ids, best, h, scratch,
-                              ws + 256, static_cast<cudaStream_t>(stream), &X, vocab_offset);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (m <= kI8MaxRows)
+        return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm_shard, ids, best, h,
+                                  scratch, ws + 256, st, &X, vocab_offset);
+    // chunk scratch after h (as in marlin_q4_decode_step)
+    uint8_t* cs = scratch + align16((size_t)m * hidden * 4);
+    for (int64_t r0 = 0; r0 < m; r0 += kI8MaxRows) {
+        const int64_t n = std::min<int64_t>(kI8MaxRows, m - r0);
+        if ((rc = decode_step_planes(h0 + r0 * hidden, n, hidden, inter, n_layers, layers, final_norm, eps, lm_shard,
+                                     ids + r0, best ? best + r0 : nullptr, h + r0 * hidden, cs, ws + 256, st, &X,
+                                     vocab_offset)))
+            return rc;
+    }
+    return MARLIN_Q4_OK;
 }
 
 int marlin_q4_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float sigma, void* stream) {

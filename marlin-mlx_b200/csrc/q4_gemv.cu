@@ -33,7 +33,6 @@
 #include "q4_gemv.cuh"
 #include "q4_stage.cuh"
 #include "q4_i8.cuh"
-#include "q4_tc.cuh"
 
 #include <cuda.h>
 
@@ -651,16 +650,7 @@ __global__ void decode_keys_kernel(const unsigned long long* keys, int64_t m, in
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
-int num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int num_sms() { return device_sm_count(); }
 
 constexpr uint32_t kSmemLimit = 225 * 1024;     // dynamic, incl. 1 KB alignment slack; leaves room for static
 constexpr uint32_t kSmemTwoPerSm = 111 * 1024;  // two CTAs per SM (228 KB per SM, 1 KB reserved each)
@@ -772,7 +762,7 @@ int g_decode_path = kPathI8;
 int decode_path() { return g_decode_path; }
 
 bool set_decode_path(int path) {
-    if (path != kPathI8 && path != kPathTc && path != kPathBf16 && path != kPathOneKernel) return false;
+    if (path != kPathI8 && path != kPathBf16) return false;
     g_decode_path = path;
     return true;
 }
@@ -784,14 +774,11 @@ int gemv_max_rows(int act_dtype, bool normed, int64_t k) {
 int lm_head_max_rows(int act_dtype, bool normed, int64_t k) {
     if (path_is_i8(g_decode_path) && i8_supported(k, 1)) return kI8MaxRows;
     const bool p3 = normed || act_dtype == kF32;
-    if (g_decode_path == kPathTc && tc_supported(k, p3 ? 30 : 32)) return p3 ? 10 : 32;
     return p3 ? 5 : 16;
 }
 
 cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
-    const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
     if (path_is_i8(g_decode_path) && i8_supported(L.w0.k, L.m)) return launch_i8_gemv(L, stream);
-    if (g_decode_path == kPathTc && tc_supported(L.w0.k, m_eff) && tc_gemv_fits(L)) return launch_tc_gemv(L, stream);
     UnitArgs a{};
     a.L = L;
     const int K = (int)L.w0.k;
@@ -848,9 +835,7 @@ cudaError_t launch_q4_gemv(const GemvLaunch& L, cudaStream_t stream) {
 }
 
 cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream) {
-    const int64_t m_eff = L.m * ((L.norm_w || L.x_dtype == kF32) ? 3 : 1);
     if (path_is_i8(g_decode_path) && i8_supported(L.w.k, L.m)) return launch_i8_lm_head(L, stream);
-    if (g_decode_path == kPathTc && tc_supported(L.w.k, m_eff) && tc_lm_head_fits(L)) return launch_tc_lm_head(L, stream);
     LmArgs a{};
     a.L = L;
     const int K = (int)L.w.k;

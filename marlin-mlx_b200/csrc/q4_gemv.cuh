@@ -50,12 +50,17 @@ struct XPlanes {
 //   part[r]   [2 parities][tp sources][m][hidden] words: partial rows of down_proj (binary32 bits),
 //   keys[r]   [tp sources][m][2] words: the low and high halves of the packed argmax keys,
 //   step      this rank's step counter (in its own buffer).
+// wait_cycles bounds each wait for a peer's word (SM clock cycles).  Once one wait has run out, the
+// device error word is set and every later exchange wait returns at once, so a rank whose peer is
+// gone finishes its step in about one wait limit instead of spinning once per word.
 constexpr int kTpMax = 8;
+constexpr unsigned long long kPeerWaitDefaultCycles = 4000000000ull;  // about 2 s at 2 GHz
 struct TpExchange {
     int tp, rank, parity, layer;
     unsigned long long* part[kTpMax];
     unsigned long long* keys[kTpMax];
     unsigned* step;
+    unsigned long long wait_cycles;
 };
 
 struct GemvLaunch {
@@ -85,14 +90,12 @@ struct GemvLaunch {
     TpExchange tp;
 };
 
-// Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default), tcgen05/TMEM, bf16
-// mma.sync, and integer MMAs with the decode step as one kernel.  Shapes a family does not cover use
-// the bf16 mma.sync kernels.
-enum DecodePath : int { kPathI8 = 0, kPathTc = 1, kPathBf16 = 2, kPathOneKernel = 3 };
+// Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default) and bf16 mma.sync.
+// Shapes the integer-MMA kernels do not cover (k % 512 != 0) use the bf16 mma.sync kernels.
+enum DecodePath : int { kPathI8 = 0, kPathBf16 = 2 };
 bool set_decode_path(int path);
 int decode_path();
-// True for the families whose GEMV / lm_head kernels are the integer-MMA ones.
-inline bool path_is_i8(int p) { return p == kPathI8 || p == kPathOneKernel; }
+inline bool path_is_i8(int p) { return p == kPathI8; }
 
 // Activation rows per launch of the selected family for this shape (the C ABI loops over passes).
 int gemv_max_rows(int act_dtype, bool normed, int64_t k);
@@ -125,6 +128,9 @@ cudaError_t launch_q4_lm_head_argmax(const LmHeadLaunch& L, cudaStream_t stream)
 
 // Device error word of this translation unit (0 ok, >0 a DeviceError code, -1 CUDA failure).
 int gemv_device_error(bool clear);
+
+// SM count of the current device, cached per device index (thread-safe; 148 if the query fails).
+int device_sm_count();
 
 // Decode packed keys [m] into ids/best (used after a cross-GPU max-merge of keys).
 cudaError_t launch_decode_keys(const unsigned long long* keys, int64_t m, int32_t* ids, float* best,

@@ -58,16 +58,7 @@ inline bool encode_q4_maps(const Q4Mat& W, int box_rows, CUtensorMap* tw, CUtens
     return true;
 }
 
-inline int device_num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+inline int device_num_sms() { return device_sm_count(); }
 
 // cudaLaunchKernelEx with optional programmatic stream serialization and cluster dimension.
 template <typename KernelT, typename ArgT>

@@ -212,18 +212,28 @@ __device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long lo
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Bounded wait for the word at p to carry `tag`; returns its low 32 bits (0 after a timeout, which
-// is recorded as a device error).
-__device__ __forceinline__ uint32_t wait_word(const unsigned long long* p, uint32_t tag) {
+__device__ __forceinline__ bool device_error_set() {
+    return *reinterpret_cast<volatile int*>(&g_marlin_device_error) != 0;
+}
+// Bounded wait for the word at p to carry `tag`; returns its low 32 bits.  Returns 0 without
+// spinning when the device error word is already set (an earlier wait ran out: the step's results
+// are void and the host must look at the error anyway), and gives up after `limit` SM cycles,
+// recording kDevErrMbarTimeout, which makes every later wait return at once.  So a step whose peer
+// never writes ends after about one limit, whatever the number of words it waits for.
+__device__ __forceinline__ uint32_t wait_word(const unsigned long long* p, uint32_t tag, unsigned long long limit) {
     unsigned long long w = ld_word_sys(p);
     if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+    if (device_error_set()) return 0u;
     const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0;; ++it) {
         w = ld_word_sys(p);
         if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
-        if ((it & 63u) == 63u && cycles_now() - t0 > kWaitCycles) {
-            record_device_error(kDevErrMbarTimeout);
-            return 0u;
+        if ((it & 63u) == 63u) {
+            if (device_error_set()) return 0u;
+            if (cycles_now() - t0 > limit || it > (1u << 30)) {
+                record_device_error(kDevErrMbarTimeout);
+                return 0u;
+            }
         }
     }
 }
@@ -252,7 +262,7 @@ __device__ __forceinline__ void tp_allreduce_rows(const TpExchange& X, int M, in
     for (int m = 0; m < MS; ++m) {
         if (m < M) {
             float v = 0.f;
-            for (int r = 0; r < tp; ++r) v += __uint_as_float(wait_word(src + ((size_t)r * M + m) * H, tag));
+            for (int r = 0; r < tp; ++r) v += __uint_as_float(wait_word(src + ((size_t)r * M + m) * H, tag, X.wait_cycles));
             o[m] = v;
         }
     }
@@ -701,8 +711,8 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
                 }
                 for (int r = 0; r < X.tp; ++r) {
                     const unsigned long long* sw = X.keys[X.rank] + ((size_t)r * M + tid) * 2;
-                    const unsigned long long kr = (unsigned long long)wait_word(sw, tag) |
-                                                  ((unsigned long long)wait_word(sw + 1, tag) << 32);
+                    const unsigned long long kr = (unsigned long long)wait_word(sw, tag, X.wait_cycles) |
+                                                  ((unsigned long long)wait_word(sw + 1, tag, X.wait_cycles) << 32);
                     k = kr > k ? kr : k;
                 }
             }

@@ -4,6 +4,8 @@
 #include "q4_host.cuh"
 #include "q4_misc.cuh"
 
+#include <atomic>
+
 namespace marlin {
 namespace {
 
@@ -151,6 +153,24 @@ __global__ void residual_add_kernel(const void* __restrict__ h, int dtype, const
     }
 }
 
+// out[i] = bf16(x[i]), round to nearest even: the activation dtype of a projection whose binary32
+// partials were summed across GPUs (tensor-parallel down_proj of the prefill MLP).  Four elements
+// per thread and step when both pointers allow 16 / 8-byte accesses.
+__global__ void cast_bf16_kernel(const float* __restrict__ x, int64_t n, uint16_t* __restrict__ out, bool vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {
+        const int64_t n4 = n / 4;
+        for (int64_t j = i; j < n4; j += stride) {
+            const float4 v = reinterpret_cast<const float4*>(x)[j];
+            reinterpret_cast<uint2*>(out)[j] = make_uint2(f32_to_bf16_bits(v.x) | (f32_to_bf16_bits(v.y) << 16),
+                                                          f32_to_bf16_bits(v.z) | (f32_to_bf16_bits(v.w) << 16));
+        }
+        i += n4 * 4;  // the tail, one element per thread
+    }
+    for (; i < n; i += stride) out[i] = (uint16_t)f32_to_bf16_bits(x[i]);
+}
+
 // Rows `ids` of a Q4 table dequantized to bf16, out[i, :] = bf16(s q + b) per element with one
 // rounding of the exact value (the operand the prefill GEMM builds): the embedding lookup
 // MarlinModel::embed_tokens (src/model/marlin.cpp:63-65, mx::take of the embedding table) served
@@ -178,18 +198,27 @@ __global__ void __launch_bounds__(256) embed_q4_kernel(const int32_t* __restrict
     }
 }
 
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return device_sm_count(); }
 
 }  // namespace
+
+int device_sm_count() {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> cache[kMaxDevices];  // 0 = not yet queried
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return 148;
+    }
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = 148;
+    }
+    cache[dev].store(n, std::memory_order_relaxed);  // every thread that races here stores the same value
+    return n;
+}
 
 cudaError_t launch_quantize(const uint16_t* w, int64_t n, int64_t k, uint32_t* wq, uint16_t* scales,
                             uint16_t* biases, cudaStream_t stream) {
@@ -213,6 +242,14 @@ cudaError_t launch_residual_add(const void* h, int dtype, const float* y, int64_
     if (n <= 0) return cudaSuccess;
     const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
     residual_add_kernel<<<(unsigned)blocks, 256, 0, stream>>>(h, dtype, y, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cast_bf16(const float* x, int64_t n, uint16_t* out, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
+    const int64_t blocks = std::min<int64_t>((n / (vec ? 4 : 1) + 255) / 256 + 1, (int64_t)sm_count() * 8);
+    cast_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, n, out, vec);
     return cudaGetLastError();
 }
 

@@ -17,6 +17,7 @@ cudaError_t launch_rms_norm(const void* x, int dtype, const uint16_t* w, int64_t
                             float* out, cudaStream_t stream);
 cudaError_t launch_residual_add(const void* h, int dtype, const float* y, int64_t n, float* out,
                                 cudaStream_t stream);
+cudaError_t launch_cast_bf16(const float* x, int64_t n, uint16_t* out, cudaStream_t stream);
 cudaError_t launch_embed_q4(const int32_t* ids, int64_t m, const uint32_t* wq, const uint16_t* scales,
                             const uint16_t* biases, int64_t n, int64_t k, uint16_t* out, cudaStream_t stream);
 int misc_device_error(bool clear);

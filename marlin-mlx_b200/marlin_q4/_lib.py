@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libmarlin_q4.so"
 OK = 0
 ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = -1, -2, -3, -4, -5, -6
 BF16, F32 = 0, 1
-PATH_I8MMA, PATH_TCGEN05, PATH_BF16MMA, PATH_ONEKERNEL = 0, 1, 2, 3
+PATH_I8MMA, PATH_BF16MMA = 0, 2
 
 # Every symbol include/marlin_q4.h declares, with its ctypes signature (restype, argtypes).
 _vp, _i64, _i32, _f32, _sz, _u64 = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float,
@@ -40,9 +40,12 @@ SIGNATURES = {
     "marlin_q4_last_cuda_error": (ctypes.c_int, []),
     "marlin_q4_device_error": (ctypes.c_int, [ctypes.c_int]),
     "marlin_q4_set_pdl": (None, [ctypes.c_int]),
+    "marlin_q4_set_wait_limit_cycles": (None, [_u64]),
     "marlin_q4_set_decode_path": (ctypes.c_int, [ctypes.c_int]),
     "marlin_q4_quantize": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     "marlin_q4_matmul": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),
+    "marlin_q4_matmul_f32": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),
+    "marlin_q4_cast_bf16": (ctypes.c_int, [_vp, _i64, _vp, _vp]),
     "marlin_q4_rms_norm": (ctypes.c_int, [_vp, _i32, _vp, _i64, _i64, _f32, _vp, _vp]),
     "marlin_q4_gate_up_swiglu": (ctypes.c_int, [_vp, _i32, _i64, _vp, _f32, _PT, _PT, _vp, _vp]),
     "marlin_q4_matmul_residual": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _i32, _vp, _vp]),

@@ -98,6 +98,28 @@ def qmatmul(x: torch.Tensor, w: QuantizedTensor) -> torch.Tensor:
     return y.reshape(*lead, w.n)
 
 
+def matmul_f32(x: torch.Tensor, w: QuantizedTensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x . dequant(W)^T with a binary32 result (the partial of a K-split projection): [m, k] -> [m, n]."""
+    _cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    if out is None:
+        out = torch.empty((x2.shape[0], w.n), dtype=torch.float32, device=x.device)
+    tw = w.c()
+    check(_lib.load().marlin_q4_matmul_f32(x2.data_ptr(), _dtype_code(x), x2.shape[0], ctypes.byref(tw),
+                                           out.data_ptr(), _stream()), "marlin_q4_matmul_f32")
+    return out
+
+
+def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(x) of a binary32 tensor, round to nearest even (marlin_q4_cast_bf16)."""
+    _cuda(x, "x")
+    assert x.dtype == torch.float32
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    check(_lib.load().marlin_q4_cast_bf16(x.data_ptr(), x.numel(), out.data_ptr(), _stream()), "marlin_q4_cast_bf16")
+    return out
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """rms_norm (src/model/marlin.cpp:12-16) with a float eps: binary32 output."""
     _cuda(x, "x")
@@ -304,11 +326,9 @@ def set_pdl(enable: bool) -> None:
     _lib.load().marlin_q4_set_pdl(1 if enable else 0)
 
 
-DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "tcgen05": _lib.PATH_TCGEN05, "bf16": _lib.PATH_BF16MMA,
-                "onekernel": _lib.PATH_ONEKERNEL}
+DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "bf16": _lib.PATH_BF16MMA}
 
 
 def set_decode_path(path: str) -> None:
-    """Select the decode kernel family: "i8" (integer MMAs, default), "tcgen05", "bf16" (mma.sync) or
-    "onekernel" (integer MMAs; marlin_q4_decode_step as one persistent kernel)."""
+    """Select the decode kernel family: "i8" (integer MMAs, default) or "bf16" (mma.sync)."""
     check(_lib.load().marlin_q4_set_decode_path(DECODE_PATHS[path]), "marlin_q4_set_decode_path")

@@ -1,6 +1,6 @@
 """Standalone driver of the decode kernels, for profilers (ncu) and quick timing.
 
-    python -m marlin_q4.prof [--m 1] [--reps 3] [--time] [--path i8|tcgen05|bf16|onekernel]
+    python -m marlin_q4.prof [--m 1] [--reps 3] [--time] [--path i8|bf16]
     python -m marlin_q4.prof --step 24 [--m 1] [--reps 3] [--time] [--path ...]
 
 Builds one decode layer (gate/up/down Q4 [6144,2048]/[2048,6144]) and the Q4 lm_head

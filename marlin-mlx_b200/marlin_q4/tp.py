@@ -12,14 +12,11 @@ Sharding (the reference is single-device; this is the B200 multi-GPU layout of t
 Keys are unsigned 64-bit; NCCL's max on int64 is signed, so keys travel XOR 2^63 (order-preserving
 map from unsigned to signed).
 
-Two implementations of the step:
-  * FusedTPDecodeStep (the product): marlin_q4_tp_decode_step, where the down_proj kernel's epilogue
-    writes its partial rows into every rank's exchange buffer over NVLink and sums all ranks' rows
-    itself, and the lm_head kernel merges the keys the same way; the exchange buffers are mapped
-    between the processes with CUDA IPC (plain peer memory, no multicast).  No collective library
-    call per step.
-  * TPDecodeStep: the same math with NCCL all-reduces between the single-op kernels (the
-    reference point the fused step is measured against).
+The decode step, FusedTPDecodeStep, is marlin_q4_tp_decode_step: the down_proj kernel's epilogue
+writes its partial rows into every rank's exchange buffer over NVLink and sums all ranks' rows
+itself, and the lm_head kernel merges the keys the same way; the exchange buffers are mapped
+between the processes with CUDA IPC (plain peer memory, no multicast).  No collective library call
+per step.  (keys_to_signed serves a merge of packed keys through a signed all-reduce(max).)
 """
 from __future__ import annotations
 
@@ -51,15 +48,35 @@ def pad_k(q: QuantizedTensor, k: int) -> QuantizedTensor:
     return QuantizedTensor(w, sc, bi)
 
 
-def shard_layer(layer: Layer, rank: int, world: int, k_multiple: int = 64) -> Layer:
+def pad_rows(q: QuantizedTensor, n: int) -> QuantizedTensor:
+    """The operand with zero output rows appended up to n (zero codes, scales and biases: those
+    outputs are exactly 0, and SwiGLU of a zero gate and up is exactly 0 too)."""
+    if q.n == n:
+        return q
+    assert n > q.n
+    w = torch.zeros((n, q.weight.shape[1]), dtype=q.weight.dtype, device=q.weight.device)
+    sc = torch.zeros((n, q.scales.shape[1]), dtype=q.scales.dtype, device=q.scales.device)
+    bi = torch.zeros((n, q.biases.shape[1]), dtype=q.biases.dtype, device=q.biases.device)
+    w[:q.n] = q.weight
+    sc[:q.n] = q.scales
+    bi[:q.n] = q.biases
+    return QuantizedTensor(w, sc, bi)
+
+
+def shard_layer(layer: Layer, rank: int, world: int, k_multiple: int = 64, pad_gate_up: bool = False) -> Layer:
     """Rank `rank`'s shard of a layer; the down_proj shard's K is zero-padded to a multiple of
-    `k_multiple` (512 for the integer-MMA kernels' tensor maps)."""
+    `k_multiple` (512 for the kernels' tensor maps).  pad_gate_up: the gate/up shards get the same
+    number of zero rows, so that their SwiGLU output already has the padded width (the prefill
+    GEMM takes its input as it is; the decode step's planes leave the padding at zero itself)."""
     inter = layer.gate_proj.n
     assert inter % world == 0 and (inter // world) % 64 == 0, "intermediate must split into 64-aligned shards"
     r0, r1 = rank * inter // world, (rank + 1) * inter // world
     down = layer.down_proj.shard_k(r0, r1)
     down = pad_k(down, -(-down.k // k_multiple) * k_multiple)
-    return Layer(layer.post_attn_norm, layer.gate_proj.shard_rows(r0, r1), layer.up_proj.shard_rows(r0, r1), down)
+    gate, up = layer.gate_proj.shard_rows(r0, r1), layer.up_proj.shard_rows(r0, r1)
+    if pad_gate_up:
+        gate, up = pad_rows(gate, down.k), pad_rows(up, down.k)
+    return Layer(layer.post_attn_norm, gate, up, down)
 
 
 def shard_vocab(lm: QuantizedTensor, rank: int, world: int) -> tuple[QuantizedTensor, int]:
@@ -72,38 +89,29 @@ def keys_to_signed(keys: torch.Tensor) -> torch.Tensor:
     return torch.bitwise_xor(keys, SIGN)
 
 
-class TPDecodeStep:
-    """Decode step over sharded weights.  Call under torch.cuda.graph() to capture all kernels and
-    the NCCL collectives in one graph."""
+class TPPrefillMLP:
+    """mlp_forward (src/model/marlin.cpp:31-35) of a prefill block of rows over the ranks of `group`:
+    rank r holds gate/up rows and down_proj input columns [r*I/tp, (r+1)*I/tp) (padded with zeros to
+    a multiple of 512, shard_layer(..., k_multiple=512, pad_gate_up=True)).  Per call: gate/up +
+    SwiGLU as one tcgen05 GEMM over the rank's rows (bf16 act, as the reference rounds it), down_proj
+    as a tcgen05 GEMM with a binary32 partial, one all-reduce(sum) of the partials over NCCL, then
+    the sum rounded to bf16 (the dtype mlp_forward returns).  Call under torch.cuda.graph() to
+    capture the kernels and the collective together."""
 
-    def __init__(self, layers: list[Layer], final_norm: torch.Tensor, lm_shard: QuantizedTensor, vocab_offset: int,
-                 m: int, group=None, eps: float = 1e-6):
-        self.layers, self.final_norm, self.lm, self.off, self.m, self.eps = layers, final_norm, lm_shard, vocab_offset, m, eps
-        self.group = group
-        dev = final_norm.device
-        H = lm_shard.k
-        inter = layers[0].gate_proj.n
-        self.h = torch.empty((m, H), dtype=torch.float32, device=dev)
-        self.partial = torch.empty((m, H), dtype=torch.float32, device=dev)
-        self.act = torch.empty((m, inter), dtype=torch.float32, device=dev)
-        self.ws = ops.LmHeadWorkspace(m, dev)
-        self.keys = torch.empty(m, dtype=torch.int64, device=dev)
+    def __init__(self, layer_shard: Layer, m: int, group=None):
+        self.layer, self.m, self.group = layer_shard, m, group
+        dev = layer_shard.post_attn_norm.device
+        self.act = torch.empty((m, layer_shard.gate_proj.n), dtype=torch.bfloat16, device=dev)
+        self.part = torch.empty((m, layer_shard.down_proj.n), dtype=torch.float32, device=dev)
+        self.y = torch.empty((m, layer_shard.down_proj.n), dtype=torch.bfloat16, device=dev)
 
-    def __call__(self, h0: torch.Tensor):
-        cur = h0
-        for L in self.layers:
-            ops.gate_up_swiglu(cur, L.gate_proj, L.up_proj, norm_weight=L.post_attn_norm, eps=self.eps, out=self.act)
-            y = ops.qmatmul(self.act, L.down_proj)  # binary32 partial of the row-parallel down_proj
-            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
-            ops.residual_add(cur, y, out=self.h)
-            cur = self.h
-        keys = ops.lm_head_argmax(cur, self.lm, norm_weight=self.final_norm, eps=self.eps, vocab_offset=self.off,
-                                  workspace=self.ws, want_keys=True)
-        sk = keys_to_signed(keys)
-        dist.all_reduce(sk, op=dist.ReduceOp.MAX, group=self.group)
-        self.keys.copy_(keys_to_signed(sk))
-        ids, best = ops.decode_keys(self.keys)
-        return ids, best, self.h
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        L = self.layer
+        assert x.dtype == torch.bfloat16 and x.shape == (self.m, L.gate_proj.k)
+        ops.gate_up_swiglu(x, L.gate_proj, L.up_proj, out=self.act)
+        ops.matmul_f32(self.act, L.down_proj, out=self.part)
+        dist.all_reduce(self.part, op=dist.ReduceOp.SUM, group=self.group)
+        return ops.cast_bf16(self.part, out=self.y)
 
 
 class FusedTPDecodeStep:

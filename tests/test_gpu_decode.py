@@ -1,9 +1,9 @@
 """GPU parity: the full Q4 decode stack (config 5) — 24 x [RMSNorm(1+w) -> Q4 MLP -> residual] ->
 final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
 
-Both forms of the step are checked: the per-kernel composition (default; above 16 rows it runs in
-16-row chunks) and the one persistent cooperative kernel ("onekernel" family, grid barriers between
-phases; rows it does not take fall back to the single-op kernels)."""
+The step runs the integer-MMA kernels with the activations handed between them as operand planes
+(above 16 rows in 16-row chunks); the bf16 mma.sync family's composition of single-op kernels is
+checked against it."""
 import numpy as np
 import pytest
 import torch
@@ -31,15 +31,8 @@ def model():
     return layers, host_layers, lm, host_q4(lm), fn, u16(fn)
 
 
-@pytest.fixture(params=["i8", "onekernel"])
-def family(request):
-    mq.set_decode_path(request.param)
-    yield request.param
-    mq.set_decode_path("i8")
-
-
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 12, 16, 20, 32])
-def test_decode_step_matches_oracle(oracle, model, family, m):
+def test_decode_step_matches_oracle(oracle, model, m):
     layers, hl, lm, hlm, fn, hfn = model
     step = mq.DecodeStep(layers, fn, lm, m)
     h0 = mq.synth_bf16((m, H), 3000 + m, 0.0, 1.0)
@@ -74,16 +67,12 @@ def test_decode_step_in_cuda_graph(model):
 
 
 @pytest.mark.parametrize("m", [1, 5])
-def test_one_kernel_step_matches_composition(model, m):
-    """The one-kernel step against the per-kernel composition (tcgen05 family)."""
+def test_bf16_family_step_matches_i8(model, m):
+    """The bf16 mma.sync family (single-op kernels composed) against the integer-MMA step."""
     layers, _, lm, _, fn, _ = model
     h0 = mq.synth_bf16((m, H), 3200 + m, 0.0, 1.0)
-    mq.set_decode_path("onekernel")
-    try:
-        ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, m)(h0))
-    finally:
-        mq.set_decode_path("i8")
-    mq.set_decode_path("tcgen05")
+    ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, m)(h0))
+    mq.set_decode_path("bf16")
     try:
         ids_c, _, h_c = mq.DecodeStep(layers, fn, lm, m)(h0)
         torch.cuda.synchronize()
@@ -95,7 +84,7 @@ def test_one_kernel_step_matches_composition(model, m):
 
 
 @pytest.mark.parametrize("nl", [1, 2])
-def test_short_stacks(oracle, model, family, nl):
+def test_short_stacks(oracle, model, nl):
     layers, hl, lm, hlm, fn, hfn = model
     step = mq.DecodeStep(layers[:nl], fn, lm, 2)
     h0 = mq.synth_bf16((2, H), 3300 + nl, 0.0, 1.0)

@@ -1,5 +1,5 @@
-"""GPU parity of the three decode kernel families — integer MMAs on the codes (default), tcgen05/TMEM
-and bf16 mma.sync — each against the CPU oracle and against each other on the same inputs."""
+"""GPU parity of the two decode kernel families — integer MMAs on the codes (default) and bf16
+mma.sync — each against the CPU oracle and against each other on the same inputs."""
 import numpy as np
 import pytest
 import torch
@@ -11,7 +11,7 @@ from gpu_util import TOL, act, f32, host_act, host_q4, make_q4, max_rel_row_err,
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["i8", "tcgen05", "bf16"])
+@pytest.fixture(params=["i8", "bf16"])
 def path(request):
     mq.set_decode_path(request.param)
     yield request.param
@@ -75,7 +75,7 @@ def test_lm_head_paths(oracle, mats, path, m, dtype, norm):
 def test_paths_agree_on_decode_layer(mats):
     h = act((2, 2048), 110, torch.float32)
     outs = []
-    for p in ("i8", "tcgen05", "bf16"):
+    for p in ("i8", "bf16"):
         mq.set_decode_path(p)
         a = mq.gate_up_swiglu(h, mats["g"], mats["u"], norm_weight=mats["nw"])
         outs.append(f32(mq.matmul_residual(a, mats["d"], h)))

@@ -113,3 +113,34 @@ def test_prefill_c4_stack(mats):
     y2 = mq.qmatmul(mq.gate_up_swiglu(x, g, u), d)
     assert torch.equal(y, y2)
     assert mq.device_error() == 0
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_sharded_prefill_mlp_on_one_gpu(world):
+    """The tensor-parallel prefill MLP's arithmetic with every shard run on this one GPU: each rank's
+    gate/up rows (zero-padded to a multiple of 512 at 8 ranks, where a shard holds 768 rows) feed
+    its binary32 down_proj partial (marlin_q4_matmul_f32, tcgen05 GEMM); the partials are summed in
+    rank order and rounded once (marlin_q4_cast_bf16).  Against the single-GPU mlp_forward: within the
+    path's tolerance and equal in nearly every element."""
+    from marlin_q4 import tp
+    S, H, I = 2048, 2048, 6144
+    g, _ = make_q4(I, H, 601)
+    u, _ = make_q4(I, H, 602)
+    d, _ = make_q4(H, I, 603)
+    layer = mq.Layer(mq.synth_bf16((H,), 604, 0.1, 0.02), g, u, d)
+    x = mq.synth_bf16((S, H), 605, 0.0, 1.0)
+    total = torch.zeros((S, H), dtype=torch.float32, device="cuda")
+    for r in range(world):
+        sh = tp.shard_layer(layer, r, world, k_multiple=512, pad_gate_up=True)
+        assert sh.gate_proj.n == sh.down_proj.k and sh.down_proj.k % 512 == 0
+        a = mq.gate_up_swiglu(x, sh.gate_proj, sh.up_proj)
+        assert torch.count_nonzero(a[:, I // world:]) == 0  # the padded features are exact zeros
+        total += mq.matmul_f32(a, sh.down_proj)
+    y = mq.cast_bf16(total)
+    ry = mq.mlp_forward(x, g, u, d)
+    torch.cuda.synchronize()
+    rel = ((y.float() - ry.float()).abs().amax(dim=1) / ry.float().abs().amax(dim=1)).max().item()
+    assert rel < TOL
+    assert (y.view(torch.int16) == ry.view(torch.int16)).float().mean().item() > 0.9
+    assert torch.equal(mq.cast_bf16(ry.float()), ry)  # bf16 values survive the round trip
+    assert mq.device_error() == 0
