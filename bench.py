@@ -216,6 +216,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # no version banner on stdout: the JSON line stays alone there
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
     def barrier():
@@ -423,6 +425,15 @@ def run_ours(args):
                               for k, v in fams.items()}
         extras["families_note"] = ("public single-op entry points (each stages its own activations), "
                                    "not the step's kernels; see step_split for those")
+        # the same step on the cluster K-split family (the kernels the step used before the whole-row
+        # layer kernels), same weights and inputs
+        mq.set_decode_path("i8splitk")
+        try:
+            stk = mq.DecodeStep(layers, fn, lm, B)
+            extras["step_family_i8splitk_ms"] = round(time_graph(torch, lambda: stk(h0), reps), 5)
+            del stk
+        finally:
+            mq.set_decode_path("i8")
 
         # config 1 GEMV: 6144x2048, bf16 x [1, 2048], over 24 distinct weight copies (170 MB > L2)
         xb = mq.synth_bf16((1, H), 7, 0.0, 1.0)
