@@ -64,7 +64,21 @@ void q4o_synth_bf16(uint16_t* out, int64_t n, uint64_t seed, float mean, float s
 
 /* ---- quantize ----------------------------------------------------------------------------- */
 /* mx::quantize(w, 64, 4) as called at src/model/weights.cpp:46 and :183.  Returns 0 or -1 on a
- * bad shape (K % 64 != 0, group_size != 64, bits != 4). */
+ * bad shape (K % 64 != 0, group_size != 64, bits != 4).
+ *
+ * The reference calls mx::quantize on MLX's default device, the Apple GPU (src/model/weights.cpp:
+ * 46-47 evaluates it right away; src/model/marlin.cpp:309-313 loads on that device), so the defaults
+ * restate what this restatement takes MLX v0.25.2's GPU affine-quantize kernel to do.  Each default
+ * is UNPINNED (no MLX here, no upstream vectors); each has a flag and a known-answer vector in
+ * tests/golden/ that tells the two readings apart:
+ *   - group maximum starts at 0, minimum at +inf (Q4O_TRUE_MINMAX starts the maximum at -inf):
+ *     an all-negative group then snaps its bias to the minimum and its scale to a positive step;
+ *   - round = ties away from zero, as Metal's round() is (Q4O_ROUND_HALF_EVEN: rint);
+ *   - zero-point snap: s = edge / round(edge / s), b = edge, so the extreme of larger magnitude is
+ *     exact (Q4O_NO_ZERO_SNAP: the documented s = (max - min) / 15, b = min);
+ *   - codes from the binary32 scale and bias, which are then rounded to bf16 only to be stored (the
+ *     kernel computes in float and casts on the store; Q4O_BF16_PARAMS_FIRST rounds them first:
+ *     kat_param_order shows the codes that differ). */
 int q4o_quantize(const uint16_t* w, int64_t N, int64_t K, int group_size, int bits,
                  uint32_t* wq, uint16_t* scales, uint16_t* biases, unsigned flags);
 /* dequantized value of element (n,k) in binary32: s*q + b */

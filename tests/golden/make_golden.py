@@ -54,6 +54,9 @@ def kat_inputs() -> dict[str, np.ndarray]:
         "all_positive": bf([[0.25 + (i % 13) * 0.0625 for i in range(64)]]),
         "outlier": bf(outlier[None, :]),
         "tie": bf(tie[None, :]),
+        # a seeded group whose codes at elements 27 and 62 depend on the order of the roundings:
+        # codes from the binary32 scale and bias give 6 and 10; from the bf16-rounded ones, 7 and 11
+        "param_order": qo.np_synth_bf16(64, 100, 0.0, 0.02).reshape(1, 64),
     }
 
 
@@ -76,7 +79,7 @@ def main() -> None:
         data[f"kat_{name}_w"] = w
         wq, s, b = qo.np_quantize(w)
         data[f"kat_{name}_wq"], data[f"kat_{name}_s"], data[f"kat_{name}_b"] = wq, s, b
-        for flags in (qo.ROUND_HALF_EVEN, qo.TRUE_MINMAX, qo.NO_ZERO_SNAP):
+        for flags in (qo.ROUND_HALF_EVEN, qo.TRUE_MINMAX, qo.NO_ZERO_SNAP, qo.BF16_PARAMS_FIRST):
             wq2, s2, b2 = qo.np_quantize(w, flags)
             data[f"kat_{name}_f{flags}_wq"], data[f"kat_{name}_f{flags}_s"], data[f"kat_{name}_f{flags}_b"] = wq2, s2, b2
     for name, (words, s, b) in KAT_EXPECT.items():

@@ -38,7 +38,8 @@ def test_quantize_lm_head_size(oracle):
 def test_quantize_known_answers():
     from pathlib import Path
     g = np.load(Path(__file__).resolve().parent / "golden" / "q4_golden.npz")
-    for name in ("ramp_up", "ramp_down", "all_zero", "constant", "all_negative", "all_positive", "outlier", "tie"):
+    for name in ("ramp_up", "ramp_down", "all_zero", "constant", "all_negative", "all_positive", "outlier", "tie",
+                 "param_order"):
         q = mq.quantize_weight(from_u16(g[f"kat_{name}_w"]))
         assert np.array_equal(u32(q.weight), g[f"kat_{name}_wq"]), name
         assert np.array_equal(u16(q.scales), g[f"kat_{name}_s"]), name

@@ -51,14 +51,14 @@ def test_kat_hand_values(golden):
 
 
 @pytest.mark.parametrize("name", ["ramp_up", "ramp_down", "all_zero", "constant", "all_negative", "all_positive",
-                                  "outlier", "tie"])
+                                  "outlier", "tie", "param_order"])
 def test_kat_c_oracle(oracle, golden, name):
     w = golden[f"kat_{name}_w"]
     q = oracle.quantize(w)
     assert np.array_equal(q.weight, golden[f"kat_{name}_wq"])
     assert np.array_equal(q.scales, golden[f"kat_{name}_s"])
     assert np.array_equal(q.biases, golden[f"kat_{name}_b"])
-    for flags in (qo.ROUND_HALF_EVEN, qo.TRUE_MINMAX, qo.NO_ZERO_SNAP):
+    for flags in (qo.ROUND_HALF_EVEN, qo.TRUE_MINMAX, qo.NO_ZERO_SNAP, qo.BF16_PARAMS_FIRST):
         q = oracle.quantize(w, flags)
         assert np.array_equal(q.weight, golden[f"kat_{name}_f{flags}_wq"])
         assert np.array_equal(q.scales, golden[f"kat_{name}_f{flags}_s"])
@@ -71,6 +71,18 @@ def test_kat_tie_rounding(golden):
     assert codes_away[2] == 3 and codes_even[2] == 2
     assert codes_away[3] == 4 and codes_even[3] == 4
     assert codes_away[4] == 1 and codes_even[4] == 0
+
+
+def test_kat_param_order(golden):
+    """The codes come from the binary32 scale and bias; only the stored copies are rounded to bf16.
+    On this group the other order (bf16-rounded parameters first) moves elements 27 and 62 up by
+    one code, while the stored scale and bias are the same either way."""
+    first_f32 = qo.np_unpack(golden["kat_param_order_wq"])[0]
+    first_bf16 = qo.np_unpack(golden["kat_param_order_f8_wq"])[0]
+    assert list(np.nonzero(first_f32 != first_bf16)[0]) == [27, 62]
+    assert list(first_f32[[27, 62]]) == [6, 10] and list(first_bf16[[27, 62]]) == [7, 11]
+    assert np.array_equal(golden["kat_param_order_s"], golden["kat_param_order_f8_s"])
+    assert np.array_equal(golden["kat_param_order_b"], golden["kat_param_order_f8_b"])
 
 
 def test_quantize_error_bound():
