@@ -330,11 +330,14 @@ def run_ours(args):
         extras["step_split"] = split
         traffic = None
         tp_path = ROOT / "profiles" / "traffic.json"
-        if world == 1 and tp_path.exists():
+        if world == 1 and B == 1 and tp_path.exists():
             traffic = json.loads(tp_path.read_text()).get("mlp_layer")
         ach = layer_bytes / (layer_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "mlp_layer: i8_unit_kernel gate/up+SwiGLU launch + down+residual launch "
-                                          "(activation planes handed between them), as run inside the step"
+        kname = ("i8_layer_kernel gate/up+SwiGLU launch + i8_layer_kernel down+residual launch (whole-row CTAs, "
+                 "each building its operand planes from the previous launch's binary32 row)" if B == 1 else
+                 "i8_unit_kernel gate/up+SwiGLU launch + down+residual launch (cluster K split, activation planes "
+                 "handed between them)")
+        roof = {"bound": "hbm", "kernel": f"mlp_layer: {kname}, as run inside the step"
                                           + (" (per rank; the down launch's epilogue holds the in-kernel all-reduce)"
                                              if world > 1 else ""),
                 "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4),
