@@ -536,11 +536,11 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     float* h = reinterpret_cast<float*>(scratch);
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
-    if (decode_path() == kPathI8 && uniform && m <= kI8MaxRows && i8_supported(hidden, m) &&
+    if (path_is_i8(decode_path()) && uniform && m <= kI8MaxRows && i8_supported(hidden, m) &&
         i8_supported(inter, m) && hidden % 128 == 0)
         return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h, scratch,
                                   lmws, st);
-    if (decode_path() == kPathI8 && uniform && i8_supported(hidden, kI8MaxRows) &&
+    if (path_is_i8(decode_path()) && uniform && i8_supported(hidden, kI8MaxRows) &&
         i8_supported(inter, kI8MaxRows) && hidden % 128 == 0) {
         // more rows than one plane hand-off serves: the rows are independent (per-row norm, GEMV and
         // argmax), so the step runs on consecutive chunks of kI8MaxRows rows, stream-ordered, each

@@ -1101,6 +1101,25 @@ uint32_t plan_i8_unit(const GemvLaunch& L, I8UnitArgs& a) {
     a.gpc = a.G / CL;
     const int nst = a.gpc / kI8StageGroups;
     const int ms = 2 * ntn;
+    // two CTAs per SM (latency hiding, and the next launch's CTAs prefetching beside this one's) with
+    // as deep a ring as fits them; else the whole weight range resident in one CTA per SM
+    for (int S = nst; S >= 2; --S) {
+        uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.gpc, a.ncols, a.off_bar, a.off_misc, a.off_scr,
+                                   a.off_xs, a.off_cs, a.off_xe, S);
+        a.off_red = off;
+        off += align_up((uint32_t)(CL + 1) * kI8Rows * ms * 4, 128);
+        a.off_ep = off;
+        off += align_up(4u * 3u * (uint32_t)ms * 4u, 128);
+        a.off_xq = off;
+        off += (uint32_t)a.gpc * a.ncols * 64;
+        off = align_up(off, 1024);
+        a.off_ring = off;
+        off += (uint32_t)S * kI8StageBytes + 1024;
+        if (off <= kI8TwoPerSm) {
+            a.S = S;
+            return off;
+        }
+    }
     for (int S = nst; S >= 2 || S == nst; --S) {
         uint32_t off = plan_common((int)L.m, K, L.norm_w != nullptr, a.gpc, a.ncols, a.off_bar, a.off_misc, a.off_scr,
                                    a.off_xs, a.off_cs, a.off_xe, S);
