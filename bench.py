@@ -333,10 +333,8 @@ def run_ours(args):
         if world == 1 and B == 1 and tp_path.exists():
             traffic = json.loads(tp_path.read_text()).get("mlp_layer")
         ach = layer_bytes / (layer_ms * 1e-3) / 1e9
-        kname = ("i8_layer_kernel gate/up+SwiGLU launch + i8_layer_kernel down+residual launch (whole-row CTAs, "
-                 "each building its operand planes from the previous launch's binary32 row)" if B == 1 else
-                 "i8_unit_kernel gate/up+SwiGLU launch + down+residual launch (cluster K split, activation planes "
-                 "handed between them)")
+        kname = ("i8_unit_kernel gate/up+SwiGLU launch + i8_unit_kernel down+residual launch (cluster K split, "
+                 "activation planes handed between them)")
         roof = {"bound": "hbm", "kernel": f"mlp_layer: {kname}, as run inside the step"
                                           + (" (per rank; the down launch's epilogue holds the in-kernel all-reduce)"
                                              if world > 1 else ""),
@@ -428,12 +426,12 @@ def run_ours(args):
                               for k, v in fams.items()}
         extras["families_note"] = ("public single-op entry points (each stages its own activations), "
                                    "not the step's kernels; see step_split for those")
-        # the same step on the cluster K-split family (the kernels the step used before the whole-row
-        # layer kernels), same weights and inputs
-        mq.set_decode_path("i8splitk")
+        # the same step with its layers on the whole-row kernels (the opt-in family for one row), same
+        # weights and inputs
+        mq.set_decode_path("i8rows")
         try:
             stk = mq.DecodeStep(layers, fn, lm, B)
-            extras["step_family_i8splitk_ms"] = round(time_graph(torch, lambda: stk(h0), reps), 5)
+            extras["step_family_i8rows_ms"] = round(time_graph(torch, lambda: stk(h0), reps), 5)
             del stk
         finally:
             mq.set_decode_path("i8")
@@ -471,7 +469,7 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_baseline_from_device(layers, fn, lm, h0, B, args.cpu_seconds)
 
-    chunks = -(-B // 16)  # above 16 rows the step runs in 16-row chunks
+    chunks = -(-B // 8)  # above 8 rows the step runs in 8-row chunks
     launches = args.steps * chunks * (2 * L + 1)  # per step: gate/up and down per layer, then the lm_head
     line = {
         "metric": METRIC,

@@ -83,16 +83,16 @@ void marlin_q4_set_pdl(int enable);
  * and each is tested against the CPU checker):
  *   MARLIN_Q4_PATH_I8MMA   (default) integer tensor-core MMAs on the raw codes and 4 s8 activation
  *                          planes, exact int32 accumulation (k % 512 == 0, m <= 16 per launch);
- *                          the decode step's layers for one activation row run on kernels whose
- *                          CTAs each own whole rows over the full K;
- *   MARLIN_Q4_PATH_I8SPLITK the same integer MMAs, the decode step's layers for every row count on
- *                          kernels that split K over thread-block clusters and hand the activations
- *                          over as ready-made operand planes;
+ *                          the decode step's layers run on kernels that split K over thread-block
+ *                          clusters and hand the activations over as ready-made operand planes;
+ *   MARLIN_Q4_PATH_I8ROWS  the same integer MMAs, the decode step's layers for one activation row on
+ *                          kernels whose CTAs each own whole rows over the full K (each kernel
+ *                          builds its own operand from the previous launch's binary32 row);
  *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0).
  * Shapes the integer-MMA family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns
  * MARLIN_Q4_ERR_ARG for an unknown path. */
 #define MARLIN_Q4_PATH_I8MMA 0
-#define MARLIN_Q4_PATH_I8SPLITK 1
+#define MARLIN_Q4_PATH_I8ROWS 1
 #define MARLIN_Q4_PATH_BF16MMA 2
 int marlin_q4_set_decode_path(int path);
 
@@ -195,7 +195,7 @@ int marlin_q4_decode_keys(const uint64_t* keys, int64_t m, int32_t* ids, float* 
  * (src/sampling/sampler.cpp:15).  h0: bf16 [m, hidden] embedding rows.  ids [m]; best [m]
  * (optional); h_out: binary32 [m, hidden] hidden state before the final norm (optional).
  * n_layers >= 1.
- * Runs as two kernels per layer plus the lm_head (more than 16 rows: in consecutive 16-row chunks,
+ * Runs as two kernels per layer plus the lm_head (more than 8 rows: in consecutive 8-row chunks,
  * each a full step; rows are independent).
  * workspace: >= marlin_q4_decode_step_workspace_size bytes, 256-byte aligned, zero-filled before
  * the first call (its head is left zeroed by every call); one workspace serves one (m, hidden,
@@ -219,8 +219,8 @@ size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t i
  * from marlin_q4_device_alloc, the others from marlin_q4_ipc_open_handle), each
  * marlin_q4_tp_exchange_size bytes, zero before the first call (it then holds the rank's step
  * counter and the last values exchanged).  All ranks must call the step the same number of times,
- * at most 120 layers.  hidden a multiple of 512, down_proj K a multiple of 512; more than 16 rows
- * run as consecutive 16-row chunks, each a full step with its own exchanges.  workspace as for
+ * at most 120 layers.  hidden a multiple of 512, down_proj K a multiple of 512; more than 8 rows
+ * run as consecutive 8-row chunks, each a full step with its own exchanges.  workspace as for
  * marlin_q4_decode_step with intermediate = down_proj K.
  * A peer that stops writing (a dead rank): the first wait that runs out (marlin_q4_set_wait_limit_cycles)
  * sets device error 1 and every later exchange wait returns at once, so the step still completes,
@@ -231,7 +231,7 @@ int marlin_q4_tp_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int3
                              const marlin_q4_tensor* lm_shard, int64_t vocab_offset, int32_t* ids, float* best,
                              float* h_out, int32_t tp_rank, int32_t tp_size, void* const* exchange, void* workspace,
                              size_t workspace_bytes, void* stream);
-/* Bytes of one rank's exchange buffer (rows beyond 16 reuse the 16-row layout chunk by chunk). */
+/* Bytes of one rank's exchange buffer (rows beyond 8 reuse the 8-row layout chunk by chunk). */
 size_t marlin_q4_tp_exchange_size(int64_t m, int64_t hidden, int32_t tp);
 /* Zero-filled device memory for an exchange buffer (cudaMalloc: its IPC handle covers exactly it). */
 int marlin_q4_device_alloc(size_t bytes, void** ptr);

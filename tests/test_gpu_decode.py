@@ -1,10 +1,10 @@
 """GPU parity: the full Q4 decode stack (config 5) — 24 x [RMSNorm(1+w) -> Q4 MLP -> residual] ->
 final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
 
-For one activation row the step runs the whole-row layer kernels (each CTA owns whole rows over the
-full K and builds its operand from the previous launch's binary32 row); otherwise the integer-MMA
-kernels that split K over clusters, with the activations handed between them as operand planes
-(above 16 rows in 16-row chunks).  The two are checked against each other at one row, and the bf16
+The step runs the integer-MMA kernels that split K over clusters, with the activations handed
+between them as operand planes (above 8 rows in 8-row chunks); the opt-in whole-row layer kernels
+(each CTA owns whole rows over the full K and builds its operand from the previous launch's binary32
+row) are checked against them at one row, and the bf16
 mma.sync family's composition of single-op kernels against the default."""
 import numpy as np
 import pytest
@@ -69,11 +69,11 @@ def test_decode_step_in_cuda_graph(model):
 
 
 def test_layer_kernels_match_split_k(model):
-    """One row: the whole-row layer kernels (default) against the cluster K-split kernels."""
+    """One row: the cluster K-split kernels (default) against the whole-row layer kernels."""
     layers, _, lm, _, fn, _ = model
     h0 = mq.synth_bf16((1, H), 3150, 0.0, 1.0)
     ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, 1)(h0))
-    mq.set_decode_path("i8splitk")
+    mq.set_decode_path("i8rows")
     try:
         ids_c, _, h_c = mq.DecodeStep(layers, fn, lm, 1)(h0)
         torch.cuda.synchronize()

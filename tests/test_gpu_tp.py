@@ -3,7 +3,7 @@ marlin_q4.tp.FusedTPDecodeStep) on 2, 4 and 8 GPUs, one process per GPU, at the 
 (24 layers, hidden 2048, intermediate 6144, vocabulary 248320): sharded weights (gate/up by rows,
 down by K with zero padding to a multiple of 512 -- 768 -> 1024 columns at 8 ranks --, lm_head by
 vocabulary rows), the per-layer all-reduce and the argmax merge done by the kernels over peer memory.
-Rows 1, 8, 16 and 32 (32 runs as two 16-row chunks, each a full step with its own exchanges).
+Rows 1, 8, 16 and 32 (16 and 32 run as 8-row chunks, each a full step with its own exchanges).
 Checked: every rank ends with the same h and ids (sums in rank order), a second call reproduces the
 first, and the result matches the unsharded single-GPU step (ids exact, h within 1e-5 of the row
 maximum; the all-reduce changes the summation order of down_proj).
@@ -172,7 +172,7 @@ def _padded_worker(rank, world, port, path, inter, pad_to, m):
 
 @pytest.mark.parametrize("inter,pad_to,m", [(6144, 6656, 2), (768, 1024, 20)])
 def test_tp_entry_one_rank_with_padded_down_k(tmp_path, inter, pad_to, m):
-    """20 rows run as a 16-row and a 4-row chunk."""
+    """20 rows run as two 8-row chunks and a 4-row chunk."""
     path = str(tmp_path / "pad.npz")
     mp.spawn(_padded_worker, args=(1, _free_port(), path, inter, pad_to, m), nprocs=1, join=True)
     r = np.load(path)
