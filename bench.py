@@ -426,16 +426,6 @@ def run_ours(args):
                               for k, v in fams.items()}
         extras["families_note"] = ("public single-op entry points (each stages its own activations), "
                                    "not the step's kernels; see step_split for those")
-        # the same step with its layers on the whole-row kernels (the opt-in family for one row), same
-        # weights and inputs
-        mq.set_decode_path("i8rows")
-        try:
-            stk = mq.DecodeStep(layers, fn, lm, B)
-            extras["step_family_i8rows_ms"] = round(time_graph(torch, lambda: stk(h0), reps), 5)
-            del stk
-        finally:
-            mq.set_decode_path("i8")
-
         # config 1 GEMV: 6144x2048, bf16 x [1, 2048], over 24 distinct weight copies (170 MB > L2)
         xb = mq.synth_bf16((1, H), 7, 0.0, 1.0)
 

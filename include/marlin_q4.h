@@ -80,19 +80,15 @@ void marlin_q4_set_wait_limit_cycles(uint64_t cycles);
  * Enabled by default; enable = 0 launches every kernel with plain stream ordering. */
 void marlin_q4_set_pdl(int enable);
 /* Decode kernel family (process-wide; both compute the same function, within the float tolerance,
- * and each is tested against the CPU checker):
+ * and each is tested against the CPU checker; value 1 is not used):
  *   MARLIN_Q4_PATH_I8MMA   (default) integer tensor-core MMAs on the raw codes and 4 s8 activation
  *                          planes, exact int32 accumulation (k % 512 == 0, m <= 16 per launch);
  *                          the decode step's layers run on kernels that split K over thread-block
  *                          clusters and hand the activations over as ready-made operand planes;
- *   MARLIN_Q4_PATH_I8ROWS  the same integer MMAs, the decode step's layers for one activation row on
- *                          kernels whose CTAs each own whole rows over the full K (each kernel
- *                          builds its own operand from the previous launch's binary32 row);
  *   MARLIN_Q4_PATH_BF16MMA bf16 mma.sync on registers (any k % 64 == 0).
  * Shapes the integer-MMA family does not cover fall back to MARLIN_Q4_PATH_BF16MMA.  Returns
  * MARLIN_Q4_ERR_ARG for an unknown path. */
 #define MARLIN_Q4_PATH_I8MMA 0
-#define MARLIN_Q4_PATH_I8ROWS 1
 #define MARLIN_Q4_PATH_BF16MMA 2
 int marlin_q4_set_decode_path(int path);
 

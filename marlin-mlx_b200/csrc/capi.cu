@@ -364,77 +364,6 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
     int rc;
     const void* cur = h0;
     int32_t cur_dtype = MARLIN_Q4_BF16;
-    if (decode_path() == kPathI8Rows && m == 1) {
-        // one activation row: the whole-row layer kernels (each builds its own operand from the
-        // previous launch's binary32 row), if every layer's shape fits them
-        bool ok = true;
-        GemvLaunch G{}, D{};
-        for (int32_t l = 0; l < n_layers && ok; ++l) {
-            G.m = D.m = m;
-            G.y_dtype = D.y_dtype = MARLIN_Q4_F32;
-            G.epi = kEpiSwiglu;
-            G.w0 = view(&layers[l].gate_proj);
-            G.w1 = view(&layers[l].up_proj);
-            D.epi = kEpiResid;
-            D.w0 = view(&layers[l].down_proj);
-            D.resid = h0;
-            ok = i8_layer_supported(G) && i8_layer_supported(D);
-        }
-        if (ok) {
-            for (int32_t l = 0; l < n_layers; ++l) {
-                const marlin_q4_layer& Ly = layers[l];
-                G = GemvLaunch{};
-                G.x = cur;
-                G.x_dtype = cur_dtype;
-                G.m = m;
-                G.norm_w = Ly.post_attn_norm;
-                G.eps = eps;
-                G.w0 = view(&Ly.gate_proj);
-                G.w1 = view(&Ly.up_proj);
-                G.y = act;
-                G.y_dtype = MARLIN_Q4_F32;
-                G.ldy = inter;  // the down kernel reads rows of its K (zero padding beyond gate's rows)
-                G.epi = kEpiSwiglu;
-                G.pdl = g_pdl;
-                if ((rc = cuda_status(launch_i8_layer(G, st)))) return rc;
-                D = GemvLaunch{};
-                D.x = act;
-                D.x_dtype = MARLIN_Q4_F32;
-                D.m = m;
-                D.w0 = view(&Ly.down_proj);
-                D.y = h;
-                D.y_dtype = MARLIN_Q4_F32;
-                D.ldy = hidden;
-                D.resid = cur;
-                D.resid_dtype = cur_dtype;
-                D.epi = kEpiResid;
-                D.pdl = g_pdl;
-                if (tpx) {
-                    D.tp = *tpx;
-                    D.tp.parity = l & 1;
-                    D.tp.layer = l;
-                }
-                if ((rc = cuda_status(launch_i8_layer(D, st)))) return rc;
-                cur = h;
-                cur_dtype = MARLIN_Q4_F32;
-            }
-            LmHeadLaunch Lh{};
-            Lh.x = h;
-            Lh.x_dtype = MARLIN_Q4_F32;
-            Lh.m = m;
-            Lh.norm_w = final_norm;
-            Lh.eps = eps;
-            Lh.w = view(lm);
-            Lh.keys = static_cast<unsigned long long*>(lmws);
-            Lh.counter = reinterpret_cast<unsigned int*>(Lh.keys + m);
-            Lh.ids = ids;
-            Lh.best = best;
-            Lh.pdl = g_pdl;
-            Lh.vocab_offset = vocab_offset;
-            if (tpx) Lh.tp = *tpx;
-            return cuda_status(launch_i8_lm_head(Lh, st));
-        }
-    }
     for (int32_t l = 0; l < n_layers; ++l) {
         const marlin_q4_layer& Ly = layers[l];
         GemvLaunch G{};

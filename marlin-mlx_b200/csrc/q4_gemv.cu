@@ -762,7 +762,7 @@ int g_decode_path = kPathI8;
 int decode_path() { return g_decode_path; }
 
 bool set_decode_path(int path) {
-    if (path != kPathI8 && path != kPathI8Rows && path != kPathBf16) return false;
+    if (path != kPathI8 && path != kPathBf16) return false;
     g_decode_path = path;
     return true;
 }

@@ -91,13 +91,12 @@ struct GemvLaunch {
 };
 
 // Decode kernel families (marlin_q4_set_decode_path): integer MMAs (default; the decode step's layers
-// on the cluster K-split kernels with operand planes handed between them), integer MMAs with the
-// step's layers for one activation row on the whole-row layer kernels, and bf16 mma.sync.  Shapes
+// on the cluster K-split kernels with operand planes handed between them) and bf16 mma.sync.  Shapes
 // the integer-MMA kernels do not cover (k % 512 != 0) use the bf16 mma.sync kernels.
-enum DecodePath : int { kPathI8 = 0, kPathI8Rows = 1, kPathBf16 = 2 };
+enum DecodePath : int { kPathI8 = 0, kPathBf16 = 2 };
 bool set_decode_path(int path);
 int decode_path();
-inline bool path_is_i8(int p) { return p == kPathI8 || p == kPathI8Rows; }
+inline bool path_is_i8(int p) { return p == kPathI8; }
 
 // Activation rows per launch of the selected family for this shape (the C ABI loops over passes).
 int gemv_max_rows(int act_dtype, bool normed, int64_t k);

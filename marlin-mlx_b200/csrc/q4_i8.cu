@@ -731,330 +731,6 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
 }
 
 // ------------------------------------------------------------------------------------------------
-// decode layer kernels for one activation row: every CTA owns whole output rows over the full K
-// ------------------------------------------------------------------------------------------------
-// Inside the decode step each launch of i8_unit_kernel spends more time around its K loop than in
-// it (dependency release, cluster K-split reduction, the planes epilogue) and 192 gate/up CTAs
-// double-load 44 of the 148 SMs.  For one activation row the layer runs instead as two launches of
-// i8_layer_kernel, each CTA owning R whole rows:
-//   * gate/up: F features per CTA (R = 2F rows: F gate rows, then F up rows), F a multiple of 8
-//     chosen so that the CTAs fit the SMs (F = 48 for 6144 features: 128 CTAs);
-//   * down: 16 rows per CTA (128 CTAs for 2048 rows).
-// Every weight byte of the CTA (gate/up: 108 KB, down: 54 KB) has its own place in shared memory
-// and is requested before griddepcontrol.wait, so it streams while the previous launch runs (the
-// two kernels' CTAs fit one SM together).  No cluster, no cross-CTA reduction: the 8 consumer warps
-// split K (warp w takes the 128-byte lines w, w + 8, ...), their partials meet in shared memory in
-// a fixed order, and the epilogue writes plain binary32 rows (act, or h = resid + down).
-// Each kernel builds its own activation operand from the previous launch's binary32 row: four s8
-// planes per 64-group with the group's exponent (as write_planes does), the RMSNorm (1 + w) folded
-// in and its row factor applied after the dot product (gate/up).  NC = operand columns per group:
-// 4 (one row; MMA lanes of columns 4..7 read columns 0..3 again and their results are dropped).
-constexpr int kLyWarps = 8;
-constexpr int kLyThreads = (kLyWarps + 1) * 32;
-constexpr int kLyMaxTiles = 6;  // 16-row tiles per CTA (gate/up: 2F / 16 with F <= 48)
-
-struct LayerArgs {
-    CUtensorMap tw0, ts0, tb0, tw1, ts1, tb1;  // gate (or down) and up: box rows = F
-    const void* x;                             // [1, K] activations (x_dtype)
-    const uint16_t* norm_w;                    // gate/up: RMSNorm weight (null: none)
-    float* y;                                  // [m, ldy] binary32: act (gate/up) or h (down)
-    const void* resid;                         // down: [1, n] residual (resid_dtype)
-    int x_dtype, resid_dtype, swiglu;
-    float eps;
-    int64_t n;   // rows of w0 (gate/up: features)
-    int64_t ldy;  // row stride of y (gate/up: the K of the down projection that reads it)
-    int K, G, lines, F;
-    TpExchange tp;  // down with tp.tp > 1: partial rows summed over the ranks before the residual
-    uint32_t off_pk, off_sc, off_bi, off_xq, off_xs, off_xe, off_red, off_bar, off_misc;
-};
-
-// Shared memory of i8_layer_kernel (offsets from the 1024-aligned base); returns the total.
-__host__ __device__ inline uint32_t plan_layer(int R, int G, int NC, LayerArgs* a) {
-    const int lines = G / 4, chunks = G / 8;
-    uint32_t off = 0;
-    a->off_pk = off;
-    off += (uint32_t)lines * R * 128;  // [line][R][128 B], 128-byte swizzle (R % 8 == 0: 1 KB atoms)
-    a->off_sc = off;
-    off += (uint32_t)chunks * R * 16;  // [chunk of 8 groups][R][8] bf16
-    a->off_bi = off;
-    off += (uint32_t)chunks * R * 16;
-    a->off_xq = off;
-    off += (uint32_t)G * NC * 64;      // [group][column][64] s8 digits
-    a->off_xs = off;
-    off += align_up((uint32_t)G * NC * 4, 128);
-    a->off_xe = off;
-    off += align_up((uint32_t)G * NC * 4, 128);
-    a->off_red = off;
-    off += align_up((uint32_t)kLyWarps * R * 4 * (NC / 4), 128);  // [warp][row][activation row] partials
-    a->off_bar = off;
-    off += align_up((uint32_t)(lines + 1) * 8, 128);
-    a->off_misc = off;
-    off += 512;  // abort, ssq per warp [8], cs [8], SwiGLU exchange [48]
-    return off;
-}
-
-template <int T, int NC>
-__global__ void __launch_bounds__(kLyThreads, 2) i8_layer_kernel(const __grid_constant__ LayerArgs a) {
-    static_assert(NC == 4 || NC == 8, "operand columns");
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = align_smem_1024(smem_raw);
-    constexpr int R = 16 * T;
-    constexpr int M = NC / 4;  // activation rows (1, or 2 with NC = 8)
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int lines = a.lines, G = a.G, K = a.K, F = a.F;
-    const bool swiglu = a.swiglu != 0;
-    const int64_t row0 = (int64_t)blockIdx.x * F;  // first row of w0 (and of w1) owned by this CTA
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + a.off_bar);
-    volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
-    float* ssqw = reinterpret_cast<float*>(smem + a.off_misc + 16);   // [8][M] sums of squares
-    float* cs = reinterpret_cast<float*>(smem + a.off_misc + 96);     // [8] plane weights
-    float* xch = reinterpret_cast<float*>(smem + a.off_misc + 128);   // [48 * M] up -> gate hand-over
-    float* red = reinterpret_cast<float*>(smem + a.off_red);          // [8][R][M]
-    uint8_t* xq = smem + a.off_xq;
-    float* xs = reinterpret_cast<float*>(smem + a.off_xs);
-    float* xe = reinterpret_cast<float*>(smem + a.off_xe);
-
-    if (tid == kLyWarps * 32) {
-        *abort = 0;
-        for (int l = 0; l < lines; ++l) mbar_init(&bar[l], 1);
-        fence_mbar_init();
-        prefetch_tmap(&a.tw0);
-        // all of the CTA's weights, before the dependency wait: line l carries its packed words and,
-        // for even l, the scales and biases of groups [4l, 4l + 8)
-        const int rb = swiglu ? F : R;  // rows per box
-        for (int l = 0; l < lines; ++l) {
-            const uint32_t bytes = (uint32_t)R * 128 + ((l & 1) ? 0u : (uint32_t)R * 32);
-            mbar_arrive_expect_tx(&bar[l], bytes);
-            uint8_t* pk = smem + a.off_pk + (uint32_t)l * R * 128;
-            tma_load_2d(pk, &a.tw0, l * 32, (int32_t)row0, &bar[l]);
-            if (swiglu) tma_load_2d(pk + rb * 128, &a.tw1, l * 32, (int32_t)row0, &bar[l]);
-            if ((l & 1) == 0) {
-                const uint32_t c = (uint32_t)(l >> 1) * R * 16;
-                tma_load_2d(smem + a.off_sc + c, &a.ts0, l * 4, (int32_t)row0, &bar[l]);
-                tma_load_2d(smem + a.off_bi + c, &a.tb0, l * 4, (int32_t)row0, &bar[l]);
-                if (swiglu) {
-                    tma_load_2d(smem + a.off_sc + c + rb * 16, &a.ts1, l * 4, (int32_t)row0, &bar[l]);
-                    tma_load_2d(smem + a.off_bi + c + rb * 16, &a.tb1, l * 4, (int32_t)row0, &bar[l]);
-                }
-            }
-        }
-    }
-    // operands that do not depend on the previous launch: the RMSNorm weights of this thread's units
-    const int units = K / 8;
-    constexpr int kMaxU = 3;  // 8-element units per consumer thread (K <= 6144)
-    uint4 nwv[kMaxU];
-#pragma unroll
-    for (int u = 0; u < kMaxU; ++u) {
-        nwv[u] = make_uint4(0, 0, 0, 0);
-        const int ui = tid + u * kLyWarps * 32;
-        if (a.norm_w && warp < kLyWarps && ui < units) nwv[u] = *reinterpret_cast<const uint4*>(a.norm_w + ui * 8);
-    }
-    __syncthreads();
-    // the next launch may start as soon as every CTA of this one is resident: it only prefetches
-    // weights until its own griddepcontrol.wait
-    pdl_launch_dependents();
-    pdl_wait();
-
-    if (warp == kLyWarps) {
-        // producer: nothing left to issue; wait for the copies before the CTA may exit
-        if (lane == 0)
-            for (int l = 0; l < lines; ++l) drain_wait(&bar[l], 0u);
-        return;
-    }
-
-    // ---- the activation operand: planes of u = x (1 + w) per 64-group, 64 sum(u), 2^e ----------
-    float ssq[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) ssq[m] = 0.f;
-    {
-        float v[M][kMaxU][8];
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int u = 0; u < kMaxU; ++u) {
-                const int ui = tid + u * kLyWarps * 32;
-                if (ui < units) load8(a.x, a.x_dtype, (int64_t)m * K + ui * 8, v[m][u]);
-            }
-#pragma unroll
-        for (int u = 0; u < kMaxU; ++u) {
-            const int ui = tid + u * kLyWarps * 32;
-            if (u * kLyWarps * 32 >= units) break;  // block-uniform
-            const bool ok = ui < units;           // units % 256 == 0 is not required: guard the tail
-            const int gi = ui >> 3, u8 = ui & 7;
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float w[8];
-                float amx = 0.f, sm = 0.f;
-                if (ok) {
-                    if (a.norm_w) ssq[m] = __fadd_rn(ssq[m], unit_ssq(v[m][u], a.x_dtype));
-                    const uint32_t w4[4] = {nwv[u].x, nwv[u].y, nwv[u].z, nwv[u].w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        w[j] = a.norm_w ? __fmul_rn(v[m][u][j],
-                                                    __fadd_rn(1.0f, bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu)))
-                                        : v[m][u][j];
-                        amx = fmaxf(amx, fabsf(w[j]));
-                        sm = __fadd_rn(sm, w[j]);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) w[j] = 0.f;
-                }
-                // the group's 8 units are 8 consecutive lanes
-                unsigned mb = __float_as_uint(amx);
-                mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
-                mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
-                mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
-                sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-                sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-                sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-                if (ok) {
-                    const int e = row_exp(mb);
-                    uint32_t b[4][2];
-                    planes8(w, e, b);
-#pragma unroll
-                    for (int p = 0; p < 4; ++p)
-                        *reinterpret_cast<uint2*>(xq + ((size_t)gi * NC + 4 * m + p) * 64 + u8 * 8) =
-                            make_uint2(b[p][0], b[p][1]);
-                    if (u8 == 0) {
-                        const float pe = pow2f(e);
-                        *reinterpret_cast<float4*>(xs + gi * NC + 4 * m) = make_float4(__fmul_rn(sm, 64.0f), 0.f, 0.f, 0.f);
-                        *reinterpret_cast<float4*>(xe + gi * NC + 4 * m) = make_float4(pe, pe, pe, pe);
-                    }
-                }
-            }
-        }
-    }
-    if (a.norm_w) {
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            float s = ssq[m];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-            if (lane == 0) ssqw[warp * M + m] = s;
-        }
-    }
-    if (tid < 8) cs[tid] = (tid >> 2) < M ? pow2f(-10 - 7 * (tid & 3)) : 0.f;
-    named_bar_sync(1, kLyWarps * 32);
-
-    // ---- K loop: warp w takes lines w, w + 8, ... (all tiles); with fewer than 8 lines the warps of a
-    // line split its tiles ---------------------------------------------------------------------------
-    const int g = lane >> 2, tq = lane & 3;
-    float y[T][4], yb[T][2];
-#pragma unroll
-    for (int t = 0; t < T; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = yb[t][0] = yb[t][1] = 0.f;
-    int l0 = warp, lstep = kLyWarps, t0 = 0, tstep = 1;
-    if (lines < kLyWarps) {
-        const int wpl = kLyWarps / lines;  // warps per line (lines divides 8)
-        l0 = warp / wpl;
-        lstep = lines;
-        t0 = warp % wpl;
-        tstep = wpl;
-    }
-    const int colb = NC == 8 ? g : (g & 3);             // operand column this lane's B fragment reads
-    const int colr = NC == 8 ? 4 * (tq >> 1) : 0;       // plane-0 column of the lane's activation row
-    for (int l = l0; l < lines; l += lstep) {
-        if (!warp_wait(&bar[l & ~1], 0u, abort)) break;  // scales and biases of the line's chunk
-        if ((l & 1) && !warp_wait(&bar[l], 0u, abort)) break;
-        const uint8_t* pk = smem + a.off_pk + (uint32_t)l * R * 128;
-        const uint8_t* sc = smem + a.off_sc + (uint32_t)(l >> 1) * R * 16;
-        const uint8_t* bi = smem + a.off_bi + (uint32_t)(l >> 1) * R * 16;
-        const int so = (l & 1) * 8;
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-            if (t < t0 || (t - t0) % tstep) continue;  // warp-uniform
-            const int r0 = 16 * t + g, r1 = r0 + 8;
-            const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
-            const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
-            const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
-            const uint2 b1 = *reinterpret_cast<const uint2*>(bi + r1 * 16 + so);
-            uint2 wa[4], wb[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t off = (uint32_t)((((2 * q + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
-                wa[q] = *reinterpret_cast<const uint2*>(pk + r0 * 128 + off);
-                wb[q] = *reinterpret_cast<const uint2*>(pk + r1 * 128 + off);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int gl = 4 * l + q;
-                const uint4 xv = *reinterpret_cast<const uint4*>(xq + ((size_t)(gl * NC + colb) * 64 + 16 * tq));
-                const int c0 = gl * NC + colr;
-                i8_group(wa[q], wb[q], xv, sel_bf16(s0, q), sel_bf16(s1, q), sel_bf16(b0, q), sel_bf16(b1, q), xe[c0],
-                         xs[c0], y[t], yb[t]);
-            }
-        }
-    }
-    // partials of this warp: rows 16t + g, 16t + g + 8 of activation row m = tq >> 1
-#pragma unroll
-    for (int t = 0; t < T; ++t) {
-        const float2 cv = *reinterpret_cast<const float2*>(cs + 2 * tq);
-        const float2 pp = i8_combine(y[t], yb[t], cv, tq);
-        const int m = tq >> 1;
-        if ((tq & 1) == 0 && m < M) {
-            red[(warp * R + 16 * t + g) * M + m] = pp.x;
-            red[(warp * R + 16 * t + g + 8) * M + m] = pp.y;
-        }
-    }
-    named_bar_sync(1, kLyWarps * 32);
-
-    // ---- epilogue: one thread per row (whole warps stay for the SwiGLU hand-over barrier) ------------
-    constexpr int kEpiThreads = ((R + 31) / 32) * 32;
-    if (tid >= kEpiThreads) return;
-    const bool er = tid < R;
-    float o[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        o[m] = 0.f;
-        if (er)
-            for (int w = 0; w < kLyWarps; ++w) o[m] += red[(w * R + tid) * M + m];
-    }
-    if (swiglu) {
-        if (a.norm_w) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float s = 0.f;
-                for (int w = 0; w < kLyWarps; ++w) s = __fadd_rn(s, ssqw[w * M + m]);
-                float var;
-                if (a.x_dtype == kBF16)
-                    var = bf16_round(__fmul_rn(bf16_round(s), bf16_round((float)(1.0 / (double)K))));
-                else
-                    var = __fmul_rn(s, (float)(1.0 / (double)K));
-                o[m] *= __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
-            }
-        }
-        if (er && tid >= F) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) xch[(tid - F) * M + m] = o[m];
-        }
-        named_bar_sync(2, kEpiThreads);
-        const int64_t f = row0 + tid;
-        if (tid < F && f < a.n) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const float gs = o[m], u = xch[tid * M + m];
-                const float sg = 1.0f / (1.0f + expf(-gs));
-                a.y[(int64_t)m * a.ldy + f] = (sg * gs) * u;
-            }
-        }
-        return;
-    }
-    if (!er) return;
-    const int64_t row = row0 + tid;
-    const bool live = row < a.n;
-    if (a.tp.tp > 1) tp_allreduce_rows<M>(a.tp, M, a.n, row, live, o);
-    if (live) {
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float hv = a.resid_dtype == kBF16
-                                 ? bf16_bits_to_f32(static_cast<const uint16_t*>(a.resid)[(int64_t)m * a.n + row])
-                                 : static_cast<const float*>(a.resid)[(int64_t)m * a.n + row];
-            a.y[(int64_t)m * a.ldy + row] = hv + o[m];
-        }
-    }
-}
-
-// ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
 int ntn_for(int64_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
@@ -1219,66 +895,6 @@ cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream) {
         }
     }
     return launch_ex(i8_lm_head_kernel<8, 8>, a, grid, LmStage<8>::kThreads, 1, smem, L.pdl, stream);
-}
-
-namespace {
-// Features per gate/up CTA of i8_layer_kernel: the smallest of 8, 16, 24, 48 that keeps the CTAs
-// within the SMs (48 beyond that).
-int layer_features(int64_t n) {
-    for (int f : {8, 16, 24}) if ((n + f - 1) / f <= device_num_sms()) return f;
-    return 48;
-}
-
-template <int T>
-cudaError_t dispatch_layer(const LayerArgs& a, int nc, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
-    if (nc == 8) return launch_ex(i8_layer_kernel<T, 8>, a, grid, kLyThreads, 1, smem, pdl, stream);
-    return launch_ex(i8_layer_kernel<T, 4>, a, grid, kLyThreads, 1, smem, pdl, stream);
-}
-}  // namespace
-
-bool i8_layer_supported(const GemvLaunch& L) {
-    if (L.m < 1 || L.m > 2 || L.y_dtype != kF32 || L.has_xin || L.has_xout) return false;
-    const int64_t k = L.w0.k;
-    // K % 512: 16-byte rows of the scale maps; K <= 6144: three 8-element units per consumer thread
-    if (k % 512 || k > 6144) return false;
-    const int64_t lines = k / 256;
-    if (lines < kLyWarps && kLyWarps % lines) return false;
-    if (L.epi == kEpiSwiglu) return L.w1.n == L.w0.n && L.w1.k == k && L.resid == nullptr;
-    return L.epi == kEpiResid && L.resid != nullptr && L.w0.n <= (int64_t)1 << 24;
-}
-
-cudaError_t launch_i8_layer(const GemvLaunch& L, cudaStream_t stream) {
-    LayerArgs a{};
-    const bool swiglu = L.epi == kEpiSwiglu;
-    a.x = L.x;
-    a.x_dtype = L.x_dtype;
-    a.norm_w = swiglu ? L.norm_w : nullptr;
-    a.eps = L.eps;
-    a.y = static_cast<float*>(L.y);
-    a.resid = L.resid;
-    a.resid_dtype = L.resid_dtype;
-    a.swiglu = swiglu ? 1 : 0;
-    a.n = L.w0.n;
-    a.ldy = L.ldy > 0 ? L.ldy : L.w0.n;
-    a.K = (int)L.w0.k;
-    a.G = a.K / kGroup;
-    a.lines = a.G / 4;
-    a.F = swiglu ? layer_features(L.w0.n) : 16;
-    a.tp = L.tp;
-    const int R = swiglu ? 2 * a.F : a.F, T = R / 16;
-    const int nc = L.m == 1 ? 4 : 8;
-    const uint32_t smem = plan_layer(R, a.G, nc, &a) + 1024;
-    if (smem > kI8SmemLimit) return cudaErrorInvalidConfiguration;
-    if (!encode_q4_maps(L.w0, a.F, &a.tw0, &a.ts0, &a.tb0)) return cudaErrorInvalidValue;
-    if (swiglu && !encode_q4_maps(L.w1, a.F, &a.tw1, &a.ts1, &a.tb1)) return cudaErrorInvalidValue;
-    const int grid = (int)((L.w0.n + a.F - 1) / a.F);
-    switch (T) {
-        case 1: return dispatch_layer<1>(a, nc, grid, smem, L.pdl, stream);
-        case 2: return dispatch_layer<2>(a, nc, grid, smem, L.pdl, stream);
-        case 3: return dispatch_layer<3>(a, nc, grid, smem, L.pdl, stream);
-        case 6: return dispatch_layer<6>(a, nc, grid, smem, L.pdl, stream);
-        default: return cudaErrorInvalidConfiguration;
-    }
 }
 
 int i8_device_error(bool clear) { return tu_device_error(clear); }

@@ -16,11 +16,6 @@ constexpr int kI8MaxRows = 16;
 bool i8_supported(int64_t k, int64_t m);
 // Decode GEMV family (same contract as launch_q4_gemv).
 cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream);
-// The decode step's layer kernels for one or two activation rows (i8_layer_kernel): gate/up +
-// SwiGLU (kEpiSwiglu, optional RMSNorm) or down + residual (kEpiResid, optional tensor-parallel
-// exchange), binary32 output rows, each CTA owning whole rows over the full K.
-bool i8_layer_supported(const GemvLaunch& L);
-cudaError_t launch_i8_layer(const GemvLaunch& L, cudaStream_t stream);
 // Fused lm_head + argmax (same contract as launch_q4_lm_head_argmax).
 cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream);
 // Device error word of this translation unit (see gemv_device_error).

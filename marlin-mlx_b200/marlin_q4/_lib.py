@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libmarlin_q4.so"
 OK = 0
 ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = -1, -2, -3, -4, -5, -6
 BF16, F32 = 0, 1
-PATH_I8MMA, PATH_I8ROWS, PATH_BF16MMA = 0, 1, 2
+PATH_I8MMA, PATH_BF16MMA = 0, 2
 
 # Every symbol include/marlin_q4.h declares, with its ctypes signature (restype, argtypes).
 _vp, _i64, _i32, _f32, _sz, _u64 = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float,

@@ -326,11 +326,10 @@ def set_pdl(enable: bool) -> None:
     _lib.load().marlin_q4_set_pdl(1 if enable else 0)
 
 
-DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "i8rows": _lib.PATH_I8ROWS, "bf16": _lib.PATH_BF16MMA}
+DECODE_PATHS = {"i8": _lib.PATH_I8MMA, "bf16": _lib.PATH_BF16MMA}
 
 
 def set_decode_path(path: str) -> None:
     """Select the decode kernel family: "i8" (integer MMAs, default: the decode step on the cluster
-    K-split kernels with operand planes handed between them), "i8rows" (integer MMAs, the step's
-    layers for one row on the whole-row kernels) or "bf16" (mma.sync)."""
+    K-split kernels with operand planes handed between them) or "bf16" (mma.sync)."""
     check(_lib.load().marlin_q4_set_decode_path(DECODE_PATHS[path]), "marlin_q4_set_decode_path")

@@ -2,10 +2,8 @@
 final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
 
 The step runs the integer-MMA kernels that split K over clusters, with the activations handed
-between them as operand planes (above 8 rows in 8-row chunks); the opt-in whole-row layer kernels
-(each CTA owns whole rows over the full K and builds its operand from the previous launch's binary32
-row) are checked against them at one row, and the bf16
-mma.sync family's composition of single-op kernels against the default."""
+between them as operand planes (above 8 rows in 8-row chunks); the bf16 mma.sync family's
+composition of single-op kernels is checked against it."""
 import numpy as np
 import pytest
 import torch
@@ -66,22 +64,6 @@ def test_decode_step_in_cuda_graph(model):
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(step.ids, ids_eager)
-
-
-def test_layer_kernels_match_split_k(model):
-    """One row: the cluster K-split kernels (default) against the whole-row layer kernels."""
-    layers, _, lm, _, fn, _ = model
-    h0 = mq.synth_bf16((1, H), 3150, 0.0, 1.0)
-    ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, 1)(h0))
-    mq.set_decode_path("i8rows")
-    try:
-        ids_c, _, h_c = mq.DecodeStep(layers, fn, lm, 1)(h0)
-        torch.cuda.synchronize()
-    finally:
-        mq.set_decode_path("i8")
-    assert max_rel_row_err(f32(h), f32(h_c).astype(np.float64)) < 1e-5
-    assert torch.equal(ids, ids_c)
-    assert mq.device_error() == 0
 
 
 @pytest.mark.parametrize("m", [1, 5])
