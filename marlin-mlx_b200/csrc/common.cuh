@@ -311,6 +311,20 @@ __device__ __forceinline__ void umma_smem_a(uint32_t d_taddr, uint64_t a_desc, u
         ::"r"(d_taddr), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
+// y0 += c (d0 - 1.5 2^23) and y1 += c (d1 - 1.5 2^23), d0 / d1 integer accumulators that started at
+// the bits of 1.5 2^23 read as binary32 (so d - 1.5 2^23 is the integer exactly): one packed add
+// and one packed fma (sm_100 f32x2), each element rounded as the scalar FADD and FFMA would be.
+__device__ __forceinline__ void fold_pair(float& y0, float& y1, uint32_t d0, uint32_t d1, float c) {
+    unsigned long long dd, yy, cc;
+    const unsigned long long mg = 0xCB400000CB400000ull;  // -1.5 2^23 twice
+    asm("mov.b64 %0, {%1, %2};" : "=l"(dd) : "r"(d0), "r"(d1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(yy) : "f"(y0), "f"(y1));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(cc) : "f"(c));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(dd) : "l"(dd), "l"(mg));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(yy) : "l"(cc), "l"(dd), "l"(yy));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(y0), "=f"(y1) : "l"(yy));
+}
+
 // Arrive on `bar` once all tcgen05.mma issued so far by this thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -88,7 +88,10 @@ __device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, con
         for (int j = 0; j < NTN; ++j) {
             const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
             const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);  // plane-0 column of the lane's row
-            i8_group(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+            if constexpr (NTN >= 2)
+                i8_group_chained(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+            else
+                i8_group(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
         }
     }
 }

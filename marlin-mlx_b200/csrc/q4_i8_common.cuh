@@ -93,6 +93,23 @@ __device__ __forceinline__ void i8_group(uint2 wa, uint2 wb, uint4 xv, float sr0
     yb[1] = fmaf(br1, x0, yb[1]);
 }
 
+// i8_group for wide column tiles: the even codes enter as 16 q ((w << 4) & 0xF0F0F0F0) so both MMAs
+// chain into one accumulator that starts at the bits of 1.5 * 2^23; read back as binary32 minus
+// 1.5 * 2^23 it is exactly 16 D_even + D_odd' (|.| < 2^20), so the fold needs no int-to-float
+// conversion and runs as packed pairs.  Same bits as i8_group.
+__device__ __forceinline__ void i8_group_chained(uint2 wa, uint2 wb, uint4 xv, float sr0, float sr1, float br0,
+                                                 float br1, float xe, float x0, float (&y)[4], float (&yb)[2]) {
+    const uint32_t lo[4] = {(wa.x << 4) & ~kNib, (wb.x << 4) & ~kNib, (wa.y << 4) & ~kNib, (wb.y << 4) & ~kNib};
+    const uint32_t hi[4] = {wa.x & ~kNib, wb.x & ~kNib, wa.y & ~kNib, wb.y & ~kNib};
+    int d[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
+    mma_u8s8_16832(d, lo, xv.x, xv.z);  // even elements, times 16
+    mma_u8s8_16832(d, hi, xv.y, xv.w);  // odd elements, times 16
+    fold_pair(y[0], y[1], (uint32_t)d[0], (uint32_t)d[1], sr0 * xe);
+    fold_pair(y[2], y[3], (uint32_t)d[2], (uint32_t)d[3], sr1 * xe);
+    yb[0] = fmaf(br0, x0, yb[0]);
+    yb[1] = fmaf(br1, x0, yb[1]);
+}
+
 // The outputs of a lane after the K loop: rows g (.x) and g + 8 (.y) of activation row
 // m = 2j + (t >> 1), summed over the lane pair (t, t ^ 1) that holds the row's four planes.
 __device__ __forceinline__ float2 i8_combine(const float (&y)[4], const float (&yb)[2], float2 cv, int tq) {
