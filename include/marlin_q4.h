@@ -91,6 +91,20 @@ void marlin_q4_set_pdl(int enable);
 #define MARLIN_Q4_PATH_I8MMA 0
 #define MARLIN_Q4_PATH_BF16MMA 2
 int marlin_q4_set_decode_path(int path);
+/* Kernels of the decode step's MLP layers with the integer-MMA family (process-wide):
+ *   MARLIN_Q4_STEP_FUSED  (default) all layers in one persistent kernel: each CTA owns 64
+ *                         intermediate features (gate/up rows, SwiGLU, their down_proj columns), the
+ *                         activations meet in thread-block clusters, the down_proj partial rows add up
+ *                         in a 64-bit fixed-point accumulator (order-independent, so deterministic),
+ *                         and one arrival counter per layer orders the layers; serves hidden in
+ *                         {512, 1024, 2048}, intermediate a multiple of 512 up to 64 x the SM count,
+ *                         at most 24 layers, rows in chunks of 8;
+ *   MARLIN_Q4_STEP_LAYERS two kernels per layer (K split over clusters, operand planes handed over).
+ * Shapes the fused kernel does not serve run on the per-layer kernels.  Returns MARLIN_Q4_ERR_ARG
+ * for an unknown value. */
+#define MARLIN_Q4_STEP_FUSED 0
+#define MARLIN_Q4_STEP_LAYERS 1
+int marlin_q4_set_step_kernels(int which);
 
 /* ---- quantize --------------------------------------------------------------------------------
  * Replaces mx::quantize(w, group_size, bits) at src/model/weights.cpp:46 (quantize_weight,

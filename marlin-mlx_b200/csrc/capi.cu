@@ -5,6 +5,7 @@
 // marlin_q4_device_error, which is documented as synchronous) and never allocates.
 #include "marlin_q4.h"
 
+#include "q4_fused.cuh"
 #include "q4_gemv.cuh"
 #include "q4_i8.cuh"
 #include "q4_prefill.cuh"
@@ -19,6 +20,7 @@ namespace {
 
 thread_local int t_last_cuda_error = 0;
 bool g_pdl = true;
+int g_step_kernels = MARLIN_Q4_STEP_FUSED;
 unsigned long long g_peer_wait_cycles = kPeerWaitDefaultCycles;
 
 int cuda_status(cudaError_t e) {
@@ -135,7 +137,8 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
     const int v_i8 = i8_device_error(clear != 0), v_pf = prefill_device_error(clear != 0),
-              v_mi = misc_device_error(clear != 0);
+              v_mi = misc_device_error(clear != 0), v_fu = fused_device_error(clear != 0);
+    if (!v) v = v_fu;
     if (!v) v = v_i8;
     if (!v) v = v_pf;
     if (!v) v = v_mi;
@@ -147,6 +150,12 @@ void marlin_q4_set_pdl(int enable) { g_pdl = enable != 0; }
 
 void marlin_q4_set_wait_limit_cycles(uint64_t cycles) {
     g_peer_wait_cycles = cycles ? (unsigned long long)cycles : kPeerWaitDefaultCycles;
+}
+
+int marlin_q4_set_step_kernels(int which) {
+    if (which != MARLIN_Q4_STEP_FUSED && which != MARLIN_Q4_STEP_LAYERS) return MARLIN_Q4_ERR_ARG;
+    g_step_kernels = which;
+    return MARLIN_Q4_OK;
 }
 
 int marlin_q4_set_decode_path(int path) {
@@ -324,7 +333,9 @@ size_t step_ssq_bytes(int64_t m, int64_t hidden) { return align16((size_t)((hidd
 size_t step_compose_bytes(int64_t m, int64_t hidden, int64_t inter) {
     size_t b = align16((size_t)m * hidden * 4) + align16((size_t)m * inter * 4);
     if (m <= kStepChunkRows)
-        b = (b + 255) / 256 * 256 + i8_planes_bytes(m, inter) + i8_planes_bytes(m, hidden) + step_ssq_bytes(m, hidden);
+        b = std::max((b + 255) / 256 * 256 + i8_planes_bytes(m, inter) + i8_planes_bytes(m, hidden) +
+                         step_ssq_bytes(m, hidden),
+                     fused_acc_bytes(m, hidden));  // or the one-kernel stack's accumulators
     else  // h for all rows, then the scratch of one chunk (the step runs in row chunks)
         b = std::max(b, align16((size_t)m * hidden * 4) + step_compose_bytes(kStepChunkRows, hidden, inter));
     return b;
@@ -429,6 +440,49 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
     if (tpx) Lh.tp = *tpx;
     return cuda_status(launch_i8_lm_head(Lh, st));
 }
+// The decode step with the MLP layers as one persistent kernel (q4_fused.cu) followed by the fused
+// lm_head + argmax, which reads the final h from the kernel's fixed-point accumulator, writes h_out
+// when asked, and clears the kernel's barrier words (sync, in the zero-invariant head of the
+// workspace) for the next step.
+int decode_step_fused(const uint16_t* h0, int64_t m, int64_t hidden, int64_t inter, int32_t n_layers,
+                      const marlin_q4_layer* layers, const uint16_t* final_norm, float eps, const marlin_q4_tensor* lm,
+                      int32_t* ids, float* best, float* h_out, uint8_t* scratch, unsigned* sync, void* lmws,
+                      cudaStream_t st) {
+    FusedLayer fl[kFusedMaxLayers];
+    for (int32_t l = 0; l < n_layers; ++l)
+        fl[l] = FusedLayer{layers[l].post_attn_norm, view(&layers[l].gate_proj), view(&layers[l].up_proj),
+                           view(&layers[l].down_proj)};
+    FusedLaunch F{};
+    F.h0 = h0;
+    F.m = m;
+    F.hidden = hidden;
+    F.inter = inter;
+    F.n_layers = n_layers;
+    F.layers = fl;
+    F.eps = eps;
+    F.acc = reinterpret_cast<unsigned long long*>(scratch);
+    F.sync = sync;
+    F.wait_cycles = g_peer_wait_cycles;
+    F.pdl = g_pdl;
+    int rc;
+    if ((rc = cuda_status(launch_fused_layers(F, st)))) return rc;
+    LmHeadLaunch Lh{};
+    Lh.x = F.acc + (size_t)(n_layers % 3) * (size_t)m * (size_t)hidden;
+    Lh.x_dtype = kFix64;
+    Lh.m = m;
+    Lh.norm_w = final_norm;
+    Lh.eps = eps;
+    Lh.w = view(lm);
+    Lh.keys = static_cast<unsigned long long*>(lmws);
+    Lh.counter = reinterpret_cast<unsigned int*>(Lh.keys + m);
+    Lh.ids = ids;
+    Lh.best = best;
+    Lh.pdl = g_pdl;
+    Lh.x_out = h_out;
+    Lh.reset = sync;
+    Lh.n_reset = 2;
+    return cuda_status(launch_i8_lm_head(Lh, st));
+}
 }  // namespace
 
 size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate) {
@@ -470,6 +524,24 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     float* h = reinterpret_cast<float*>(scratch);
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
+    unsigned* sync = reinterpret_cast<unsigned*>(ws);  // barrier words of the one-kernel stack, zero-invariant
+    const bool fused = path_is_i8(decode_path()) && g_step_kernels == MARLIN_Q4_STEP_FUSED && uniform &&
+                       i8_supported(hidden, std::min<int64_t>(m, kStepChunkRows)) &&
+                       fused_supported(std::min<int64_t>(m, kStepChunkRows), hidden, inter, n_layers);
+    if (fused && m <= kStepChunkRows)
+        return decode_step_fused(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h_out,
+                                 scratch, sync, lmws, st);
+    if (fused) {  // consecutive chunks of kStepChunkRows rows (the rows are independent)
+        uint8_t* cs = scratch + align16((size_t)m * hidden * 4);
+        for (int64_t r0 = 0; r0 < m; r0 += kStepChunkRows) {
+            const int64_t mc = std::min<int64_t>(kStepChunkRows, m - r0);
+            if ((rc = decode_step_fused(h0 + r0 * hidden, mc, hidden, inter, n_layers, layers, final_norm, eps, lm,
+                                        ids + r0, best ? best + r0 : nullptr, h_out ? h_out + r0 * hidden : nullptr,
+                                        cs, sync, lmws, st)))
+                return rc;
+        }
+        return MARLIN_Q4_OK;
+    }
     if (path_is_i8(decode_path()) && uniform && m <= kStepChunkRows && i8_supported(hidden, m) &&
         i8_supported(inter, m) && hidden % 128 == 0)
         return decode_step_planes(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h, scratch,

@@ -1,0 +1,722 @@
+// q4_fused.cu — the Q4 MLP layers of a decode step as one persistent kernel (sm_100a).
+//
+// Replaces, for decode-sized batches, the layer loop of marlin-mlx's text model restricted to its
+// Q4 sublayers (src/model/marlin.cpp:103-146: per layer h += mlp_forward(rms_norm(h)), with
+// rms_norm :12-16, swiglu :27-29, mlp_forward :31-35 and the qmatmul of :18-25 on every
+// projection).  The final norm, lm_head and argmax follow as the fused lm_head kernel.
+//
+// Why one kernel.  At one activation row a layer streams 21 MB (3.3 us at HBM speed), but as two
+// dependent launches it pays a launch boundary, a cluster reduction and an epilogue twice.  Here
+// each layer costs one grid-wide arrival counter, and the weights of the next layer stream into
+// shared memory while the current one finishes.
+//
+// Work split (inter = 64 G features, G CTAs, thread-block clusters of 8):
+//   CTA c owns intermediate features [64 c, 64 c + 64): it computes their gate and up rows over all
+//   of `hidden` from the exact s8 planes of rms_norm(h) (the integer-MMA arithmetic of q4_i8.cu),
+//   then SwiGLU, and writes the 64 activations as s8 planes into the shared memory of all eight
+//   CTAs of its cluster (distributed shared memory, one mbarrier per CTA counts the arrivals).
+//   CTA rank i of cluster j then multiplies down_proj rows [i hidden/8, (i+1) hidden/8) by the
+//   cluster's 512 features (columns [512 j, 512 j + 512): one 16-byte scale box per row, fully
+//   used) and adds the partial rows into a 64-bit fixed-point accumulator of h (value * 2^32) with
+//   integer atomics: the sum does not depend on their order, so the result is deterministic.
+//   Cluster 0 also adds the residual h.  Every CTA then bumps one arrival counter; the next layer
+//   starts when it reaches (layer + 2) * G, and each CTA reads the whole new h from L2.
+//
+// Accumulators rotate over three buffers (acc_l = acc[l % 3]); acc_{l+2} is zeroed, one slice per
+// CTA, after the barrier that starts layer l (everyone has read acc_{l-1} by then), and acc_1,
+// acc_2 at kernel start behind a start arrival.  The counter is cleared by the next kernel.
+//
+// Warp roles: warps 0-7 compute; warp 8 is the TMA producer, which walks every layer's stages
+// (gate/up: 64 + 64 rows x 4 groups; down_proj: up to 128 rows x 4 groups; 20 KB each) through one
+// ring, so the next layer's weights stream while the consumers wait at the layer barrier.
+//
+// Every wait is bounded (SM clock cycles): one that runs out records a device error, raises the
+// CTA's abort flag and the grid's abort word, and every other wait then returns at once; the CTAs
+// leave through the closing cluster barrier.
+#include "common.cuh"
+#include "q4_fused.cuh"
+#include "q4_gemv.cuh"
+#include "q4_host.cuh"
+#include "q4_i8_common.cuh"
+#include "q4_stage.cuh"
+
+#include <algorithm>
+#include <mutex>
+
+// Optional timeline hooks, empty in the library build: FUSED_MARK(layer, point) at the phase
+// boundaries of each layer, evaluated by every consumer thread (a definition keeps thread 0's);
+// FUSED_PMARK(layer, point) in the producer thread when it issues a layer's first and last stage.
+#ifndef FUSED_MARK
+#define FUSED_MARK(l, k)
+#endif
+#ifndef FUSED_PMARK
+#define FUSED_PMARK(l, k)
+#endif
+
+namespace marlin {
+namespace {
+
+constexpr int kFWarps = 8;                          // consumer warps
+constexpr int kFThreads = (kFWarps + 1) * 32;       // + the TMA producer warp
+constexpr int kFCluster = 8;
+constexpr int kFRows = 128;                         // rows per ring stage
+constexpr uint32_t kFPacked = kFRows * 128;         // packed lines of one stage (4 groups per row)
+constexpr uint32_t kFSb = kFRows * 16;              // scale (or bias) box: 8 groups x 128 rows
+constexpr uint32_t kFStage = kFPacked + 2 * kFSb;   // 20 KB
+constexpr uint32_t kFSmemLimit = 226 * 1024;
+constexpr int kFBar = 1;                            // named barrier of the consumer warps
+#ifndef FUSED_CHAIN
+#define FUSED_CHAIN 1
+#endif
+constexpr bool kFChain = FUSED_CHAIN != 0;          // chained even/odd MMAs and packed fold at every width
+
+struct FusedLayerMaps {
+    CUtensorMap g, gs, gb, u, us, ub, d, ds, db;  // gate/up boxes of 64 rows, down_proj boxes of RB rows
+};
+
+struct FusedArgs {
+    FusedLayerMaps lay[kFusedMaxLayers];
+    const uint16_t* norm_w[kFusedMaxLayers];
+    const uint16_t* h0;
+    unsigned long long* acc;
+    unsigned* sync;
+    unsigned long long wait_cycles;
+    int M, H, n_layers, S;
+    float eps;
+    uint32_t off_bar, off_misc, off_hq, off_hxs, off_hxe, off_cs, off_aq, off_axs, off_axe, off_out, off_res, off_ring;
+};
+static_assert(sizeof(FusedArgs) <= 32000, "kernel parameters above the 32 KB limit");
+
+// ---- fixed point, global synchronisation -------------------------------------------------------------
+constexpr float kFixScale = 4294967296.0f;  // 2^32
+
+__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * kFixScale); }
+
+__device__ __forceinline__ void red_add_u64(unsigned long long* p, long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)v) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Thread 0 of the consumers: wait until the arrival counter reaches `target`, bounded; on a timeout
+// or a raised grid abort word, raise the CTA's abort flag and return.
+__device__ void grid_wait(unsigned* sync, unsigned target, unsigned long long limit, volatile int* abort) {
+    const unsigned long long t0 = cycles_now();
+    for (uint32_t it = 0;; ++it) {
+        if (ld_relaxed(sync) >= target) {
+            fence_acq_rel_gpu();
+            return;
+        }
+        if ((it & 15u) == 15u) {
+            if (ld_relaxed(sync + 1)) {
+                *abort = 1;
+                return;
+            }
+            if (cycles_now() - t0 > limit) {
+                record_device_error(kDevErrMbarTimeout);
+                atomicExch(sync + 1, 1u);
+                *abort = 1;
+                return;
+            }
+        }
+    }
+}
+
+// Named barrier of the consumer warps that also returns whether any of them passed `p` true: the
+// abort decision is taken once per phase, identically in every consumer thread.
+__device__ __forceinline__ bool cons_bar_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(kFBar), "r"(kFWarps * 32)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void cons_bar() { asm volatile("bar.sync %0, %1;" ::"r"(kFBar), "r"(kFWarps * 32) : "memory"); }
+
+// ---- distributed shared memory ---------------------------------------------------------------------
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t x, uint32_t y) {
+    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrive on the mbarrier at cluster address `addr` without ordering: the caller has made its stores
+// visible with fence_acq_rel_cluster() first (one fence for all targets instead of a release per
+// arrival, each of which costs a round trip).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Warp-wide bounded wait for the cluster's activation planes; gives up on a timeout, the CTA's abort
+// flag or the grid's abort word.
+__device__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, const unsigned* gabort,
+                                  unsigned long long limit) {
+    if (__all_sync(0xffffffffu, mbar_try_wait_cluster(bar, parity) ? 1 : 0)) return true;
+    const unsigned long long t0 = cycles_now();
+    for (uint32_t it = 0;; ++it) {
+        if (__all_sync(0xffffffffu, mbar_try_wait_cluster(bar, parity) ? 1 : 0)) return true;
+        if ((it & 63u) == 63u) {
+            int stop = 0;
+            if ((threadIdx.x & 31) == 0) {
+                if (*abort || ld_relaxed(gabort)) {
+                    stop = 1;
+                } else if (cycles_now() - t0 > limit) {
+                    record_device_error(kDevErrMbarTimeout);
+                    stop = 1;
+                }
+            }
+            if (__shfl_sync(0xffffffffu, stop, 0)) {
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Zero this CTA's slice of an n-word accumulator (L2 only).
+__device__ __forceinline__ void zero_slice(unsigned long long* p, size_t n, int c, int G, int tid) {
+    const size_t b = n * (size_t)c / (size_t)G, e = n * (size_t)(c + 1) / (size_t)G;
+    for (size_t i = b + tid; i < e; i += kFWarps * 32) __stcg(p + i, 0ull);
+}
+
+// ------------------------------------------------------------------------------------------------
+// the kernel
+// ------------------------------------------------------------------------------------------------
+template <int NTN>
+__global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid_constant__ FusedArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = align_smem_1024(smem_raw);
+    constexpr int MS = 2 * NTN;     // activation rows per pass (2 per 8-column MMA tile)
+    constexpr int ncols = 8 * NTN;  // MMA columns: 4 planes per row
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int M = a.M, H = a.H, S = a.S, NL = a.n_layers;
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    const uint32_t crank = cluster_rank();
+    const int cj = c / kFCluster;
+    const int HG = H / kGroup;                 // 64-groups of h
+    const int RD = H / kFCluster;              // down_proj rows of this CTA
+    const int rd0 = (int)crank * RD;
+    const int RB = RD < kFRows ? RD : kFRows;  // rows per down_proj stage
+    const int nhalf = RD / RB;
+    const int gu_st = HG / 4;                  // gate/up stages per layer
+    const int per_layer = gu_st + 2 * nhalf;
+    const size_t MH = (size_t)M * H;
+
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+    uint64_t* empty = full + S;
+    uint64_t* actbar = empty + S;  // [2]: activation planes of the cluster, by layer parity
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
+    float* red = reinterpret_cast<float*>(smem + a.off_misc + 64);  // [8 warps][MS] sums of squares
+    float* rf = red + kFWarps * MS;                                   // [MS] RMSNorm factors
+    uint8_t* hq = smem + a.off_hq;                                    // [HG][ncols][64] planes of rms_norm(h)
+    float* hxs = reinterpret_cast<float*>(smem + a.off_hxs);
+    float* hxe = reinterpret_cast<float*>(smem + a.off_hxe);
+    float* cs = reinterpret_cast<float*>(smem + a.off_cs);
+    uint8_t* aq = smem + a.off_aq;                                    // [2][8][ncols][64] act planes
+    float* axs = reinterpret_cast<float*>(smem + a.off_axs);          // [2][8][ncols]
+    float* axe = reinterpret_cast<float*>(smem + a.off_axe);
+    float* out = reinterpret_cast<float*>(smem + a.off_out);          // [128][MS] gate / up rows
+    float* res = reinterpret_cast<float*>(smem + a.off_res);          // [RD][MS] residual rows
+    uint8_t* ring = smem + a.off_ring;
+    const uint32_t aq_bytes = (uint32_t)kFCluster * ncols * 64, ax_words = (uint32_t)kFCluster * ncols;
+
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kFWarps);
+        }
+        // every writer thread of every CTA of the cluster arrives once per layer
+        mbar_init(&actbar[0], (uint32_t)(kFCluster * 8 * M));
+        mbar_init(&actbar[1], (uint32_t)(kFCluster * 8 * M));
+        fence_mbar_init();
+    }
+    // operand buffers start at zero (padding columns and the plane 1-3 sums are never written)
+    for (int i = tid; i < HG * ncols * 4; i += kFThreads) reinterpret_cast<uint4*>(hq)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < HG * ncols; i += kFThreads) hxs[i] = hxe[i] = 0.f;
+    for (int i = tid; i < (int)(2 * aq_bytes / 16); i += kFThreads) reinterpret_cast<uint4*>(aq)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < (int)(2 * ax_words); i += kFThreads) axs[i] = axe[i] = 0.f;
+    for (int i = tid; i < ncols; i += kFThreads) cs[i] = (i >> 2) < M ? pow2f(-10 - 7 * (i & 3)) : 0.f;
+    __syncthreads();
+    cluster_sync_all();  // peers' barriers and buffers are ready before any remote store or arrival
+
+    if (warp == kFWarps) {
+        // ---- TMA producer: every layer's stages in order through the ring ------------------------------
+        pdl_launch_dependents();
+        if (lane == 0) {
+            int slot = 0, q = 0;
+            uint32_t wrap = 0u;
+            bool ok = true;
+            for (int L = 0; L < NL && ok; ++L) {
+                const FusedLayerMaps& mp = a.lay[L];
+                for (int t = 0; t < per_layer; ++t) {
+                    if (q >= S && !thread_wait(&empty[slot], wrap ^ 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = ring + (size_t)slot * kFStage;
+                    if (t == 0) FUSED_PMARK(L, 12);
+                    if (t == per_layer - 1) FUSED_PMARK(L, 13);
+                    if (t < gu_st) {  // gate rows 64c.. at rows 0-63 of the stage, up rows at 64-127
+                        const int gs = 4 * t, y = 64 * c;
+                        mbar_arrive_expect_tx(&full[slot], kFStage);
+                        tma_load_2d(st, &mp.g, gs * 8, y, &full[slot]);
+                        tma_load_2d(st + kFPacked, &mp.gs, gs & ~7, y, &full[slot]);
+                        tma_load_2d(st + kFPacked + kFSb, &mp.gb, gs & ~7, y, &full[slot]);
+                        tma_load_2d(st + 64 * 128, &mp.u, gs * 8, y, &full[slot]);
+                        tma_load_2d(st + kFPacked + 64 * 16, &mp.us, gs & ~7, y, &full[slot]);
+                        tma_load_2d(st + kFPacked + kFSb + 64 * 16, &mp.ub, gs & ~7, y, &full[slot]);
+                    } else {  // down_proj rows rd0 + h RB .., groups 8 cj + 4 s ..
+                        const int d = t - gu_st, h = d >> 1, s = d & 1;
+                        const int gs = 8 * cj + 4 * s, y = rd0 + h * RB;
+                        mbar_arrive_expect_tx(&full[slot], (uint32_t)RB * 160u);
+                        tma_load_2d(st, &mp.d, gs * 8, y, &full[slot]);
+                        tma_load_2d(st + kFPacked, &mp.ds, gs & ~7, y, &full[slot]);
+                        tma_load_2d(st + kFPacked + kFSb, &mp.db, gs & ~7, y, &full[slot]);
+                    }
+                    ++q;
+                    if (++slot == S) {
+                        slot = 0;
+                        wrap ^= 1u;
+                    }
+                }
+            }
+            // every issued stage has landed before the CTA may leave
+            for (int r = std::max(0, q - S); r < q; ++r) drain_wait(&full[r % S], (uint32_t)((r / S) & 1));
+        }
+        __syncwarp();
+    } else {
+        // ---- consumers ---------------------------------------------------------------------------------
+        pdl_wait();  // h0 and the cleared counter come from earlier kernels
+        pdl_launch_dependents();
+        const int units = H / 8;
+        const bool has_unit = tid < units;  // thread t holds elements 8t..8t+7 of every row
+        const int g = lane >> 2, tq = lane & 3;
+        zero_slice(a.acc + MH, MH, c, G, tid);
+        zero_slice(a.acc + 2 * MH, MH, c, G, tid);
+        cons_bar();
+        if (tid == 0) red_release_add(a.sync, 1u);  // start arrival: acc_1, acc_2 cleared
+        int slot = 0;
+        uint32_t fpar = 0u;
+        for (int L = 0; L < NL; ++L) {
+            const int par = L & 1;
+            uint4 nw = make_uint4(0, 0, 0, 0);
+            if (has_unit) nw = *reinterpret_cast<const uint4*>(a.norm_w[L] + 8 * tid);
+            if (L > 0 && tid == 0 && !*abort) grid_wait(a.sync, (unsigned)(L + 1) * (unsigned)G, a.wait_cycles, abort);
+            if (cons_bar_or(*abort != 0)) break;
+            FUSED_MARK(L, 0);
+            if (L > 0) zero_slice(a.acc + (size_t)((L + 2) % 3) * MH, MH, c, G, tid);
+            const unsigned long long* accL = a.acc + (size_t)(L % 3) * MH;
+            unsigned long long* accN = a.acc + (size_t)((L + 1) % 3) * MH;
+
+            // ---- h_L -> rms_norm -> s8 planes (per-group exponents) ----------------------------------
+            float v[MS][8];
+#pragma unroll
+            for (int m = 0; m < MS; ++m) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[m][j] = 0.f;
+                if (m < M && has_unit) {
+                    if (L == 0) load8(a.h0, kBF16, (int64_t)m * H + 8 * tid, v[m]);
+                    else load_fix8(accL + (size_t)m * H + 8 * tid, v[m]);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MS; ++m) {
+                if (m < M) {
+                    float s = has_unit ? unit_ssq(v[m], L == 0 ? kBF16 : kF32) : 0.f;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+                    if (lane == 0) red[warp * MS + m] = s;
+                }
+            }
+            FUSED_MARK(L, 10);
+            cons_bar();
+            if (tid < M) {
+                float s = 0.f;
+                for (int w = 0; w < kFWarps; ++w) s = __fadd_rn(s, red[w * MS + tid]);
+                float var;
+                if (L == 0)  // bf16 h0: MLX evaluates mean(square(x)) in bf16
+                    var = bf16_round(__fmul_rn(bf16_round(s), bf16_round((float)(1.0 / (double)H))));
+                else
+                    var = __fmul_rn(s, (float)(1.0 / (double)H));
+                rf[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+            }
+            cons_bar();
+            FUSED_MARK(L, 11);
+            if (has_unit) {
+                const int grp = tid >> 3, u8 = tid & 7;
+                const bool resid_rows = cj == 0 && 8 * tid >= rd0 && 8 * tid < rd0 + RD;
+#pragma unroll
+                for (int m = 0; m < MS; ++m) {
+                    if (m < M) {
+                        if (resid_rows) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) res[(8 * tid - rd0 + j) * MS + m] = v[m][j];
+                        }
+                        norm8(v[m], nw, rf[m]);
+                        float amx = 0.f, sm = 0.f;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            amx = fmaxf(amx, fabsf(v[m][j]));
+                            sm = __fadd_rn(sm, v[m][j]);
+                        }
+                        unsigned bits = __float_as_uint(amx);
+#pragma unroll
+                        for (int o = 1; o < 8; o <<= 1) {
+                            bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+                            sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                        }
+                        const int e = row_exp(bits);
+                        uint32_t b[4][2];
+                        planes8(v[m], e, b);
+#pragma unroll
+                        for (int p = 0; p < 4; ++p)
+                            *reinterpret_cast<uint2*>(hq + ((size_t)(grp * ncols + 4 * m + p) * 64 + 8 * u8)) =
+                                make_uint2(b[p][0], b[p][1]);
+                        if (u8 == 0) {
+                            hxs[grp * ncols + 4 * m] = __fmul_rn(sm, 64.0f);
+                            hxe[grp * ncols + 4 * m] = pow2f(e);
+                        }
+                    }
+                }
+            }
+            cons_bar();
+            FUSED_MARK(L, 1);
+
+            // ---- gate / up rows of the CTA's 64 features over all of hidden -----------------------------
+            const I8X txh{hq, hxs, cs, nullptr, nullptr, nullptr, hxe};
+            float y[NTN][4], yb[NTN][2];
+#pragma unroll
+            for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
+            bool wok = true;
+            for (int t = 0; t < gu_st; ++t) {
+                if (wok) wok = warp_wait(&full[slot], fpar, abort);
+                if (t == 0) FUSED_MARK(L, 6);
+                if (t == gu_st - 1) FUSED_MARK(L, 8);
+                if (wok) {
+                    i8_stage<NTN, kFRows, kFChain>(ring + (size_t)slot * kFStage, ((4 * t) & 7) * 2, 4 * t, txh, warp,
+                                                   lane, y, yb);
+#pragma unroll
+                    for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
+                        hold_regs(y[j]);
+                        hold_regs(yb[j]);
+                    }
+                }
+                __syncwarp();
+                if (wok && lane == 0) mbar_arrive(&empty[slot]);
+                if (++slot == S) {
+                    slot = 0;
+                    fpar ^= 1u;
+                }
+            }
+            if (wok) {
+                const int r0 = 16 * warp + g;
+#pragma unroll
+                for (int j = 0; j < NTN; ++j) {
+                    const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
+                    const float2 pp = i8_combine(y[j], yb[j], cv, tq);
+                    const int m = 2 * j + (tq >> 1);
+                    if ((tq & 1) == 0 && m < M) {
+                        out[r0 * MS + m] = pp.x;
+                        out[(r0 + 8) * MS + m] = pp.y;
+                    }
+                }
+            }
+            FUSED_MARK(L, 2);
+            if (cons_bar_or(*abort != 0)) break;
+
+            // ---- SwiGLU -> activation planes into every CTA of the cluster -----------------------------
+            uint8_t* aqp = aq + (size_t)par * aq_bytes;
+            float* axsp = axs + (size_t)par * ax_words;
+            float* axep = axe + (size_t)par * ax_words;
+            if (tid < 64) {  // thread 8 m + u: features 8u..8u+7 of row m (whole warps shuffle)
+                const int m = tid >> 3, u = tid & 7;
+                const bool live = m < M;
+                float av[8];
+                float amx = 0.f, sm = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    av[j] = 0.f;
+                    if (live) {
+                        const float gv = out[(8 * u + j) * MS + m], uv = out[(64 + 8 * u + j) * MS + m];
+                        const float sg = 1.0f / (1.0f + expf(-gv));
+                        av[j] = (sg * gv) * uv;
+                    }
+                    amx = fmaxf(amx, fabsf(av[j]));
+                    sm = __fadd_rn(sm, av[j]);
+                }
+                unsigned bits = __float_as_uint(amx);
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+                    sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                }
+                if (live) {
+                    const int e = row_exp(bits);
+                    uint32_t b[4][2];
+                    planes8(av, e, b);
+                    const uint32_t qoff = (uint32_t)((crank * ncols + 4 * m) * 64 + 8 * u);
+                    const uint32_t xoff = (uint32_t)(crank * ncols + 4 * m) * 4u;
+                    const uint32_t lq = smem_u32(aqp) + qoff, lxs = smem_u32(axsp) + xoff, lxe = smem_u32(axep) + xoff;
+                    const uint32_t lbar = smem_u32(&actbar[par]);
+                    const float xsv = __fmul_rn(sm, 64.0f), xev = pow2f(e);
+                    // every store first, one fence, then the arrivals
+#pragma unroll
+                    for (uint32_t r = 0; r < (uint32_t)kFCluster; ++r) {
+                        const uint32_t dq = mapa_u32(lq, r);
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) st_cluster_v2(dq + 64u * p, b[p][0], b[p][1]);
+                        if (u == 0) {
+                            st_cluster_f(mapa_u32(lxs, r), xsv);
+                            st_cluster_f(mapa_u32(lxe, r), xev);
+                        }
+                    }
+                    fence_acq_rel_cluster();
+#pragma unroll
+                    for (uint32_t r = 0; r < (uint32_t)kFCluster; ++r) mbar_arrive_cluster_relaxed(mapa_u32(lbar, r));
+                }
+            }
+            FUSED_MARK(L, 3);
+            if (L == 0 && tid == 0 && !*abort) grid_wait(a.sync, (unsigned)G, a.wait_cycles, abort);  // acc_1 cleared
+            wok = warp_wait_cluster(&actbar[par], (uint32_t)((L >> 1) & 1), abort, a.sync + 1, a.wait_cycles);
+            if (cons_bar_or(!wok || *abort != 0)) break;
+            FUSED_MARK(L, 4);
+
+            // ---- down_proj rows of this CTA x the cluster's 512 features -> fixed-point partials --------
+            const I8X txa{aqp, axsp, cs, nullptr, nullptr, nullptr, axep};
+            const bool rows_here = 16 * warp < RB;
+            for (int h = 0; h < nhalf; ++h) {
+#pragma unroll
+                for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
+                for (int s = 0; s < 2; ++s) {
+                    if (wok) wok = warp_wait(&full[slot], fpar, abort);
+                    if (h == 0 && s == 0) FUSED_MARK(L, 7);
+                    if (h == nhalf - 1 && s == 1) FUSED_MARK(L, 9);
+                    if (wok && rows_here) {
+                        i8_stage<NTN, kFRows, kFChain>(ring + (size_t)slot * kFStage, 8 * s, 4 * s, txa, warp, lane, y,
+                                                       yb);
+#pragma unroll
+                        for (int j = 0; j < NTN; ++j) {
+                            hold_regs(y[j]);
+                            hold_regs(yb[j]);
+                        }
+                    }
+                    __syncwarp();
+                    if (wok && lane == 0) mbar_arrive(&empty[slot]);
+                    if (++slot == S) {
+                        slot = 0;
+                        fpar ^= 1u;
+                    }
+                }
+                if (wok && rows_here) {
+                    const int lr0 = h * RB + 16 * warp + g, lr1 = lr0 + 8;  // rows within this CTA's range
+#pragma unroll
+                    for (int j = 0; j < NTN; ++j) {
+                        const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
+                        const float2 pp = i8_combine(y[j], yb[j], cv, tq);
+                        const int m = 2 * j + (tq >> 1);
+                        if ((tq & 1) == 0 && m < M) {
+                            long long f0 = to_fix(pp.x), f1 = to_fix(pp.y);
+                            if (cj == 0) {
+                                f0 += to_fix(res[lr0 * MS + m]);
+                                f1 += to_fix(res[lr1 * MS + m]);
+                            }
+                            red_add_u64(accN + (size_t)m * H + rd0 + lr0, f0);
+                            red_add_u64(accN + (size_t)m * H + rd0 + lr1, f1);
+                        }
+                    }
+                }
+            }
+            FUSED_MARK(L, 5);
+            if (cons_bar_or(!wok || *abort != 0)) break;
+            if (tid == 0) red_release_add(a.sync, 1u);  // layer L's partials are in acc_{L+1}
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while a peer may still write into its shared memory
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+int fused_ntn(int64_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : 4); }
+
+uint32_t plan_fused(FusedArgs& a, int M, int H) {
+    const int ntn = fused_ntn(M), ncols = 8 * ntn, MS = 2 * ntn;
+    const int HG = H / kGroup, RD = H / kFCluster;
+    auto al = [](uint32_t v, uint32_t x) { return (v + x - 1) / x * x; };
+    for (int S = 12; S >= 3; --S) {
+        uint32_t off = 0;
+        a.off_bar = off;
+        off += al((2u * S + 2u) * 8u, 128);
+        a.off_misc = off;
+        off += al(64u + (uint32_t)(kFWarps + 1) * MS * 4u, 128);
+        a.off_hq = off;
+        off += (uint32_t)HG * ncols * 64;
+        a.off_hxs = off;
+        off += al((uint32_t)HG * ncols * 4, 128);
+        a.off_hxe = off;
+        off += al((uint32_t)HG * ncols * 4, 128);
+        a.off_cs = off;
+        off += al((uint32_t)ncols * 4, 128);
+        a.off_aq = off;
+        off += 2u * kFCluster * ncols * 64;
+        a.off_axs = off;
+        off += al(2u * kFCluster * ncols * 4, 128);
+        a.off_axe = off;
+        off += al(2u * kFCluster * ncols * 4, 128);
+        a.off_out = off;
+        off += al((uint32_t)kFRows * MS * 4, 128);
+        a.off_res = off;
+        off += al((uint32_t)RD * MS * 4, 128);
+        off = al(off, 1024);
+        a.off_ring = off;
+        off += (uint32_t)S * kFStage + 1024;  // + the alignment of the dynamic shared-memory base
+        if (off <= kFSmemLimit) {
+            a.S = S;
+            return off;
+        }
+    }
+    return 0;
+}
+
+template <int NTN>
+cudaError_t fused_config(int grid, uint32_t smem, bool pdl, cudaStream_t stream, cudaLaunchConfig_t& cfg,
+                         cudaLaunchAttribute (&attr)[2]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(fused_layers_kernel<NTN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kFThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = kFCluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaSuccess;
+}
+
+template <int NTN>
+cudaError_t fused_max_clusters(uint32_t smem, int* n) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    cudaError_t e = fused_config<NTN>(kFCluster, smem, false, nullptr, cfg, attr);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveClusters(n, fused_layers_kernel<NTN>, &cfg);
+}
+
+// Whether `grid` CTAs in clusters of 8 can all be resident at once on the current device (the layer
+// barriers need every CTA running).  Cached per device and activation width.
+bool fused_coresident(int ntn, int grid, uint32_t smem) {
+    static std::mutex mu;
+    static int cache[64][3];  // [device][ntn index]: 0 unknown, else max active clusters + 1
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const int ti = ntn == 1 ? 0 : (ntn == 2 ? 1 : 2);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!cache[dev][ti]) {
+        int n = 0;
+        const cudaError_t e = ntn == 1   ? fused_max_clusters<1>(smem, &n)
+                              : ntn == 2 ? fused_max_clusters<2>(smem, &n)
+                                         : fused_max_clusters<4>(smem, &n);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cache[dev][ti] = n + 1;
+    }
+    return (cache[dev][ti] - 1) * kFCluster >= grid;
+}
+
+}  // namespace
+
+size_t fused_acc_bytes(int64_t m, int64_t hidden) { return (size_t)3 * (size_t)m * (size_t)hidden * 8; }
+
+bool fused_supported(int64_t m, int64_t hidden, int64_t inter, int n_layers) {
+    if (m < 1 || m > kFusedMaxRows || n_layers < 1 || n_layers > kFusedMaxLayers) return false;
+    if (hidden != 512 && hidden != 1024 && hidden != 2048) return false;
+    if (inter % 512 != 0 || inter / kGroup > device_num_sms() || tmap_encode_fn() == nullptr) return false;
+    FusedArgs a;
+    const uint32_t smem = plan_fused(a, (int)m, (int)hidden);
+    return smem != 0 && fused_coresident(fused_ntn(m), (int)(inter / kGroup), smem);
+}
+
+cudaError_t launch_fused_layers(const FusedLaunch& F, cudaStream_t stream) {
+    static FusedArgs a;  // 28 KB: kept off the stack (the launch copies it)
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    a = FusedArgs{};
+    const int M = (int)F.m, H = (int)F.hidden;
+    const uint32_t smem = plan_fused(a, M, H);
+    if (!smem) return cudaErrorInvalidConfiguration;
+    const int RD = H / kFCluster, RB = std::min(RD, kFRows);
+    for (int l = 0; l < F.n_layers; ++l) {
+        const FusedLayer& Ly = F.layers[l];
+        FusedLayerMaps& mp = a.lay[l];
+        if (!encode_q4_maps(Ly.gate, 64, &mp.g, &mp.gs, &mp.gb) || !encode_q4_maps(Ly.up, 64, &mp.u, &mp.us, &mp.ub) ||
+            !encode_q4_maps(Ly.down, RB, &mp.d, &mp.ds, &mp.db))
+            return cudaErrorInvalidValue;
+        a.norm_w[l] = Ly.norm_w;
+    }
+    a.h0 = F.h0;
+    a.acc = F.acc;
+    a.sync = F.sync;
+    a.wait_cycles = F.wait_cycles;
+    a.M = M;
+    a.H = H;
+    a.n_layers = F.n_layers;
+    a.eps = F.eps;
+    const int grid = (int)(F.inter / kGroup);
+    const int ntn = fused_ntn(M);
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    cudaError_t e = ntn == 1   ? fused_config<1>(grid, smem, F.pdl, stream, cfg, attr)
+                    : ntn == 2 ? fused_config<2>(grid, smem, F.pdl, stream, cfg, attr)
+                               : fused_config<4>(grid, smem, F.pdl, stream, cfg, attr);
+    if (e != cudaSuccess) return e;
+    if (ntn == 1) return cudaLaunchKernelEx(&cfg, fused_layers_kernel<1>, a);
+    if (ntn == 2) return cudaLaunchKernelEx(&cfg, fused_layers_kernel<2>, a);
+    return cudaLaunchKernelEx(&cfg, fused_layers_kernel<4>, a);
+}
+
+int fused_device_error(bool clear) { return tu_device_error(clear); }
+
+}  // namespace marlin

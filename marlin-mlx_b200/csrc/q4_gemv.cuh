@@ -6,7 +6,8 @@
 
 namespace marlin {
 
-enum ActDtype : int { kBF16 = 0, kF32 = 1 };
+// kFix64 (internal): 64-bit fixed point, value * 2^32 (the one-kernel layer stack's h accumulator).
+enum ActDtype : int { kBF16 = 0, kF32 = 1, kFix64 = 2 };
 
 // Device view of a QuantizedTensor (MLX layout).
 struct Q4Mat {
@@ -122,6 +123,12 @@ struct LmHeadLaunch {
     bool pdl;
     bool has_xin;            // integer-MMA family only: hidden state taken from planes (see XPlanes)
     XPlanes xin;
+    // integer-MMA family, x_dtype kFix64 only: block 0 also writes x as binary32 [m, k] (optional)
+    float* x_out;
+    // words cleared by block 0 once the previous kernel in the stream has completed (the one-kernel
+    // layer stack's barrier counter and abort word); null = none
+    unsigned* reset;
+    int n_reset;
     TpExchange tp;           // tp.tp > 1: the final keys are max-merged over the ranks (exchange)
 };
 

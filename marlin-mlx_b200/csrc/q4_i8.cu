@@ -55,47 +55,6 @@ constexpr uint32_t kI8StageBytes = kI8Packed + 2 * kI8Sb;  // 20 KB
 constexpr uint32_t kI8SmemLimit = 225 * 1024;
 constexpr uint32_t kI8TwoPerSm = 110 * 1024;          // two CTAs per SM (PDL overlap of neighbours)
 
-// ------------------------------------------------------------------------------------------------
-// one stage (4 groups) of one warp's 16 rows: y[j][0..1] row g, y[j][2..3] row g+8, columns
-// 8j + 2t + {0, 1} (lane = 4g + t).  A stage of ROWS rows holds the packed lines [ROWS][128 B],
-// then the scales [ROWS][8 groups] and the biases [ROWS][8 groups].
-// ------------------------------------------------------------------------------------------------
-template <int NTN, int ROWS = kI8Rows>
-__device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int warp, int lane,
-                                         float (&y)[NTN][4], float (&yb)[NTN][2]) {
-    constexpr int ncols = 8 * NTN;  // activation columns (compile-time, so plane addresses fold)
-    // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
-    const int g = lane >> 2, tq = lane & 3;
-    const int r0 = 16 * warp + g, r1 = r0 + 8;
-    const uint8_t* sc = st + ROWS * 128;
-    const uint8_t* bi = sc + ROWS * 16;
-    const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
-    const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
-    const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
-    const uint2 b1 = *reinterpret_cast<const uint2*>(bi + r1 * 16 + so);
-    uint2 wa[4], wb[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {  // the group's 32 bytes are units 2q, 2q+1 of the swizzled line
-        const uint32_t off = (uint32_t)((((2 * q + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
-        wa[q] = *reinterpret_cast<const uint2*>(st + r0 * 128 + off);
-        wb[q] = *reinterpret_cast<const uint2*>(st + r1 * 128 + off);
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float sr0 = sel_bf16(s0, q), sr1 = sel_bf16(s1, q), br0 = sel_bf16(b0, q), br1 = sel_bf16(b1, q);
-        const int gl = gl0 + q;
-#pragma unroll
-        for (int j = 0; j < NTN; ++j) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
-            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);  // plane-0 column of the lane's row
-            if constexpr (NTN >= 2)
-                i8_group_chained(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
-            else
-                i8_group(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
-        }
-    }
-}
-
 // Issue the TMA copies of one stage: groups [gs, gs + 4) of rows [row0, row0 + rows) of one matrix
 // (rows = 128, or 64 per matrix for the gate/up pair with row offset ro).
 __device__ __forceinline__ void i8_issue(uint8_t* st, const CUtensorMap* tw, const CUtensorMap* ts,
@@ -583,6 +542,14 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
     __syncthreads();
     pdl_wait();
     pdl_launch_dependents();
+    if (blockIdx.x == 0) {
+        if (L.reset && tid < L.n_reset) L.reset[tid] = 0u;
+        if (L.x_out && L.x_dtype == kFix64) {
+            const unsigned long long* xf = static_cast<const unsigned long long*>(L.x);
+            for (int i = tid; i < M * (int)L.w.k; i += blockDim.x)
+                L.x_out[i] = __ll2float_rn((long long)__ldcg(xf + i)) * 2.3283064365386963e-10f;
+        }
+    }
     uint64_t* xbar = full + 2 * S;  // planes copied in (has_xin)
     if (L.has_xin) {
         if (tid == W * 32) copy_planes_in(L.xin, 0, G, ncols, tx, xbar);

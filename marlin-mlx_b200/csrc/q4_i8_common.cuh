@@ -328,5 +328,47 @@ __device__ __forceinline__ float sel_bf16(uint2 v, int q) {
     return __uint_as_float((q & 1) ? (w & 0xffff0000u) : (w << 16));
 }
 
+// ------------------------------------------------------------------------------------------------
+// one stage (4 groups) of one warp's 16 rows: y[j][0..1] row g, y[j][2..3] row g+8, columns
+// 8j + 2t + {0, 1} (lane = 4g + t).  A stage of ROWS rows holds the packed lines [ROWS][128 B],
+// then the scales [ROWS][8 groups] and the biases [ROWS][8 groups].
+// ------------------------------------------------------------------------------------------------
+template <int NTN, int ROWS = 128, bool CHAIN = (NTN >= 2)>
+__device__ __forceinline__ void i8_stage(const uint8_t* st, int so, int gl0, const I8X& t, int warp, int lane,
+                                         float (&y)[NTN][4], float (&yb)[NTN][2]) {
+    constexpr int ncols = 8 * NTN;  // activation columns (compile-time, so plane addresses fold)
+    // plain loads (not volatile asm) so the compiler can hoist and interleave them across groups
+    const int g = lane >> 2, tq = lane & 3;
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    const uint8_t* sc = st + ROWS * 128;
+    const uint8_t* bi = sc + ROWS * 16;
+    const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
+    const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
+    const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
+    const uint2 b1 = *reinterpret_cast<const uint2*>(bi + r1 * 16 + so);
+    uint2 wa[4], wb[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // the group's 32 bytes are units 2q, 2q+1 of the swizzled line
+        const uint32_t off = (uint32_t)((((2 * q + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
+        wa[q] = *reinterpret_cast<const uint2*>(st + r0 * 128 + off);
+        wb[q] = *reinterpret_cast<const uint2*>(st + r1 * 128 + off);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float sr0 = sel_bf16(s0, q), sr1 = sel_bf16(s1, q), br0 = sel_bf16(b0, q), br1 = sel_bf16(b1, q);
+        const int gl = gl0 + q;
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
+            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);  // plane-0 column of the lane's row
+            if constexpr (CHAIN)
+                i8_group_chained(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+            else
+                i8_group(wa[q], wb[q], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+        }
+    }
+}
+
+
 }  // namespace
 }  // namespace marlin

@@ -27,9 +27,22 @@ struct XGeom {
     int M, P, M_eff, XRS, GC;
 };
 
+// Eight consecutive 64-bit fixed-point values (value * 2^32, two's complement, as the one-kernel
+// layer stack accumulates h) as binary32, read from L2 (the words were written by atomics).
+__device__ __forceinline__ void load_fix8(const unsigned long long* p, float v[8]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const ulonglong2 q = __ldcg(reinterpret_cast<const ulonglong2*>(p) + k);
+        v[2 * k] = __ll2float_rn((long long)q.x) * 2.3283064365386963e-10f;
+        v[2 * k + 1] = __ll2float_rn((long long)q.y) * 2.3283064365386963e-10f;
+    }
+}
+
 // Eight consecutive activations starting at element i (i % 8 == 0), as binary32.
 __device__ __forceinline__ void load8(const void* x, int dtype, int64_t i, float v[8]) {
-    if (dtype == kBF16) {
+    if (dtype == kFix64) {
+        load_fix8(static_cast<const unsigned long long*>(x) + i, v);
+    } else if (dtype == kBF16) {
         const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + i);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll

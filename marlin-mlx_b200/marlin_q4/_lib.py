@@ -14,6 +14,7 @@ OK = 0
 ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = -1, -2, -3, -4, -5, -6
 BF16, F32 = 0, 1
 PATH_I8MMA, PATH_BF16MMA = 0, 2
+STEP_FUSED, STEP_LAYERS = 0, 1
 
 # Every symbol include/marlin_q4.h declares, with its ctypes signature (restype, argtypes).
 _vp, _i64, _i32, _f32, _sz, _u64 = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float,
@@ -42,6 +43,7 @@ SIGNATURES = {
     "marlin_q4_set_pdl": (None, [ctypes.c_int]),
     "marlin_q4_set_wait_limit_cycles": (None, [_u64]),
     "marlin_q4_set_decode_path": (ctypes.c_int, [ctypes.c_int]),
+    "marlin_q4_set_step_kernels": (ctypes.c_int, [ctypes.c_int]),
     "marlin_q4_quantize": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     "marlin_q4_matmul": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),
     "marlin_q4_matmul_f32": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),

@@ -333,3 +333,12 @@ def set_decode_path(path: str) -> None:
     """Select the decode kernel family: "i8" (integer MMAs, default: the decode step on the cluster
     K-split kernels with operand planes handed between them) or "bf16" (mma.sync)."""
     check(_lib.load().marlin_q4_set_decode_path(DECODE_PATHS[path]), "marlin_q4_set_decode_path")
+
+
+STEP_KERNELS = {"fused": _lib.STEP_FUSED, "layers": _lib.STEP_LAYERS}
+
+
+def set_step_kernels(which: str) -> None:
+    """Select the kernels of the decode step's MLP layers: "fused" (default: all layers in one
+    persistent kernel) or "layers" (two cluster split-K kernels per layer)."""
+    check(_lib.load().marlin_q4_set_step_kernels(STEP_KERNELS[which]), "marlin_q4_set_step_kernels")

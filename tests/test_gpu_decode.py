@@ -1,9 +1,9 @@
 """GPU parity: the full Q4 decode stack (config 5) — 24 x [RMSNorm(1+w) -> Q4 MLP -> residual] ->
 final RMSNorm -> Q4 lm_head -> argmax — against the CPU oracle, fed the GPU-quantized weights.
 
-The step runs the integer-MMA kernels that split K over clusters, with the activations handed
-between them as operand planes (above 8 rows in 8-row chunks); the bf16 mma.sync family's
-composition of single-op kernels is checked against it."""
+The step runs its MLP layers as one persistent kernel (above 8 rows in 8-row chunks); the per-layer
+integer-MMA kernels that split K over clusters and the bf16 mma.sync family's composition of
+single-op kernels are checked against it."""
 import numpy as np
 import pytest
 import torch
@@ -45,6 +45,27 @@ def test_decode_step_matches_oracle(oracle, model, m):
     # deterministic across calls
     ids2, _, h2 = step(h0)
     assert torch.equal(ids2, ids) and torch.equal(h2, h)
+
+
+@pytest.mark.parametrize("m", [1, 5, 8, 20])
+def test_layer_kernels_step_matches_oracle(oracle, model, m):
+    """The per-layer kernels (two cluster split-K launches per layer) against the oracle and against
+    the one-kernel layer stack (the default)."""
+    layers, hl, lm, hlm, fn, hfn = model
+    h0 = mq.synth_bf16((m, H), 3400 + m, 0.0, 1.0)
+    ids_f, _, h_f = (t.clone() for t in mq.DecodeStep(layers, fn, lm, m)(h0))
+    mq.set_step_kernels("layers")
+    try:
+        ids, _, h = mq.DecodeStep(layers, fn, lm, m)(h0)
+        torch.cuda.synchronize()
+    finally:
+        mq.set_step_kernels("fused")
+    rids, _, rh = oracle.decode_step(u16(h0), hl, hfn, hlm)
+    assert max_rel_row_err(f32(h), rh) < 1e-3
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    assert max_rel_row_err(f32(h_f), f32(h).astype(np.float64)) < 1e-5
+    assert torch.equal(ids_f, ids)
+    assert mq.device_error() == 0
 
 
 def test_decode_step_in_cuda_graph(model):
