@@ -12,23 +12,30 @@
 //
 // Work split (inter = 64 G features, G CTAs, thread-block clusters of 8):
 //   CTA c owns intermediate features [64 c, 64 c + 64): it computes their gate and up rows over all
-//   of `hidden` from the exact s8 planes of rms_norm(h) (the integer-MMA arithmetic of q4_i8.cu),
-//   then SwiGLU, and writes the 64 activations as s8 planes into the shared memory of all eight
-//   CTAs of its cluster (distributed shared memory, one mbarrier per CTA counts the arrivals).
+//   of `hidden` from the exact s8 planes of h * (1 + w) (the integer-MMA arithmetic of q4_i8.cu;
+//   the RMSNorm factor multiplies the row sums afterwards), then SwiGLU, and copies the 64
+//   activations as s8 planes into the shared memory of the other seven CTAs of its cluster (bulk
+//   copies over distributed shared memory, counted in bytes on one mbarrier per CTA).
 //   CTA rank i of cluster j then multiplies down_proj rows [i hidden/8, (i+1) hidden/8) by the
 //   cluster's 512 features (columns [512 j, 512 j + 512): one 16-byte scale box per row, fully
-//   used) and adds the partial rows into a 64-bit fixed-point accumulator of h (value * 2^32) with
-//   integer atomics: the sum does not depend on their order, so the result is deterministic.
-//   Cluster 0 also adds the residual h.  Every CTA then bumps one arrival counter; the next layer
-//   starts when it reaches (layer + 2) * G, and each CTA reads the whole new h from L2.
+//   used) and adds the partial rows into the accumulator of the next h with integer atomics.
 //
-// Accumulators rotate over three buffers (acc_l = acc[l % 3]); acc_{l+2} is zeroed, one slice per
-// CTA, after the barrier that starts layer l (everyone has read acc_{l-1} by then), and acc_1,
-// acc_2 at kernel start behind a start arrival.  The counter is cleared by the next kernel.
+// Counted fixed point (load_fix8): every accumulator word is (value * 2^27) << 5 plus a 5-bit count
+// of the contributions added to it, each atomic add bringing +1.  The sum does not depend on the
+// order of the adds (deterministic), and a word is complete when its count reaches the known number
+// of contributions, so the next layer waits on the words themselves: no arrival counter, no
+// release fence and no second round trip to read the data.  Cluster 0 also adds the residual h.
 //
-// Warp roles: warps 0-7 compute; warp 8 is the TMA producer, which walks every layer's stages
+// Accumulators rotate over three buffers (acc_l = acc[l % 3]).  acc_{l+2} is zeroed, one slice per
+// CTA, during layer l (complete words of acc_l prove that every CTA has read acc_{l-1}), followed
+// by a fence before the CTA's own adds of layer l; acc_1 and acc_2 are zeroed at kernel start
+// behind one arrival counter, which the next kernel clears.
+//
+// Warp roles: W = 8 or 16 consumer warps (16 at one or two activation rows: two warps share each
+// 16-row tile, each taking two of a stage's four groups, which doubles the warps that hide the MMA
+// and shared-memory latencies); the last warp is the TMA producer, which walks every layer's stages
 // (gate/up: 64 + 64 rows x 4 groups; down_proj: up to 128 rows x 4 groups; 20 KB each) through one
-// ring, so the next layer's weights stream while the consumers wait at the layer barrier.
+// ring, so the next layer's weights stream while the consumers wait for the current h.
 //
 // Every wait is bounded (SM clock cycles): one that runs out records a device error, raises the
 // CTA's abort flag and the grid's abort word, and every other wait then returns at once; the CTAs
@@ -56,8 +63,6 @@
 namespace marlin {
 namespace {
 
-constexpr int kFWarps = 8;                          // consumer warps
-constexpr int kFThreads = (kFWarps + 1) * 32;       // + the TMA producer warp
 constexpr int kFCluster = 8;
 constexpr int kFRows = 128;                         // rows per ring stage
 constexpr uint32_t kFPacked = kFRows * 128;         // packed lines of one stage (4 groups per row)
@@ -65,10 +70,9 @@ constexpr uint32_t kFSb = kFRows * 16;              // scale (or bias) box: 8 gr
 constexpr uint32_t kFStage = kFPacked + 2 * kFSb;   // 20 KB
 constexpr uint32_t kFSmemLimit = 226 * 1024;
 constexpr int kFBar = 1;                            // named barrier of the consumer warps
-#ifndef FUSED_CHAIN
-#define FUSED_CHAIN 1
-#endif
-constexpr bool kFChain = FUSED_CHAIN != 0;          // chained even/odd MMAs and packed fold at every width
+constexpr int kFWriteBar = 2;                       // named barrier of the 64 SwiGLU writer threads
+
+__host__ __device__ constexpr int fused_threads(int W) { return (W + 1) * 32; }
 
 struct FusedLayerMaps {
     CUtensorMap g, gs, gb, u, us, ub, d, ds, db;  // gate/up boxes of 64 rows, down_proj boxes of RB rows
@@ -87,13 +91,15 @@ struct FusedArgs {
 };
 static_assert(sizeof(FusedArgs) <= 32000, "kernel parameters above the 32 KB limit");
 
-// ---- fixed point, global synchronisation -------------------------------------------------------------
-constexpr float kFixScale = 4294967296.0f;  // 2^32
+// ---- counted fixed point, global synchronisation ------------------------------------------------------
+// One contribution: round(v * 2^27) in the value field, +1 in the count field.
+__device__ __forceinline__ unsigned long long fix_word(long long f) {
+    return ((unsigned long long)f << kFixCountBits) + 1ull;
+}
+__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * 134217728.0f); }
 
-__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * kFixScale); }
-
-__device__ __forceinline__ void red_add_u64(unsigned long long* p, long long v) {
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)v) : "memory");
+__device__ __forceinline__ void red_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -103,10 +109,21 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ ulonglong2 ld_acquire_v2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.acquire.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
-// Thread 0 of the consumers: wait until the arrival counter reaches `target`, bounded; on a timeout
-// or a raised grid abort word, raise the CTA's abort flag and return.
+// Gives up a wait: records the timeout once, raises the grid's abort word and the CTA's flag.
+__device__ __forceinline__ void give_up(unsigned* gabort, volatile int* abort) {
+    record_device_error(kDevErrMbarTimeout);
+    atomicExch(gabort, 1u);
+    *abort = 1;
+}
+
+// Thread 0 of the consumers: wait until the start counter reaches `target`, bounded.
 __device__ void grid_wait(unsigned* sync, unsigned target, unsigned long long limit, volatile int* abort) {
     const unsigned long long t0 = cycles_now();
     for (uint32_t it = 0;; ++it) {
@@ -120,17 +137,52 @@ __device__ void grid_wait(unsigned* sync, unsigned target, unsigned long long li
                 return;
             }
             if (cycles_now() - t0 > limit) {
-                record_device_error(kDevErrMbarTimeout);
-                atomicExch(sync + 1, 1u);
-                *abort = 1;
+                give_up(sync + 1, abort);
                 return;
             }
         }
     }
 }
 
+// Eight accumulator words of h, waited for until each holds `target` contributions (bounded; gives
+// up on a timeout or an abort), as binary32.
+__device__ void poll_fix8(const unsigned long long* p, unsigned target, float (&v)[8], unsigned* gabort,
+                          unsigned long long limit, volatile int* abort) {
+    ulonglong2 q[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) q[k] = ld_acquire_v2(p + 2 * k);
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        bool done = true;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            done = done && ((unsigned)q[k].x & 31u) == target && ((unsigned)q[k].y & 31u) == target;
+        if (done) break;
+        if (it == 0) {
+            t0 = cycles_now();
+        } else if ((it & 7u) == 0u) {
+            if (*abort || ld_relaxed(gabort)) {
+                *abort = 1;
+                break;
+            }
+            if (cycles_now() - t0 > limit) {
+                give_up(gabort, abort);
+                break;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = ld_acquire_v2(p + 2 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[2 * k] = fix_value(q[k].x);
+        v[2 * k + 1] = fix_value(q[k].y);
+    }
+}
+
 // Named barrier of the consumer warps that also returns whether any of them passed `p` true: the
 // abort decision is taken once per phase, identically in every consumer thread.
+template <int W>
 __device__ __forceinline__ bool cons_bar_or(bool p) {
     uint32_t r;
     asm volatile(
@@ -139,11 +191,14 @@ __device__ __forceinline__ bool cons_bar_or(bool p) {
         "bar.red.or.pred po, %2, %3, pi;\n\t"
         "selp.u32 %0, 1, 0, po;\n\t}"
         : "=r"(r)
-        : "r"((uint32_t)p), "r"(kFBar), "r"(kFWarps * 32)
+        : "r"((uint32_t)p), "r"(kFBar), "r"(W * 32)
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void cons_bar() { asm volatile("bar.sync %0, %1;" ::"r"(kFBar), "r"(kFWarps * 32) : "memory"); }
+template <int W>
+__device__ __forceinline__ void cons_bar() {
+    asm volatile("bar.sync %0, %1;" ::"r"(kFBar), "r"(W * 32) : "memory");
+}
 
 // ---- distributed shared memory ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t mapa_u32(uint32_t local, uint32_t rank) {
@@ -151,19 +206,13 @@ __device__ __forceinline__ uint32_t mapa_u32(uint32_t local, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t x, uint32_t y) {
-    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(x), "r"(y) : "memory");
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to the cluster address dst,
+// counted on the destination's mbarrier (cluster address bar).
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
-__device__ __forceinline__ void st_cluster_f(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-// Arrive on the mbarrier at cluster address `addr` without ordering: the caller has made its stores
-// visible with fence_acq_rel_cluster() first (one fence for all targets instead of a release per
-// arrival, each of which costs a round trip).
-__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t addr) {
-    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -177,7 +226,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 // Warp-wide bounded wait for the cluster's activation planes; gives up on a timeout, the CTA's abort
 // flag or the grid's abort word.
-__device__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, const unsigned* gabort,
+__device__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned* gabort,
                                   unsigned long long limit) {
     if (__all_sync(0xffffffffu, mbar_try_wait_cluster(bar, parity) ? 1 : 0)) return true;
     const unsigned long long t0 = cycles_now();
@@ -189,7 +238,7 @@ __device__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* 
                 if (*abort || ld_relaxed(gabort)) {
                     stop = 1;
                 } else if (cycles_now() - t0 > limit) {
-                    record_device_error(kDevErrMbarTimeout);
+                    give_up(gabort, abort);
                     stop = 1;
                 }
             }
@@ -201,26 +250,71 @@ __device__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* 
     }
 }
 
-// Zero this CTA's slice of an n-word accumulator (L2 only).
-__device__ __forceinline__ void zero_slice(unsigned long long* p, size_t n, int c, int G, int tid) {
+// Zero this CTA's slice of an n-word accumulator (L2 only) with `nt` threads; true if any stored.
+__device__ __forceinline__ bool zero_slice(unsigned long long* p, size_t n, int c, int G, int t, int nt) {
     const size_t b = n * (size_t)c / (size_t)G, e = n * (size_t)(c + 1) / (size_t)G;
-    for (size_t i = b + tid; i < e; i += kFWarps * 32) __stcg(p + i, 0ull);
+    for (size_t i = b + t; i < e; i += nt) __stcg(p + i, 0ull);
+    return b + t < e;
+}
+
+// One ring stage for a warp's 16-row tile rt, groups [q0, q0 + NQ) of the stage's four (see i8_stage
+// in q4_i8_common.cuh for the layout and the arithmetic).
+template <int NTN, int NQ, bool CHAIN>
+__device__ __forceinline__ void f_stage(const uint8_t* st, int so, int gl0, int q0, const I8X& t, int rt, int lane,
+                                        float (&y)[NTN][4], float (&yb)[NTN][2]) {
+    constexpr int ncols = 8 * NTN;
+    const int g = lane >> 2, tq = lane & 3;
+    const int r0 = 16 * rt + g, r1 = r0 + 8;
+    const uint8_t* sc = st + kFRows * 128;
+    const uint8_t* bi = sc + kFRows * 16;
+    const uint2 s0 = *reinterpret_cast<const uint2*>(sc + r0 * 16 + so);
+    const uint2 s1 = *reinterpret_cast<const uint2*>(sc + r1 * 16 + so);
+    const uint2 b0 = *reinterpret_cast<const uint2*>(bi + r0 * 16 + so);
+    const uint2 b1 = *reinterpret_cast<const uint2*>(bi + r1 * 16 + so);
+    uint2 wa[NQ], wb[NQ];
+#pragma unroll
+    for (int qq = 0; qq < NQ; ++qq) {
+        const int q = NQ == 4 ? qq : q0 + qq;
+        const uint32_t off = (uint32_t)((((2 * q + (tq >> 1)) ^ g) << 4) + 8 * (tq & 1));
+        wa[qq] = *reinterpret_cast<const uint2*>(st + r0 * 128 + off);
+        wb[qq] = *reinterpret_cast<const uint2*>(st + r1 * 128 + off);
+    }
+#pragma unroll
+    for (int qq = 0; qq < NQ; ++qq) {
+        const int q = NQ == 4 ? qq : q0 + qq;
+        const float sr0 = sel_bf16(s0, q), sr1 = sel_bf16(s1, q), br0 = sel_bf16(b0, q), br1 = sel_bf16(b1, q);
+        const int gl = gl0 + q;
+#pragma unroll
+        for (int j = 0; j < NTN; ++j) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
+            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);
+            if constexpr (CHAIN)
+                i8_group_chained(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+            else
+                i8_group(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------------------
-// the kernel
+// the kernel: NTN activation column tiles (2 rows each), W consumer warps
 // ------------------------------------------------------------------------------------------------
-template <int NTN>
-__global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid_constant__ FusedArgs a) {
+template <int NTN, int W>
+__global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const __grid_constant__ FusedArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align_smem_1024(smem_raw);
     constexpr int MS = 2 * NTN;     // activation rows per pass (2 per 8-column MMA tile)
     constexpr int ncols = 8 * NTN;  // MMA columns: 4 planes per row
+    constexpr int KP = W / 8;       // warps per 16-row tile (each takes 4 / KP groups of a stage)
+    constexpr int NQ = 4 / KP;
+    constexpr bool CHAIN = NTN >= 2;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rt = warp & 7, kp = warp >> 3;
     const int M = a.M, H = a.H, S = a.S, NL = a.n_layers;
     const int G = (int)gridDim.x, c = (int)blockIdx.x;
     const uint32_t crank = cluster_rank();
     const int cj = c / kFCluster;
+    const unsigned target = (unsigned)(KP * (G / kFCluster));  // contributions per accumulator word
     const int HG = H / kGroup;                 // 64-groups of h
     const int RD = H / kFCluster;              // down_proj rows of this CTA
     const int rd0 = (int)crank * RD;
@@ -234,41 +328,41 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
     uint64_t* empty = full + S;
     uint64_t* actbar = empty + S;  // [2]: activation planes of the cluster, by layer parity
     volatile int* abort = reinterpret_cast<volatile int*>(smem + a.off_misc);
-    float* red = reinterpret_cast<float*>(smem + a.off_misc + 64);  // [8 warps][MS] sums of squares
-    float* rf = red + kFWarps * MS;                                   // [MS] RMSNorm factors
-    uint8_t* hq = smem + a.off_hq;                                    // [HG][ncols][64] planes of rms_norm(h)
+    float* red = reinterpret_cast<float*>(smem + a.off_misc + 64);  // [W][MS] sums of squares
+    uint8_t* hq = smem + a.off_hq;                                    // [HG][ncols][64] planes of h (1 + w)
     float* hxs = reinterpret_cast<float*>(smem + a.off_hxs);
     float* hxe = reinterpret_cast<float*>(smem + a.off_hxe);
     float* cs = reinterpret_cast<float*>(smem + a.off_cs);
     uint8_t* aq = smem + a.off_aq;                                    // [2][8][ncols][64] act planes
     float* axs = reinterpret_cast<float*>(smem + a.off_axs);          // [2][8][ncols]
     float* axe = reinterpret_cast<float*>(smem + a.off_axe);
-    float* out = reinterpret_cast<float*>(smem + a.off_out);          // [128][MS] gate / up rows
+    float* out = reinterpret_cast<float*>(smem + a.off_out);          // [KP][128][MS] gate / up rows
     float* res = reinterpret_cast<float*>(smem + a.off_res);          // [RD][MS] residual rows
     uint8_t* ring = smem + a.off_ring;
     const uint32_t aq_bytes = (uint32_t)kFCluster * ncols * 64, ax_words = (uint32_t)kFCluster * ncols;
+    const uint32_t src_bytes = (uint32_t)ncols * (64 + 8);  // one CTA's slot: planes, sums, exponents
 
     if (tid == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kFWarps);
+            mbar_init(&empty[s], W);
         }
-        // every writer thread of every CTA of the cluster arrives once per layer
-        mbar_init(&actbar[0], (uint32_t)(kFCluster * 8 * M));
-        mbar_init(&actbar[1], (uint32_t)(kFCluster * 8 * M));
+        mbar_init(&actbar[0], 1);  // own arrival (with the expected bytes of the seven peers' copies)
+        mbar_init(&actbar[1], 1);
         fence_mbar_init();
     }
     // operand buffers start at zero (padding columns and the plane 1-3 sums are never written)
-    for (int i = tid; i < HG * ncols * 4; i += kFThreads) reinterpret_cast<uint4*>(hq)[i] = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < HG * ncols; i += kFThreads) hxs[i] = hxe[i] = 0.f;
-    for (int i = tid; i < (int)(2 * aq_bytes / 16); i += kFThreads) reinterpret_cast<uint4*>(aq)[i] = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < (int)(2 * ax_words); i += kFThreads) axs[i] = axe[i] = 0.f;
-    for (int i = tid; i < ncols; i += kFThreads) cs[i] = (i >> 2) < M ? pow2f(-10 - 7 * (i & 3)) : 0.f;
+    for (int i = tid; i < HG * ncols * 4; i += fused_threads(W)) reinterpret_cast<uint4*>(hq)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < HG * ncols; i += fused_threads(W)) hxs[i] = hxe[i] = 0.f;
+    for (int i = tid; i < (int)(2 * aq_bytes / 16); i += fused_threads(W))
+        reinterpret_cast<uint4*>(aq)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < (int)(2 * ax_words); i += fused_threads(W)) axs[i] = axe[i] = 0.f;
+    for (int i = tid; i < ncols; i += fused_threads(W)) cs[i] = (i >> 2) < M ? pow2f(-10 - 7 * (i & 3)) : 0.f;
     __syncthreads();
-    cluster_sync_all();  // peers' barriers and buffers are ready before any remote store or arrival
+    cluster_sync_all();  // peers' barriers and buffers are ready before any remote copy
 
-    if (warp == kFWarps) {
+    if (warp == W) {
         // ---- TMA producer: every layer's stages in order through the ring ------------------------------
         pdl_launch_dependents();
         if (lane == 0) {
@@ -320,9 +414,9 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
         const int units = H / 8;
         const bool has_unit = tid < units;  // thread t holds elements 8t..8t+7 of every row
         const int g = lane >> 2, tq = lane & 3;
-        zero_slice(a.acc + MH, MH, c, G, tid);
-        zero_slice(a.acc + 2 * MH, MH, c, G, tid);
-        cons_bar();
+        zero_slice(a.acc + MH, MH, c, G, tid, W * 32);
+        zero_slice(a.acc + 2 * MH, MH, c, G, tid, W * 32);
+        cons_bar<W>();
         if (tid == 0) red_release_add(a.sync, 1u);  // start arrival: acc_1, acc_2 cleared
         int slot = 0;
         uint32_t fpar = 0u;
@@ -330,14 +424,11 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
             const int par = L & 1;
             uint4 nw = make_uint4(0, 0, 0, 0);
             if (has_unit) nw = *reinterpret_cast<const uint4*>(a.norm_w[L] + 8 * tid);
-            if (L > 0 && tid == 0 && !*abort) grid_wait(a.sync, (unsigned)(L + 1) * (unsigned)G, a.wait_cycles, abort);
-            if (cons_bar_or(*abort != 0)) break;
-            FUSED_MARK(L, 0);
-            if (L > 0) zero_slice(a.acc + (size_t)((L + 2) % 3) * MH, MH, c, G, tid);
             const unsigned long long* accL = a.acc + (size_t)(L % 3) * MH;
             unsigned long long* accN = a.acc + (size_t)((L + 1) % 3) * MH;
+            FUSED_MARK(L, 0);
 
-            // ---- h_L -> rms_norm -> s8 planes (per-group exponents) ----------------------------------
+            // ---- h_L (complete words) -> planes of h (1 + w) with per-group exponents; sums of squares --
             float v[MS][8];
 #pragma unroll
             for (int m = 0; m < MS; ++m) {
@@ -345,46 +436,26 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                 for (int j = 0; j < 8; ++j) v[m][j] = 0.f;
                 if (m < M && has_unit) {
                     if (L == 0) load8(a.h0, kBF16, (int64_t)m * H + 8 * tid, v[m]);
-                    else load_fix8(accL + (size_t)m * H + 8 * tid, v[m]);
-                }
-            }
-#pragma unroll
-            for (int m = 0; m < MS; ++m) {
-                if (m < M) {
-                    float s = has_unit ? unit_ssq(v[m], L == 0 ? kBF16 : kF32) : 0.f;
-#pragma unroll
-                    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-                    if (lane == 0) red[warp * MS + m] = s;
+                    else poll_fix8(accL + (size_t)m * H + 8 * tid, target, v[m], a.sync + 1, a.wait_cycles, abort);
                 }
             }
             FUSED_MARK(L, 10);
-            cons_bar();
-            if (tid < M) {
-                float s = 0.f;
-                for (int w = 0; w < kFWarps; ++w) s = __fadd_rn(s, red[w * MS + tid]);
-                float var;
-                if (L == 0)  // bf16 h0: MLX evaluates mean(square(x)) in bf16
-                    var = bf16_round(__fmul_rn(bf16_round(s), bf16_round((float)(1.0 / (double)H))));
-                else
-                    var = __fmul_rn(s, (float)(1.0 / (double)H));
-                rf[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
-            }
-            cons_bar();
-            FUSED_MARK(L, 11);
             if (has_unit) {
                 const int grp = tid >> 3, u8 = tid & 7;
                 const bool resid_rows = cj == 0 && 8 * tid >= rd0 && 8 * tid < rd0 + RD;
 #pragma unroll
                 for (int m = 0; m < MS; ++m) {
                     if (m < M) {
+                        const float ssq = unit_ssq(v[m], L == 0 ? kBF16 : kF32);
                         if (resid_rows) {
 #pragma unroll
                             for (int j = 0; j < 8; ++j) res[(8 * tid - rd0 + j) * MS + m] = v[m][j];
                         }
-                        norm8(v[m], nw, rf[m]);
+                        const uint32_t w4[4] = {nw.x, nw.y, nw.z, nw.w};
                         float amx = 0.f, sm = 0.f;
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
+                            v[m][j] = __fmul_rn(v[m][j], __fadd_rn(1.0f, bf16_bits_to_f32((w4[j >> 1] >> (16 * (j & 1))) & 0xffffu)));
                             amx = fmaxf(amx, fabsf(v[m][j]));
                             sm = __fadd_rn(sm, v[m][j]);
                         }
@@ -405,11 +476,28 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                             hxs[grp * ncols + 4 * m] = __fmul_rn(sm, 64.0f);
                             hxe[grp * ncols + 4 * m] = pow2f(e);
                         }
+                        float sq = ssq;
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+                        if (lane == 0) red[warp * MS + m] = sq;
                     }
                 }
+            } else if (lane == 0) {
+#pragma unroll
+                for (int m = 0; m < MS; ++m) red[warp * MS + m] = 0.f;
             }
-            cons_bar();
+            if (cons_bar_or<W>(*abort != 0)) break;
             FUSED_MARK(L, 1);
+            // RMSNorm row factor of row `lane` (lanes < M): r = 1/sqrt(mean(h^2) + eps), warps summed in order
+            float rfl = 0.f;
+            if (lane < M) {
+                float s2 = 0.f;
+                for (int w = 0; w < W; ++w) s2 = __fadd_rn(s2, red[w * MS + lane]);
+                const float var = L == 0  // bf16 h0: MLX evaluates mean(square(x)) in bf16
+                                      ? bf16_round(__fmul_rn(bf16_round(s2), bf16_round((float)(1.0 / (double)H))))
+                                      : __fmul_rn(s2, (float)(1.0 / (double)H));
+                rfl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+            }
 
             // ---- gate / up rows of the CTA's 64 features over all of hidden -----------------------------
             const I8X txh{hq, hxs, cs, nullptr, nullptr, nullptr, hxe};
@@ -422,8 +510,8 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                 if (t == 0) FUSED_MARK(L, 6);
                 if (t == gu_st - 1) FUSED_MARK(L, 8);
                 if (wok) {
-                    i8_stage<NTN, kFRows, kFChain>(ring + (size_t)slot * kFStage, ((4 * t) & 7) * 2, 4 * t, txh, warp,
-                                                   lane, y, yb);
+                    f_stage<NTN, NQ, CHAIN>(ring + (size_t)slot * kFStage, ((4 * t) & 7) * 2, 4 * t, kp * NQ, txh, rt,
+                                            lane, y, yb);
 #pragma unroll
                     for (int j = 0; j < NTN; ++j) {  // the stage's data is consumed before release
                         hold_regs(y[j]);
@@ -437,23 +525,24 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                     fpar ^= 1u;
                 }
             }
-            if (wok) {
-                const int r0 = 16 * warp + g;
+            {
+                const int r0 = kp * kFRows + 16 * rt + g;
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
                     const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
                     const float2 pp = i8_combine(y[j], yb[j], cv, tq);
                     const int m = 2 * j + (tq >> 1);
+                    const float rfm = __shfl_sync(0xffffffffu, rfl, m & 31);
                     if ((tq & 1) == 0 && m < M) {
-                        out[r0 * MS + m] = pp.x;
-                        out[(r0 + 8) * MS + m] = pp.y;
+                        out[r0 * MS + m] = pp.x * rfm;
+                        out[(r0 + 8) * MS + m] = pp.y * rfm;
                     }
                 }
             }
             FUSED_MARK(L, 2);
-            if (cons_bar_or(*abort != 0)) break;
+            if (cons_bar_or<W>(*abort != 0)) break;
 
-            // ---- SwiGLU -> activation planes into every CTA of the cluster -----------------------------
+            // ---- SwiGLU -> activation planes, copied into every CTA of the cluster ----------------------
             uint8_t* aqp = aq + (size_t)par * aq_bytes;
             float* axsp = axs + (size_t)par * ax_words;
             float* axep = axe + (size_t)par * ax_words;
@@ -466,7 +555,12 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                 for (int j = 0; j < 8; ++j) {
                     av[j] = 0.f;
                     if (live) {
-                        const float gv = out[(8 * u + j) * MS + m], uv = out[(64 + 8 * u + j) * MS + m];
+                        float gv = 0.f, uv = 0.f;
+#pragma unroll
+                        for (int k = 0; k < KP; ++k) {
+                            gv += out[(k * kFRows + 8 * u + j) * MS + m];
+                            uv += out[(k * kFRows + 64 + 8 * u + j) * MS + m];
+                        }
                         const float sg = 1.0f / (1.0f + expf(-gv));
                         av[j] = (sg * gv) * uv;
                     }
@@ -483,36 +577,43 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                     const int e = row_exp(bits);
                     uint32_t b[4][2];
                     planes8(av, e, b);
-                    const uint32_t qoff = (uint32_t)((crank * ncols + 4 * m) * 64 + 8 * u);
-                    const uint32_t xoff = (uint32_t)(crank * ncols + 4 * m) * 4u;
-                    const uint32_t lq = smem_u32(aqp) + qoff, lxs = smem_u32(axsp) + xoff, lxe = smem_u32(axep) + xoff;
-                    const uint32_t lbar = smem_u32(&actbar[par]);
-                    const float xsv = __fmul_rn(sm, 64.0f), xev = pow2f(e);
-                    // every store first, one fence, then the arrivals
 #pragma unroll
-                    for (uint32_t r = 0; r < (uint32_t)kFCluster; ++r) {
-                        const uint32_t dq = mapa_u32(lq, r);
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) st_cluster_v2(dq + 64u * p, b[p][0], b[p][1]);
-                        if (u == 0) {
-                            st_cluster_f(mapa_u32(lxs, r), xsv);
-                            st_cluster_f(mapa_u32(lxe, r), xev);
-                        }
+                    for (int p = 0; p < 4; ++p)
+                        *reinterpret_cast<uint2*>(aqp + ((crank * ncols + 4 * m + p) * 64 + 8 * u)) =
+                            make_uint2(b[p][0], b[p][1]);
+                    if (u == 0) {
+                        axsp[crank * ncols + 4 * m] = __fmul_rn(sm, 64.0f);
+                        axep[crank * ncols + 4 * m] = pow2f(e);
                     }
-                    fence_acq_rel_cluster();
-#pragma unroll
-                    for (uint32_t r = 0; r < (uint32_t)kFCluster; ++r) mbar_arrive_cluster_relaxed(mapa_u32(lbar, r));
                 }
+                fence_proxy_async_smem();  // the slot is read by the bulk copies below
+                asm volatile("bar.sync %0, %1;" ::"r"(kFWriteBar), "r"(64) : "memory");
+                if (tid == 0) {
+                    const uint32_t lq = smem_u32(aqp) + crank * ncols * 64, lxs = smem_u32(axsp) + crank * ncols * 4,
+                                   lxe = smem_u32(axep) + crank * ncols * 4, lbar = smem_u32(&actbar[par]);
+                    for (uint32_t r = 1; r < (uint32_t)kFCluster; ++r) {
+                        const uint32_t dst = (crank + r) % kFCluster, rbar = mapa_u32(lbar, dst);
+                        bulk_s2cluster(mapa_u32(lq, dst), lq, (uint32_t)ncols * 64, rbar);
+                        bulk_s2cluster(mapa_u32(lxs, dst), lxs, (uint32_t)ncols * 4, rbar);
+                        bulk_s2cluster(mapa_u32(lxe, dst), lxe, (uint32_t)ncols * 4, rbar);
+                    }
+                    mbar_arrive_expect_tx(&actbar[par], (kFCluster - 1) * src_bytes);
+                }
+            } else if (L > 0) {
+                // idle during SwiGLU: clear this CTA's slice of acc_{L+2} (complete words of acc_L show that
+                // every CTA has read acc_{L-1}, which it reuses); the fence orders the zeros before this
+                // CTA's own adds of layer L, which any later adder to acc_{L+2} waits for
+                if (zero_slice(a.acc + (size_t)((L + 2) % 3) * MH, MH, c, G, tid - 64, W * 32 - 64)) fence_acq_rel_gpu();
             }
             FUSED_MARK(L, 3);
             if (L == 0 && tid == 0 && !*abort) grid_wait(a.sync, (unsigned)G, a.wait_cycles, abort);  // acc_1 cleared
             wok = warp_wait_cluster(&actbar[par], (uint32_t)((L >> 1) & 1), abort, a.sync + 1, a.wait_cycles);
-            if (cons_bar_or(!wok || *abort != 0)) break;
+            if (cons_bar_or<W>(!wok || *abort != 0)) break;
             FUSED_MARK(L, 4);
 
-            // ---- down_proj rows of this CTA x the cluster's 512 features -> fixed-point partials --------
+            // ---- down_proj rows of this CTA x the cluster's 512 features -> counted fixed point ---------
             const I8X txa{aqp, axsp, cs, nullptr, nullptr, nullptr, axep};
-            const bool rows_here = 16 * warp < RB;
+            const bool rows_here = 16 * rt < RB;
             for (int h = 0; h < nhalf; ++h) {
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
@@ -521,8 +622,8 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                     if (h == 0 && s == 0) FUSED_MARK(L, 7);
                     if (h == nhalf - 1 && s == 1) FUSED_MARK(L, 9);
                     if (wok && rows_here) {
-                        i8_stage<NTN, kFRows, kFChain>(ring + (size_t)slot * kFStage, 8 * s, 4 * s, txa, warp, lane, y,
-                                                       yb);
+                        f_stage<NTN, NQ, CHAIN>(ring + (size_t)slot * kFStage, 8 * s, 4 * s, kp * NQ, txa, rt, lane, y,
+                                                yb);
 #pragma unroll
                         for (int j = 0; j < NTN; ++j) {
                             hold_regs(y[j]);
@@ -537,7 +638,8 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                     }
                 }
                 if (wok && rows_here) {
-                    const int lr0 = h * RB + 16 * warp + g, lr1 = lr0 + 8;  // rows within this CTA's range
+                    const int lr0 = h * RB + 16 * rt + g, lr1 = lr0 + 8;  // rows within this CTA's range
+                    const bool add_res = cj == 0 && kp == 0;
 #pragma unroll
                     for (int j = 0; j < NTN; ++j) {
                         const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
@@ -545,31 +647,34 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_layers_kernel(const __grid
                         const int m = 2 * j + (tq >> 1);
                         if ((tq & 1) == 0 && m < M) {
                             long long f0 = to_fix(pp.x), f1 = to_fix(pp.y);
-                            if (cj == 0) {
+                            if (add_res) {
                                 f0 += to_fix(res[lr0 * MS + m]);
                                 f1 += to_fix(res[lr1 * MS + m]);
                             }
-                            red_add_u64(accN + (size_t)m * H + rd0 + lr0, f0);
-                            red_add_u64(accN + (size_t)m * H + rd0 + lr1, f1);
+                            red_add_u64(accN + (size_t)m * H + rd0 + lr0, fix_word(f0));
+                            red_add_u64(accN + (size_t)m * H + rd0 + lr1, fix_word(f1));
                         }
                     }
                 }
             }
             FUSED_MARK(L, 5);
-            if (cons_bar_or(!wok || *abort != 0)) break;
-            if (tid == 0) red_release_add(a.sync, 1u);  // layer L's partials are in acc_{L+1}
+            if (cons_bar_or<W>(!wok || *abort != 0)) break;
         }
     }
-    cluster_sync_all();  // no CTA leaves while a peer may still write into its shared memory
+    cluster_sync_all();  // no CTA leaves while a peer may still copy into its shared memory
 }
 
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
 int fused_ntn(int64_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : 4); }
+#ifndef FUSED_W1
+#define FUSED_W1 16
+#endif
+int fused_warps(int ntn) { return ntn == 1 ? FUSED_W1 : 8; }
 
 uint32_t plan_fused(FusedArgs& a, int M, int H) {
-    const int ntn = fused_ntn(M), ncols = 8 * ntn, MS = 2 * ntn;
+    const int ntn = fused_ntn(M), ncols = 8 * ntn, MS = 2 * ntn, W = fused_warps(ntn);
     const int HG = H / kGroup, RD = H / kFCluster;
     auto al = [](uint32_t v, uint32_t x) { return (v + x - 1) / x * x; };
     for (int S = 12; S >= 3; --S) {
@@ -577,7 +682,7 @@ uint32_t plan_fused(FusedArgs& a, int M, int H) {
         a.off_bar = off;
         off += al((2u * S + 2u) * 8u, 128);
         a.off_misc = off;
-        off += al(64u + (uint32_t)(kFWarps + 1) * MS * 4u, 128);
+        off += al(64u + (uint32_t)W * MS * 4u, 128);
         a.off_hq = off;
         off += (uint32_t)HG * ncols * 64;
         a.off_hxs = off;
@@ -593,7 +698,7 @@ uint32_t plan_fused(FusedArgs& a, int M, int H) {
         a.off_axe = off;
         off += al(2u * kFCluster * ncols * 4, 128);
         a.off_out = off;
-        off += al((uint32_t)kFRows * MS * 4, 128);
+        off += al((uint32_t)(W / 8) * kFRows * MS * 4, 128);
         a.off_res = off;
         off += al((uint32_t)RD * MS * 4, 128);
         off = al(off, 1024);
@@ -607,15 +712,15 @@ uint32_t plan_fused(FusedArgs& a, int M, int H) {
     return 0;
 }
 
-template <int NTN>
+template <int NTN, int W>
 cudaError_t fused_config(int grid, uint32_t smem, bool pdl, cudaStream_t stream, cudaLaunchConfig_t& cfg,
                          cudaLaunchAttribute (&attr)[2]) {
     cudaError_t e =
-        cudaFuncSetAttribute(fused_layers_kernel<NTN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(fused_layers_kernel<NTN, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kFThreads);
+    cfg.blockDim = dim3(fused_threads(W));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     int na = 0;
@@ -634,17 +739,26 @@ cudaError_t fused_config(int grid, uint32_t smem, bool pdl, cudaStream_t stream,
     return cudaSuccess;
 }
 
-template <int NTN>
+template <int NTN, int W>
 cudaError_t fused_max_clusters(uint32_t smem, int* n) {
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
-    cudaError_t e = fused_config<NTN>(kFCluster, smem, false, nullptr, cfg, attr);
+    cudaError_t e = fused_config<NTN, W>(kFCluster, smem, false, nullptr, cfg, attr);
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveClusters(n, fused_layers_kernel<NTN>, &cfg);
+    return cudaOccupancyMaxActiveClusters(n, fused_layers_kernel<NTN, W>, &cfg);
+}
+
+template <int NTN, int W>
+cudaError_t fused_launch(const FusedArgs& a, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    const cudaError_t e = fused_config<NTN, W>(grid, smem, pdl, stream, cfg, attr);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, fused_layers_kernel<NTN, W>, a);
 }
 
 // Whether `grid` CTAs in clusters of 8 can all be resident at once on the current device (the layer
-// barriers need every CTA running).  Cached per device and activation width.
+// waits need every CTA running).  Cached per device and activation width.
 bool fused_coresident(int ntn, int grid, uint32_t smem) {
     static std::mutex mu;
     static int cache[64][3];  // [device][ntn index]: 0 unknown, else max active clusters + 1
@@ -654,9 +768,9 @@ bool fused_coresident(int ntn, int grid, uint32_t smem) {
     std::lock_guard<std::mutex> lk(mu);
     if (!cache[dev][ti]) {
         int n = 0;
-        const cudaError_t e = ntn == 1   ? fused_max_clusters<1>(smem, &n)
-                              : ntn == 2 ? fused_max_clusters<2>(smem, &n)
-                                         : fused_max_clusters<4>(smem, &n);
+        const cudaError_t e = ntn == 1   ? fused_max_clusters<1, FUSED_W1>(smem, &n)
+                              : ntn == 2 ? fused_max_clusters<2, 8>(smem, &n)
+                                         : fused_max_clusters<4, 8>(smem, &n);
         if (e != cudaSuccess) {
             cudaGetLastError();
             n = 0;
@@ -673,10 +787,14 @@ size_t fused_acc_bytes(int64_t m, int64_t hidden) { return (size_t)3 * (size_t)m
 bool fused_supported(int64_t m, int64_t hidden, int64_t inter, int n_layers) {
     if (m < 1 || m > kFusedMaxRows || n_layers < 1 || n_layers > kFusedMaxLayers) return false;
     if (hidden != 512 && hidden != 1024 && hidden != 2048) return false;
-    if (inter % 512 != 0 || inter / kGroup > device_num_sms() || tmap_encode_fn() == nullptr) return false;
+    // inter / 64 CTAs on distinct SMs; the count field holds up to 31 contributions per word
+    const int64_t G = inter / kGroup;
+    if (inter % 512 != 0 || G > device_num_sms() || (fused_warps(fused_ntn(m)) / 8) * (G / kFCluster) > 31 ||
+        tmap_encode_fn() == nullptr)
+        return false;
     FusedArgs a;
     const uint32_t smem = plan_fused(a, (int)m, (int)hidden);
-    return smem != 0 && fused_coresident(fused_ntn(m), (int)(inter / kGroup), smem);
+    return smem != 0 && fused_coresident(fused_ntn(m), (int)G, smem);
 }
 
 cudaError_t launch_fused_layers(const FusedLaunch& F, cudaStream_t stream) {
@@ -705,16 +823,11 @@ cudaError_t launch_fused_layers(const FusedLaunch& F, cudaStream_t stream) {
     a.n_layers = F.n_layers;
     a.eps = F.eps;
     const int grid = (int)(F.inter / kGroup);
-    const int ntn = fused_ntn(M);
-    cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr[2];
-    cudaError_t e = ntn == 1   ? fused_config<1>(grid, smem, F.pdl, stream, cfg, attr)
-                    : ntn == 2 ? fused_config<2>(grid, smem, F.pdl, stream, cfg, attr)
-                               : fused_config<4>(grid, smem, F.pdl, stream, cfg, attr);
-    if (e != cudaSuccess) return e;
-    if (ntn == 1) return cudaLaunchKernelEx(&cfg, fused_layers_kernel<1>, a);
-    if (ntn == 2) return cudaLaunchKernelEx(&cfg, fused_layers_kernel<2>, a);
-    return cudaLaunchKernelEx(&cfg, fused_layers_kernel<4>, a);
+    switch (fused_ntn(M)) {
+        case 1: return fused_launch<1, FUSED_W1>(a, grid, smem, F.pdl, stream);
+        case 2: return fused_launch<2, 8>(a, grid, smem, F.pdl, stream);
+        default: return fused_launch<4, 8>(a, grid, smem, F.pdl, stream);
+    }
 }
 
 int fused_device_error(bool clear) { return tu_device_error(clear); }

@@ -6,7 +6,8 @@
 
 namespace marlin {
 
-// kFix64 (internal): 64-bit fixed point, value * 2^32 (the one-kernel layer stack's h accumulator).
+// kFix64 (internal): counted 64-bit fixed point (the one-kernel layer stack's h accumulator, see
+// load_fix8).
 enum ActDtype : int { kBF16 = 0, kF32 = 1, kFix64 = 2 };
 
 // Device view of a QuantizedTensor (MLX layout).

@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(LmStage<W>::kThreads, 1) i8_lm_head_kernel(con
         if (L.x_out && L.x_dtype == kFix64) {
             const unsigned long long* xf = static_cast<const unsigned long long*>(L.x);
             for (int i = tid; i < M * (int)L.w.k; i += blockDim.x)
-                L.x_out[i] = __ll2float_rn((long long)__ldcg(xf + i)) * 2.3283064365386963e-10f;
+                L.x_out[i] = fix_value(__ldcg(xf + i));
         }
     }
     uint64_t* xbar = full + 2 * S;  // planes copied in (has_xin)

@@ -27,14 +27,23 @@ struct XGeom {
     int M, P, M_eff, XRS, GC;
 };
 
-// Eight consecutive 64-bit fixed-point values (value * 2^32, two's complement, as the one-kernel
-// layer stack accumulates h) as binary32, read from L2 (the words were written by atomics).
+// Counted fixed point, the one-kernel layer stack's accumulator of h: a 64-bit two's-complement
+// word holds (value * 2^27) << 5 plus, in its low 5 bits, the number of contributions added so far
+// (each atomic add carries +1 there), so a reader knows from the word itself when it is complete.
+constexpr int kFixCountBits = 5;
+constexpr float kFixUnit = 7.450580596923828125e-9f;  // 2^-27
+
+__device__ __forceinline__ float fix_value(unsigned long long w) {
+    return __ll2float_rn((long long)w >> kFixCountBits) * kFixUnit;
+}
+
+// Eight consecutive counted fixed-point words (complete ones) as binary32, read from L2.
 __device__ __forceinline__ void load_fix8(const unsigned long long* p, float v[8]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const ulonglong2 q = __ldcg(reinterpret_cast<const ulonglong2*>(p) + k);
-        v[2 * k] = __ll2float_rn((long long)q.x) * 2.3283064365386963e-10f;
-        v[2 * k + 1] = __ll2float_rn((long long)q.y) * 2.3283064365386963e-10f;
+        v[2 * k] = fix_value(q.x);
+        v[2 * k + 1] = fix_value(q.y);
     }
 }
 
