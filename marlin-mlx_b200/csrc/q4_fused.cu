@@ -59,6 +59,10 @@
 #ifndef FUSED_PMARK
 #define FUSED_PMARK(l, k)
 #endif
+// FUSED_READY(l, ready): per warp and ring stage, whether the stage had landed when first polled.
+#ifndef FUSED_READY
+#define FUSED_READY(l, r)
+#endif
 
 namespace marlin {
 namespace {
@@ -70,7 +74,6 @@ constexpr uint32_t kFSb = kFRows * 16;              // scale (or bias) box: 8 gr
 constexpr uint32_t kFStage = kFPacked + 2 * kFSb;   // 20 KB
 constexpr uint32_t kFSmemLimit = 226 * 1024;
 constexpr int kFBar = 1;                            // named barrier of the consumer warps
-constexpr int kFWriteBar = 2;                       // named barrier of the 64 SwiGLU writer threads
 
 __host__ __device__ constexpr int fused_threads(int W) { return (W + 1) * 32; }
 
@@ -87,7 +90,7 @@ struct FusedArgs {
     unsigned long long wait_cycles;
     int M, H, n_layers, S;
     float eps;
-    uint32_t off_bar, off_misc, off_hq, off_hxs, off_hxe, off_cs, off_aq, off_axs, off_axe, off_out, off_res, off_ring;
+    uint32_t off_bar, off_misc, off_hq, off_hxs, off_hxe, off_cs, off_aq, off_out, off_res, off_ring;
 };
 static_assert(sizeof(FusedArgs) <= 32000, "kernel parameters above the 32 KB limit");
 
@@ -257,12 +260,20 @@ __device__ __forceinline__ bool zero_slice(unsigned long long* p, size_t n, int 
     return b + t < e;
 }
 
+// Activation operand in shared memory: per 64-group gl, the planes at xq + gl * qstride
+// ([ncols][64] bytes), 64 x the group sums at xs[gl * xstride + column] and 2^e at xe[...].
+struct FOperand {
+    const uint8_t* xq;
+    const float* xs;
+    const float* xe;
+    int qstride, xstride;
+};
+
 // One ring stage for a warp's 16-row tile rt, groups [q0, q0 + NQ) of the stage's four (see i8_stage
 // in q4_i8_common.cuh for the layout and the arithmetic).
 template <int NTN, int NQ, bool CHAIN>
-__device__ __forceinline__ void f_stage(const uint8_t* st, int so, int gl0, int q0, const I8X& t, int rt, int lane,
-                                        float (&y)[NTN][4], float (&yb)[NTN][2]) {
-    constexpr int ncols = 8 * NTN;
+__device__ __forceinline__ void f_stage(const uint8_t* st, int so, int gl0, int q0, const FOperand& t, int rt,
+                                        int lane, float (&y)[NTN][4], float (&yb)[NTN][2]) {
     const int g = lane >> 2, tq = lane & 3;
     const int r0 = 16 * rt + g, r1 = r0 + 8;
     const uint8_t* sc = st + kFRows * 128;
@@ -286,8 +297,8 @@ __device__ __forceinline__ void f_stage(const uint8_t* st, int so, int gl0, int 
         const int gl = gl0 + q;
 #pragma unroll
         for (int j = 0; j < NTN; ++j) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + ((size_t)(gl * ncols + 8 * j + g) * 64 + 16 * tq));
-            const int c0 = gl * ncols + 8 * j + 4 * (tq >> 1);
+            const uint4 xv = *reinterpret_cast<const uint4*>(t.xq + (size_t)gl * t.qstride + (8 * j + g) * 64 + 16 * tq);
+            const int c0 = gl * t.xstride + 8 * j + 4 * (tq >> 1);
             if constexpr (CHAIN)
                 i8_group_chained(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
             else
@@ -333,14 +344,13 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
     float* hxs = reinterpret_cast<float*>(smem + a.off_hxs);
     float* hxe = reinterpret_cast<float*>(smem + a.off_hxe);
     float* cs = reinterpret_cast<float*>(smem + a.off_cs);
-    uint8_t* aq = smem + a.off_aq;                                    // [2][8][ncols][64] act planes
-    float* axs = reinterpret_cast<float*>(smem + a.off_axs);          // [2][8][ncols]
-    float* axe = reinterpret_cast<float*>(smem + a.off_axe);
+    uint8_t* aq = smem + a.off_aq;  // [2 parities][8 slots]: activation planes [ncols][64], sums, exponents
     float* out = reinterpret_cast<float*>(smem + a.off_out);          // [KP][128][MS] gate / up rows
     float* res = reinterpret_cast<float*>(smem + a.off_res);          // [RD][MS] residual rows
     uint8_t* ring = smem + a.off_ring;
-    const uint32_t aq_bytes = (uint32_t)kFCluster * ncols * 64, ax_words = (uint32_t)kFCluster * ncols;
-    const uint32_t src_bytes = (uint32_t)ncols * (64 + 8);  // one CTA's slot: planes, sums, exponents
+    constexpr uint32_t SB = (uint32_t)ncols * (64 + 8);  // one CTA's slot (copied as one piece)
+    constexpr uint32_t aq_bytes = kFCluster * SB;
+    float* xch = red + W * MS;  // [2][4][MS]: SwiGLU group maxima and sums of the two half-group warps
 
     if (tid == 0) {
         *abort = 0;
@@ -357,7 +367,6 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
     for (int i = tid; i < HG * ncols; i += fused_threads(W)) hxs[i] = hxe[i] = 0.f;
     for (int i = tid; i < (int)(2 * aq_bytes / 16); i += fused_threads(W))
         reinterpret_cast<uint4*>(aq)[i] = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < (int)(2 * ax_words); i += fused_threads(W)) axs[i] = axe[i] = 0.f;
     for (int i = tid; i < ncols; i += fused_threads(W)) cs[i] = (i >> 2) < M ? pow2f(-10 - 7 * (i & 3)) : 0.f;
     __syncthreads();
     cluster_sync_all();  // peers' barriers and buffers are ready before any remote copy
@@ -500,12 +509,13 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
             }
 
             // ---- gate / up rows of the CTA's 64 features over all of hidden -----------------------------
-            const I8X txh{hq, hxs, cs, nullptr, nullptr, nullptr, hxe};
+            const FOperand txh{hq, hxs, hxe, ncols * 64, ncols};
             float y[NTN][4], yb[NTN][2];
 #pragma unroll
             for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
             bool wok = true;
             for (int t = 0; t < gu_st; ++t) {
+                FUSED_READY(L, mbar_try_wait(&full[slot], fpar));
                 if (wok) wok = warp_wait(&full[slot], fpar, abort);
                 if (t == 0) FUSED_MARK(L, 6);
                 if (t == gu_st - 1) FUSED_MARK(L, 8);
@@ -543,66 +553,77 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
             if (cons_bar_or<W>(*abort != 0)) break;
 
             // ---- SwiGLU -> activation planes, copied into every CTA of the cluster ----------------------
+            // one activation per thread (feature f of row m); the group's exponent and sum come from
+            // the two warps of the row (shuffles, then a consumer barrier); the planes are written
+            // byte by byte into this CTA's slot, which then goes to the seven peers as one bulk copy
             uint8_t* aqp = aq + (size_t)par * aq_bytes;
-            float* axsp = axs + (size_t)par * ax_words;
-            float* axep = axe + (size_t)par * ax_words;
-            if (tid < 64) {  // thread 8 m + u: features 8u..8u+7 of row m (whole warps shuffle)
-                const int m = tid >> 3, u = tid & 7;
-                const bool live = m < M;
-                float av[8];
-                float amx = 0.f, sm = 0.f;
+            uint8_t* slot_p = aqp + crank * SB;
+            float* sxs = reinterpret_cast<float*>(slot_p + ncols * 64);
+            float* sxe = sxs + ncols;
+            float av[(64 * MS + W * 32 - 1) / (W * 32)];
+            constexpr int NA = (64 * MS + W * 32 - 1) / (W * 32);  // activations per thread
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    av[j] = 0.f;
-                    if (live) {
-                        float gv = 0.f, uv = 0.f;
+            for (int i = 0; i < NA; ++i) {
+                const int idx = tid + i * W * 32, m = idx >> 6, f = idx & 63;
+                av[i] = 0.f;
+                if (m < M) {
+                    float gv = 0.f, uv = 0.f;
 #pragma unroll
-                        for (int k = 0; k < KP; ++k) {
-                            gv += out[(k * kFRows + 8 * u + j) * MS + m];
-                            uv += out[(k * kFRows + 64 + 8 * u + j) * MS + m];
-                        }
-                        const float sg = 1.0f / (1.0f + expf(-gv));
-                        av[j] = (sg * gv) * uv;
+                    for (int k = 0; k < KP; ++k) {
+                        gv += out[(k * kFRows + f) * MS + m];
+                        uv += out[(k * kFRows + 64 + f) * MS + m];
                     }
-                    amx = fmaxf(amx, fabsf(av[j]));
-                    sm = __fadd_rn(sm, av[j]);
+                    const float sg = 1.0f / (1.0f + expf(-gv));
+                    av[i] = (sg * gv) * uv;
                 }
-                unsigned bits = __float_as_uint(amx);
+                if ((idx >> 6) < MS) {  // warp-uniform: whole warps of rows below MS
+                    const unsigned bm = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av[i])));
+                    float sm = av[i];
 #pragma unroll
-                for (int o = 1; o < 8; o <<= 1) {
-                    bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
-                    sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                }
-                if (live) {
-                    const int e = row_exp(bits);
-                    uint32_t b[4][2];
-                    planes8(av, e, b);
-#pragma unroll
-                    for (int p = 0; p < 4; ++p)
-                        *reinterpret_cast<uint2*>(aqp + ((crank * ncols + 4 * m + p) * 64 + 8 * u)) =
-                            make_uint2(b[p][0], b[p][1]);
-                    if (u == 0) {
-                        axsp[crank * ncols + 4 * m] = __fmul_rn(sm, 64.0f);
-                        axep[crank * ncols + 4 * m] = pow2f(e);
+                    for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                    if (lane == 0) {
+                        xch[((f >> 5) * 4 + 0) * MS + m] = __uint_as_float(bm);
+                        xch[((f >> 5) * 4 + 1) * MS + m] = sm;
                     }
                 }
-                fence_proxy_async_smem();  // the slot is read by the bulk copies below
-                asm volatile("bar.sync %0, %1;" ::"r"(kFWriteBar), "r"(64) : "memory");
-                if (tid == 0) {
-                    const uint32_t lq = smem_u32(aqp) + crank * ncols * 64, lxs = smem_u32(axsp) + crank * ncols * 4,
-                                   lxe = smem_u32(axep) + crank * ncols * 4, lbar = smem_u32(&actbar[par]);
-                    for (uint32_t r = 1; r < (uint32_t)kFCluster; ++r) {
-                        const uint32_t dst = (crank + r) % kFCluster, rbar = mapa_u32(lbar, dst);
-                        bulk_s2cluster(mapa_u32(lq, dst), lq, (uint32_t)ncols * 64, rbar);
-                        bulk_s2cluster(mapa_u32(lxs, dst), lxs, (uint32_t)ncols * 4, rbar);
-                        bulk_s2cluster(mapa_u32(lxe, dst), lxe, (uint32_t)ncols * 4, rbar);
+            }
+            FUSED_MARK(L, 11);
+            cons_bar<W>();
+#pragma unroll
+            for (int i = 0; i < NA; ++i) {
+                const int idx = tid + i * W * 32, m = idx >> 6, f = idx & 63;
+                if (m < M) {
+                    const float gmax = fmaxf(xch[(0 * 4 + 0) * MS + m], xch[(1 * 4 + 0) * MS + m]);
+                    const int e = row_exp(__float_as_uint(gmax));
+                    const float qa = rintf(__fmul_rn(av[i], pow2f(13 - e)));
+                    const int A = (int)qa;
+                    const int B = __float2int_rn(__fmul_rn(fmaf(-qa, pow2f(e - 13), av[i]), pow2f(27 - e)));
+                    const int i0 = (A + 64) >> 7, i2 = (B + 64) >> 7;
+                    const int d[4] = {i0, A - (i0 << 7), i2, B - (i2 << 7)};
+                    const int pos = plane_pos(f);
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) slot_p[(4 * m + p) * 64 + pos] = (uint8_t)(d[p] & 0xff);
+                    if (f == 0) {
+                        sxs[4 * m] = __fmul_rn(xch[(0 * 4 + 1) * MS + m] + xch[(1 * 4 + 1) * MS + m], 64.0f);
+                        sxe[4 * m] = pow2f(e);
                     }
-                    mbar_arrive_expect_tx(&actbar[par], (kFCluster - 1) * src_bytes);
                 }
-            } else if (L > 0) {
-                // idle during SwiGLU: clear this CTA's slice of acc_{L+2} (complete words of acc_L show that
-                // every CTA has read acc_{L-1}, which it reuses); the fence orders the zeros before this
-                // CTA's own adds of layer L, which any later adder to acc_{L+2} waits for
+            }
+            fence_proxy_async_smem();  // the slot is read by the bulk copies below
+            cons_bar<W>();
+            FUSED_MARK(L, 14);
+            if (warp == 0 && lane < kFCluster) {
+                const uint32_t ls = smem_u32(slot_p), lbar = smem_u32(&actbar[par]);
+                if (lane > 0) {
+                    const uint32_t dst = (crank + (uint32_t)lane) % kFCluster;
+                    bulk_s2cluster(mapa_u32(ls, dst), ls, SB, mapa_u32(lbar, dst));
+                } else {
+                    mbar_arrive_expect_tx(&actbar[par], (kFCluster - 1) * SB);
+                }
+            } else if (L > 0 && tid >= 64) {
+                // clear this CTA's slice of acc_{L+2} (complete words of acc_L show that every CTA has read
+                // acc_{L-1}, which it reuses); the fence orders the zeros before this CTA's own adds of
+                // layer L, which any later adder to acc_{L+2} waits for
                 if (zero_slice(a.acc + (size_t)((L + 2) % 3) * MH, MH, c, G, tid - 64, W * 32 - 64)) fence_acq_rel_gpu();
             }
             FUSED_MARK(L, 3);
@@ -612,12 +633,14 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
             FUSED_MARK(L, 4);
 
             // ---- down_proj rows of this CTA x the cluster's 512 features -> counted fixed point ---------
-            const I8X txa{aqp, axsp, cs, nullptr, nullptr, nullptr, axep};
+            const FOperand txa{aqp, reinterpret_cast<const float*>(aqp + ncols * 64),
+                               reinterpret_cast<const float*>(aqp + ncols * 64) + ncols, (int)SB, (int)(SB / 4)};
             const bool rows_here = 16 * rt < RB;
             for (int h = 0; h < nhalf; ++h) {
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = yb[j][0] = yb[j][1] = 0.f;
                 for (int s = 0; s < 2; ++s) {
+                    FUSED_READY(L, mbar_try_wait(&full[slot], fpar));
                     if (wok) wok = warp_wait(&full[slot], fpar, abort);
                     if (h == 0 && s == 0) FUSED_MARK(L, 7);
                     if (h == nhalf - 1 && s == 1) FUSED_MARK(L, 9);
@@ -682,7 +705,7 @@ uint32_t plan_fused(FusedArgs& a, int M, int H) {
         a.off_bar = off;
         off += al((2u * S + 2u) * 8u, 128);
         a.off_misc = off;
-        off += al(64u + (uint32_t)W * MS * 4u, 128);
+        off += al(64u + (uint32_t)(W + 8) * MS * 4u, 128);
         a.off_hq = off;
         off += (uint32_t)HG * ncols * 64;
         a.off_hxs = off;
@@ -692,11 +715,7 @@ uint32_t plan_fused(FusedArgs& a, int M, int H) {
         a.off_cs = off;
         off += al((uint32_t)ncols * 4, 128);
         a.off_aq = off;
-        off += 2u * kFCluster * ncols * 64;
-        a.off_axs = off;
-        off += al(2u * kFCluster * ncols * 4, 128);
-        a.off_axe = off;
-        off += al(2u * kFCluster * ncols * 4, 128);
+        off += al(2u * kFCluster * ncols * 72, 128);
         a.off_out = off;
         off += al((uint32_t)(W / 8) * kFRows * MS * 4, 128);
         a.off_res = off;
