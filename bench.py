@@ -15,9 +15,10 @@ memory (marlin_q4_tp_decode_step): strong scaling.
 least one second has been timed, each repeat bracketed by a barrier and a synchronize, the max over
 ranks per repeat, the median over repeats.  `e2e` repeats the measurement through the public API
 with the step's embeddings copied from pinned host memory and the token ids read back to the host
-every step.  `roofline` covers the step's dominant part, the per-layer pair of MLP kernels as they
-run inside the step (per-layer time = (t(24 layers) - t(1 layer)) / 23, both CUDA-graph replays of
-the same public call; per rank at N > 1).  At N > 1 `parity` compares the sharded step's ids and h
+every step.  `roofline` covers the step's dominant part, the MLP layers as they run inside the step
+(at N = 1 one persistent kernel for all layers, at N > 1 two kernels per layer; per-layer time =
+(t(24 layers) - t(1 layer)) / 23, both CUDA-graph replays of the same public call; per rank at
+N > 1).  `extras.step_per_layer_kernels` times the N = 1 step on the per-layer kernels as well.  At N > 1 `parity` compares the sharded step's ids and h
 with the unsharded single-GPU step on the same inputs; `extras.batch_sweep` gives batch 1/8/32 and
 `extras.prefill_c4` the config-4 prefill MLP layer at every N.  `gemv` is the metric's first half
 (config 1: one 6144x2048 Q4 GEMV, bf16 x, N = 1).
@@ -331,17 +332,35 @@ def run_ours(args):
         traffic = None
         tp_path = ROOT / "profiles" / "traffic.json"
         if world == 1 and B == 1 and tp_path.exists():
-            traffic = json.loads(tp_path.read_text()).get("mlp_layer")
+            traffic = json.loads(tp_path.read_text()).get("fused_layer")
         ach = layer_bytes / (layer_ms * 1e-3) / 1e9
-        kname = ("i8_unit_kernel gate/up+SwiGLU launch + i8_unit_kernel down+residual launch (cluster K split, "
-                 "activation planes handed between them)")
-        roof = {"bound": "hbm", "kernel": f"mlp_layer: {kname}, as run inside the step"
-                                          + (" (per rank; the down launch's epilogue holds the in-kernel all-reduce)"
-                                             if world > 1 else ""),
+        if world == 1:
+            kname = ("fused_layers_kernel: all 24 MLP layers in one persistent launch (CTA per 64 intermediate "
+                     "features, SwiGLU activations shared in 8-CTA clusters, down_proj partials in a counted "
+                     "fixed-point accumulator); per layer")
+            launches = 1
+        else:
+            kname = ("i8_unit_kernel gate/up+SwiGLU launch + i8_unit_kernel down+residual launch (cluster K split, "
+                     "activation planes handed between them), per rank; the down launch's epilogue holds the "
+                     "in-kernel all-reduce")
+            launches = 2
+        roof = {"bound": "hbm", "kernel": f"mlp_layer: {kname}, as run inside the step",
                 "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4),
-                "traffic": traffic, "algorithmic_bytes_per_launch": layer_bytes, "launches": 2,
-                "launch_us": round(layer_ms * 1e3, 3), "peak_source": pk["source"],
+                "traffic": traffic, "algorithmic_bytes_per_layer": layer_bytes, "launches_per_layer": launches,
+                "layer_us": round(layer_ms * 1e3, 3), "peak_source": pk["source"],
                 "share_of_step": split["layers_share"]}
+        if world == 1:
+            # the same step on the per-layer kernels (two cluster split-K launches per layer), for comparison
+            mq.set_step_kernels("layers")
+            try:
+                stl = make_step(layers, B)
+                t_layers = time_graph(torch, lambda: stl(h0), reps)
+                del stl
+            finally:
+                mq.set_step_kernels("fused")
+            extras["step_per_layer_kernels"] = {"ms_per_step": round(t_layers, 4),
+                                                "tokens_per_s": round(B / (t_layers / 1e3), 1),
+                                                "note": "marlin_q4_set_step_kernels(MARLIN_Q4_STEP_LAYERS)"}
 
         # batch sweep of the full step (every N)
         sweep = {}
@@ -460,7 +479,9 @@ def run_ours(args):
         cpu = cpu_baseline_from_device(layers, fn, lm, h0, B, args.cpu_seconds)
 
     chunks = -(-B // 8)  # above 8 rows the step runs in 8-row chunks
-    launches = args.steps * chunks * (2 * L + 1)  # per step: gate/up and down per layer, then the lm_head
+    # per chunk: one layer-stack launch and the lm_head at N = 1; gate/up and down per layer, then the
+    # lm_head, at N > 1
+    launches = args.steps * chunks * (2 if world == 1 else 2 * L + 1)
     line = {
         "metric": METRIC,
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

@@ -203,7 +203,7 @@ __device__ __forceinline__ void cons_bar() {
 }
 
 // Non-blocking test of an mbarrier phase (the timeline hook's readiness probe).
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ __attribute__((unused)) bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
