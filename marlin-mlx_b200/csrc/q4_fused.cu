@@ -383,6 +383,7 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
     __syncthreads();
     cluster_sync_all();  // peers' barriers and buffers are ready before any remote copy
 
+    int armed = -1;  // consumers: last layer whose activation barrier was armed and not yet waited for
     if (warp == W) {
         // ---- TMA producer: every layer's stages in order through the ring ------------------------------
         pdl_launch_dependents();
@@ -654,10 +655,12 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
                 // layer L, which any later adder to acc_{L+2} waits for
                 if (zero_slice(a.acc + (size_t)((L + 2) % 3) * MH, MH, c, G, tid - 64, W * 32 - 64)) fence_acq_rel_gpu();
             }
+            armed = L;
             FUSED_MARK(L, 3);
             if (L == 0 && tid == 0 && !*abort) grid_wait(a.sync, (unsigned)G, a.wait_cycles, abort);  // acc_1 cleared
             wok = warp_wait_cluster(&actbar[par], (uint32_t)((L >> 1) & 1), abort, a.sync + 1, a.wait_cycles);
             if (cons_bar_or<W>(!wok || *abort != 0)) break;
+            armed = -1;
             FUSED_MARK(L, 4);
 
             // ---- down_proj rows of this CTA x the cluster's 512 features -> counted fixed point ---------
@@ -724,7 +727,19 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
             if (cons_bar_or<W>(!wok || *abort != 0)) break;
         }
     }
-    cluster_sync_all();  // no CTA leaves while a peer may still copy into its shared memory
+    // Exit.  After the first cluster barrier no CTA issues another copy; a CTA that left the layer loop
+    // early (an abort) with its activation barrier armed then waits, bounded, for the copies its peers
+    // issued into it to land, and the second barrier keeps every CTA until all have done so: no CTA
+    // leaves while a peer's copy may still write into its shared memory.
+    cluster_sync_all();
+    if (warp < W && armed >= 0) {
+        uint64_t* bar = &actbar[armed & 1];
+        const uint32_t ph = (uint32_t)((armed >> 1) & 1);
+        const unsigned long long t0 = cycles_now();
+        while (!mbar_try_wait_cluster(bar, ph) && cycles_now() - t0 < (1ull << 22)) {
+        }
+    }
+    cluster_sync_all();
 }
 
 // ------------------------------------------------------------------------------------------------
