@@ -137,8 +137,10 @@ int marlin_q4_last_cuda_error(void) { return t_last_cuda_error; }
 int marlin_q4_device_error(int clear) {
     int v = gemv_device_error(clear != 0);
     const int v_i8 = i8_device_error(clear != 0), v_pf = prefill_device_error(clear != 0),
-              v_mi = misc_device_error(clear != 0), v_fu = fused_device_error(clear != 0);
+              v_mi = misc_device_error(clear != 0), v_fu = fused_device_error(clear != 0),
+              v_ro = rows_device_error(clear != 0);
     if (!v) v = v_fu;
+    if (!v) v = v_ro;
     if (!v) v = v_i8;
     if (!v) v = v_pf;
     if (!v) v = v_mi;

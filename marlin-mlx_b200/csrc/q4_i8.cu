@@ -832,6 +832,7 @@ bool i8_supported(int64_t k, int64_t m) {
 }
 
 cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream) {
+    if (rows_gemv_applies(L)) return launch_rows_gemv(L, stream);
     I8UnitArgs a{};
     const uint32_t smem = plan_i8_unit(L, a);
     if (!smem) return cudaErrorInvalidConfiguration;

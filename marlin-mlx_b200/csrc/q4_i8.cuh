@@ -20,6 +20,11 @@ cudaError_t launch_i8_gemv(const GemvLaunch& L, cudaStream_t stream);
 cudaError_t launch_i8_lm_head(const LmHeadLaunch& L, cudaStream_t stream);
 // Device error word of this translation unit (see gemv_device_error).
 int i8_device_error(bool clear);
+// Whole-row GEMV for one or two activation rows (q4_rows.cu): plain products (store epilogue, no
+// RMSNorm, no planes in or out), k a multiple of 1024.  launch_i8_gemv takes it when it applies.
+bool rows_gemv_applies(const GemvLaunch& L);
+cudaError_t launch_rows_gemv(const GemvLaunch& L, cudaStream_t stream);
+int rows_device_error(bool clear);
 
 // Activation columns of the integer-MMA kernels for m rows (4 planes per row, MMA tiles of 8).
 int i8_ncols(int64_t m);
