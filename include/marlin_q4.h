@@ -105,6 +105,12 @@ int marlin_q4_set_decode_path(int path);
 #define MARLIN_Q4_STEP_FUSED 0
 #define MARLIN_Q4_STEP_LAYERS 1
 int marlin_q4_set_step_kernels(int which);
+/* The kernels marlin_q4_decode_step runs, with the current settings on the current device, for m
+ * rows of a model with the given hidden and intermediate sizes and n_layers layers of one shape:
+ * MARLIN_Q4_STEP_FUSED or MARLIN_Q4_STEP_LAYERS (the latter also when the integer-MMA family is
+ * off); MARLIN_Q4_ERR_ARG for a size below 1.  Queries the device (occupancy of the layer-stack
+ * clusters) the first time; no launch. */
+int marlin_q4_decode_step_kernels(int64_t m, int64_t hidden, int64_t intermediate, int32_t n_layers);
 
 /* ---- quantize --------------------------------------------------------------------------------
  * Replaces mx::quantize(w, group_size, bits) at src/model/weights.cpp:46 (quantize_weight,

@@ -442,6 +442,14 @@ int decode_step_planes(const uint16_t* h0, int64_t m, int64_t hidden, int64_t in
     if (tpx) Lh.tp = *tpx;
     return cuda_status(launch_i8_lm_head(Lh, st));
 }
+// Whether marlin_q4_decode_step runs its MLP layers on the one-kernel layer stack (rows in chunks of
+// kStepChunkRows), with the current settings on the current device.
+bool step_uses_fused(int64_t m, int64_t hidden, int64_t inter, int32_t n_layers) {
+    const int64_t mc = std::min<int64_t>(m, kStepChunkRows);
+    return path_is_i8(decode_path()) && g_step_kernels == MARLIN_Q4_STEP_FUSED && i8_supported(hidden, mc) &&
+           fused_supported(mc, hidden, inter, n_layers);
+}
+
 // The decode step with the MLP layers as one persistent kernel (q4_fused.cu) followed by the fused
 // lm_head + argmax, which reads the final h from the kernel's fixed-point accumulator, writes h_out
 // when asked, and clears the kernel's barrier words (sync, in the zero-invariant head of the
@@ -487,6 +495,11 @@ int decode_step_fused(const uint16_t* h0, int64_t m, int64_t hidden, int64_t int
 }
 }  // namespace
 
+int marlin_q4_decode_step_kernels(int64_t m, int64_t hidden, int64_t intermediate, int32_t n_layers) {
+    if (m < 1 || hidden < 1 || intermediate < 1 || n_layers < 1) return MARLIN_Q4_ERR_ARG;
+    return step_uses_fused(m, hidden, intermediate, n_layers) ? MARLIN_Q4_STEP_FUSED : MARLIN_Q4_STEP_LAYERS;
+}
+
 size_t marlin_q4_decode_step_workspace_size(int64_t m, int64_t hidden, int64_t intermediate) {
     if (m <= 0 || hidden <= 0 || intermediate <= 0) return 0;
     return step_zero_bytes(m) + step_compose_bytes(m, hidden, intermediate);
@@ -527,9 +540,7 @@ int marlin_q4_decode_step(const uint16_t* h0, int64_t m, int64_t hidden, int32_t
     float* act = reinterpret_cast<float*>(scratch + align16((size_t)m * hidden * 4));
     if (h_out) h = h_out;
     unsigned* sync = reinterpret_cast<unsigned*>(ws);  // barrier words of the one-kernel stack, zero-invariant
-    const bool fused = path_is_i8(decode_path()) && g_step_kernels == MARLIN_Q4_STEP_FUSED && uniform &&
-                       i8_supported(hidden, std::min<int64_t>(m, kStepChunkRows)) &&
-                       fused_supported(std::min<int64_t>(m, kStepChunkRows), hidden, inter, n_layers);
+    const bool fused = uniform && step_uses_fused(m, hidden, inter, n_layers);
     if (fused && m <= kStepChunkRows)
         return decode_step_fused(h0, m, hidden, inter, n_layers, layers, final_norm, eps, lm, ids, best, h_out,
                                  scratch, sync, lmws, st);

@@ -44,6 +44,7 @@ SIGNATURES = {
     "marlin_q4_set_wait_limit_cycles": (None, [_u64]),
     "marlin_q4_set_decode_path": (ctypes.c_int, [ctypes.c_int]),
     "marlin_q4_set_step_kernels": (ctypes.c_int, [ctypes.c_int]),
+    "marlin_q4_decode_step_kernels": (ctypes.c_int, [_i64, _i64, _i64, _i32]),
     "marlin_q4_quantize": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     "marlin_q4_matmul": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),
     "marlin_q4_matmul_f32": (ctypes.c_int, [_vp, _i32, _i64, _PT, _vp, _vp]),

@@ -342,3 +342,10 @@ def set_step_kernels(which: str) -> None:
     """Select the kernels of the decode step's MLP layers: "fused" (default: all layers in one
     persistent kernel) or "layers" (two cluster split-K kernels per layer)."""
     check(_lib.load().marlin_q4_set_step_kernels(STEP_KERNELS[which]), "marlin_q4_set_step_kernels")
+
+
+def decode_step_kernels(m: int, hidden: int, intermediate: int, n_layers: int) -> str:
+    """Which kernels marlin_q4_decode_step runs for this shape here: "fused" or "layers"."""
+    r = _lib.load().marlin_q4_decode_step_kernels(m, hidden, intermediate, n_layers)
+    check(min(r, 0), "marlin_q4_decode_step_kernels")
+    return "fused" if r == _lib.STEP_FUSED else "layers"
