@@ -73,6 +73,19 @@ constexpr uint32_t kFSb = kFRows * 16;              // scale (or bias) box: 8 gr
 constexpr uint32_t kFStage = kFPacked + 2 * kFSb;   // 20 KB
 constexpr uint32_t kFSmemLimit = 226 * 1024;
 constexpr int kFBar = 1;                            // named barrier of the consumer warps
+#ifndef FUSED_PAIRFOLD
+#define FUSED_PAIRFOLD 1
+#endif
+// one-tile fold of plane pairs (i8_group_pair): measured at one row 290.9 us per step against 293.2
+constexpr bool kFPairFold = FUSED_PAIRFOLD != 0;
+
+// Plane weights of the lane's two columns in the combine (the pair fold keeps one value per row).
+template <bool CHAIN>
+__device__ __forceinline__ float2 fold_weights(const float* cs, int j, int tq) {
+    const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
+    if constexpr (!CHAIN && kFPairFold) return make_float2(cv.y, 0.f);
+    return cv;
+}
 
 __host__ __device__ constexpr int fused_threads(int W) { return (W + 1) * 32; }
 
@@ -272,6 +285,24 @@ __device__ __forceinline__ bool zero_slice(unsigned long long* p, size_t n, int 
     return b + t < e;
 }
 
+// i8_group with the lane's two plane columns folded as one integer, 128 D_p + D_{p+1} (exact, below
+// 2^27), so each row takes one conversion and one fma per group instead of two; the pair's weight in
+// the combine is that of plane p + 1.
+__device__ __forceinline__ void i8_group_pair(uint2 wa, uint2 wb, uint4 xv, float sr0, float sr1, float br0, float br1,
+                                              float xe, float x0, float (&y)[4], float (&yb)[2]) {
+    const uint32_t lo[4] = {wa.x & kNib, wb.x & kNib, wa.y & kNib, wb.y & kNib};
+    const uint32_t hi[4] = {wa.x & ~kNib, wb.x & ~kNib, wa.y & ~kNib, wb.y & ~kNib};
+    int c[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
+    mma_u8s8_16832(c, lo, xv.x, xv.z);  // even elements
+    mma_u8s8_16832(e, hi, xv.y, xv.w);  // odd elements, times 16
+    const int p0 = 128 * (16 * c[0] + e[0]) + (16 * c[1] + e[1]);
+    const int p1 = 128 * (16 * c[2] + e[2]) + (16 * c[3] + e[3]);
+    y[0] = fmaf(sr0 * xe, (float)p0, y[0]);
+    y[2] = fmaf(sr1 * xe, (float)p1, y[2]);
+    yb[0] = fmaf(br0, x0, yb[0]);
+    yb[1] = fmaf(br1, x0, yb[1]);
+}
+
 // Activation operand in shared memory: per 64-group gl, the planes at xq + gl * qstride
 // ([ncols][64] bytes), 64 x the group sums at xs[gl * xstride + column] and 2^e at xe[...].
 struct FOperand {
@@ -313,6 +344,8 @@ __device__ __forceinline__ void f_stage(const uint8_t* st, int so, int gl0, int 
             const int c0 = gl * t.xstride + 8 * j + 4 * (tq >> 1);
             if constexpr (CHAIN)
                 i8_group_chained(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
+            else if constexpr (kFPairFold)
+                i8_group_pair(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
             else
                 i8_group(wa[qq], wb[qq], xv, sr0, sr1, br0, br1, t.xe[c0], t.xs[c0], y[j], yb[j]);
         }
@@ -568,7 +601,7 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
                 const int r0 = kp * kFRows + 16 * rt + g;
 #pragma unroll
                 for (int j = 0; j < NTN; ++j) {
-                    const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
+                    const float2 cv = fold_weights<CHAIN>(cs, j, tq);
                     const float2 pp = i8_combine(y[j], yb[j], cv, tq);
                     const int m = 2 * j + (tq >> 1);
                     const float rfm = __shfl_sync(0xffffffffu, rfl, m & 31);
@@ -708,7 +741,7 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
                     const bool add_res = cj == 0 && kp == 0;
 #pragma unroll
                     for (int j = 0; j < NTN; ++j) {
-                        const float2 cv = *reinterpret_cast<const float2*>(cs + 8 * j + 2 * tq);
+                        const float2 cv = fold_weights<CHAIN>(cs, j, tq);
                         const float2 pp = i8_combine(y[j], yb[j], cv, tq);
                         const int m = 2 * j + (tq >> 1);
                         if ((tq & 1) == 0 && m < M) {
