@@ -6,8 +6,8 @@
 // projection).  The final norm, lm_head and argmax follow as the fused lm_head kernel.
 //
 // Why one kernel.  At one activation row a layer streams 21 MB (3.3 us at HBM speed), but as two
-// dependent launches it pays a launch boundary, a cluster reduction and an epilogue twice.  Here
-// each layer costs one grid-wide arrival counter, and the weights of the next layer stream into
+// dependent launches it pays a launch boundary, a cluster reduction and an epilogue twice.  Here a
+// layer waits once, on the words of its input h, and the weights of the next layer stream into
 // shared memory while the current one finishes.
 //
 // Work split (inter = 64 G features, G CTAs, thread-block clusters of 8):
@@ -32,9 +32,10 @@
 // behind one arrival counter, which the next kernel clears.
 //
 // Warp roles: W consumer warps (8; the kernel also builds with 16, two warps per 16-row tile each
-// taking two of a stage's four groups); the last warp is the TMA producer, which walks every layer's stages
-// (gate/up: 64 + 64 rows x 4 groups; down_proj: up to 128 rows x 4 groups; 20 KB each) through one
-// ring, so the next layer's weights stream while the consumers wait for the current h.
+// taking two of a stage's four groups), which take the ring stages in pairs; the last warp is the TMA
+// producer, which walks every layer's stages (gate/up: 64 + 64 rows x 4 groups; down_proj: up to 128
+// rows x 4 groups; 20 KB each) through one ring, so the next layer's weights stream while the
+// consumers wait for the current h.
 //
 // Every wait is bounded (SM clock cycles): one that runs out records a device error, raises the
 // CTA's abort flag and the grid's abort word, and every other wait then returns at once; the CTAs

@@ -64,6 +64,9 @@ def test_argument_validation_without_gpu(lib):
     from marlin_q4 import _lib as L
     fake = 0x10000  # never dereferenced: every call below fails validation first
     assert lib.marlin_q4_quantize(None, 8, 64, 64, 4, fake, fake, fake, None) == L.ERR_ARG
+    assert lib.marlin_q4_decode_step_kernels(0, 2048, 6144, 24) == L.ERR_ARG
+    assert lib.marlin_q4_decode_step_kernels(1, 2048, 6144, 0) == L.ERR_ARG
+    assert lib.marlin_q4_set_step_kernels(7) == L.ERR_ARG
     assert lib.marlin_q4_quantize(fake, 8, 96, 64, 4, fake, fake, fake, None) == L.ERR_SHAPE
     assert lib.marlin_q4_quantize(fake, 8, 64, 32, 4, fake, fake, fake, None) == L.ERR_SHAPE
     assert lib.marlin_q4_quantize(fake, 8, 64, 64, 8, fake, fake, fake, None) == L.ERR_SHAPE
