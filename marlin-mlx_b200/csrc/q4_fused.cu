@@ -765,12 +765,19 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
     // early (an abort) with its activation barrier armed then waits, bounded, for the copies its peers
     // issued into it to land, and the second barrier keeps every CTA until all have done so: no CTA
     // leaves while a peer's copy may still write into its shared memory.
+    // A CTA that aborted without arming (it left before its SwiGLU) cannot tell whether a peer already
+    // copied into it, so it lets about 100 us pass (a copy of one slot lands within microseconds),
+    // and the second barrier holds the whole cluster meanwhile.  The normal path waits for nothing.
     cluster_sync_all();
     if (warp < W && armed >= 0) {
         uint64_t* bar = &actbar[armed & 1];
         const uint32_t ph = (uint32_t)((armed >> 1) & 1);
         const unsigned long long t0 = cycles_now();
         while (!mbar_try_wait_cluster(bar, ph) && cycles_now() - t0 < (1ull << 22)) {
+        }
+    } else if (tid == 0 && *abort) {
+        const unsigned long long t0 = cycles_now();
+        while (cycles_now() - t0 < 200000ull) {
         }
     }
     cluster_sync_all();
