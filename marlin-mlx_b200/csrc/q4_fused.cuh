@@ -27,8 +27,9 @@ struct FusedLaunch {
     int n_layers;
     const FusedLayer* layers;
     float eps;
-    // Three [m][hidden] 64-bit fixed-point accumulators (value * 2^32, two's complement); after the
-    // launch the final h is acc[n_layers % 3].  No state is carried between launches in them.
+    // Three [m][hidden] 64-bit counted fixed-point accumulators (two's complement: (value * 2^27)
+    // << 5 plus a 5-bit count of the contributions added); after the launch the final h is
+    // acc[n_layers % 3].  No state is carried between launches in them.
     unsigned long long* acc;
     // Two words: the arrival counter of the layer barriers and the abort word.  Zero on entry; left
     // non-zero, the next kernel in the stream must clear them (the lm_head kernel does, see
