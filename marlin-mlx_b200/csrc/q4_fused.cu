@@ -20,7 +20,7 @@
 //   cluster's 512 features (columns [512 j, 512 j + 512): one 16-byte scale box per row, fully
 //   used) and adds the partial rows into the accumulator of the next h with integer atomics.
 //
-// Counted fixed point (load_fix8): every accumulator word is (value * 2^27) << 5 plus a 5-bit count
+// Counted fixed point (poll_fix_rows): every accumulator word is (value * 2^27) << 5 plus a 5-bit count
 // of the contributions added to it, each atomic add bringing +1.  The sum does not depend on the
 // order of the adds (deterministic), and a word is complete when its count reaches the known number
 // of contributions, so the next layer waits on the words themselves: no arrival counter, no
@@ -77,6 +77,10 @@ constexpr int kFBar = 1;                            // named barrier of the cons
 #ifndef FUSED_PAIRFOLD
 #define FUSED_PAIRFOLD 1
 #endif
+// rows of h polled per round trip (more holds more words in registers: 4 spills at 8 rows)
+#ifndef FUSED_POLL_ROWS
+#define FUSED_POLL_ROWS 2
+#endif
 // one-tile fold of plane pairs (i8_group_pair): measured at one row 290.9 us per step against 293.2
 constexpr bool kFPairFold = FUSED_PAIRFOLD != 0;
 
@@ -125,11 +129,6 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ ulonglong2 ld_acquire_v2(const unsigned long long* p) {
-    ulonglong2 v;
-    asm volatile("ld.acquire.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 // Gives up a wait: records the timeout once, raises the grid's abort word and the CTA's flag.
@@ -160,40 +159,69 @@ __device__ void grid_wait(unsigned* sync, unsigned target, unsigned long long li
     }
 }
 
-// Eight accumulator words of h, waited for until each holds `target` contributions (bounded; gives
-// up on a timeout or an abort), as binary32.
-__device__ void poll_fix8(const unsigned long long* p, unsigned target, float (&v)[8], unsigned* gabort,
-                          unsigned long long limit, volatile int* abort) {
-    ulonglong2 q[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) q[k] = ld_acquire_v2(p + 2 * k);
+__device__ __forceinline__ ulonglong2 ld_relaxed_v2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// Eight accumulator words of each of rows 0..M-1 (at p + m * stride), waited for until each holds
+// `target` contributions (bounded; gives up on a timeout or an abort), as binary32.  The rows go in
+// batches of up to four: every pending row's words of a batch are requested before any of them is
+// checked, so a batch costs one round trip to L2 (8 rows: two, not eight).  The loads are relaxed;
+// the fence after them gives the words acquire order (and with them the adders' earlier reads of
+// the accumulator this CTA clears next).
+template <int MS>
+__device__ void poll_fix_rows(const unsigned long long* p, size_t stride, int M, unsigned target,
+                              float (&v)[MS][8], unsigned* gabort, unsigned long long limit, volatile int* abort) {
+    constexpr int PB = MS < FUSED_POLL_ROWS ? MS : FUSED_POLL_ROWS;
     unsigned long long t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        bool done = true;
+    uint32_t it = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            done = done && ((unsigned)q[k].x & 31u) == target && ((unsigned)q[k].y & 31u) == target;
-        if (done) break;
-        if (it == 0) {
-            t0 = cycles_now();
-        } else if ((it & 7u) == 0u) {
-            if (*abort || ld_relaxed(gabort)) {
-                *abort = 1;
-                break;
+    for (int b0 = 0; b0 < MS; b0 += PB) {
+        unsigned pend = 0;
+#pragma unroll
+        for (int i = 0; i < PB; ++i)
+            if (b0 + i < M) pend |= 1u << i;
+        while (pend && !*abort) {
+            ulonglong2 q[PB][4];
+#pragma unroll
+            for (int i = 0; i < PB; ++i) {
+                if ((pend >> i) & 1u) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) q[i][k] = ld_relaxed_v2(p + (size_t)(b0 + i) * stride + 2 * k);
+                }
             }
-            if (cycles_now() - t0 > limit) {
-                give_up(gabort, abort);
-                break;
+#pragma unroll
+            for (int i = 0; i < PB; ++i) {
+                if ((pend >> i) & 1u) {
+                    bool done = true;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        done = done && ((unsigned)q[i][k].x & 31u) == target && ((unsigned)q[i][k].y & 31u) == target;
+                    if (done) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            v[b0 + i][2 * k] = fix_value(q[i][k].x);
+                            v[b0 + i][2 * k + 1] = fix_value(q[i][k].y);
+                        }
+                        pend &= ~(1u << i);
+                    }
+                }
+            }
+            if (!pend) break;
+            if (it++ == 0) {
+                t0 = cycles_now();
+            } else if ((it & 7u) == 0u) {
+                if (ld_relaxed(gabort)) {
+                    *abort = 1;
+                } else if (cycles_now() - t0 > limit) {
+                    give_up(gabort, abort);
+                }
             }
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = ld_acquire_v2(p + 2 * k);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        v[2 * k] = fix_value(q[k].x);
-        v[2 * k + 1] = fix_value(q[k].y);
-    }
+    fence_acq_rel_gpu();
 }
 
 // Named barrier of the consumer warps that also returns whether any of them passed `p` true: the
@@ -490,11 +518,9 @@ __global__ void __launch_bounds__(fused_threads(W), 1) fused_layers_kernel(const
             for (int m = 0; m < MS; ++m) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[m][j] = 0.f;
-                if (m < M && has_unit) {
-                    if (L == 0) load8(a.h0, kBF16, (int64_t)m * H + 8 * tid, v[m]);
-                    else poll_fix8(accL + (size_t)m * H + 8 * tid, target, v[m], a.sync + 1, a.wait_cycles, abort);
-                }
+                if (L == 0 && m < M && has_unit) load8(a.h0, kBF16, (int64_t)m * H + 8 * tid, v[m]);
             }
+            if (L > 0 && has_unit) poll_fix_rows<MS>(accL + 8 * tid, (size_t)H, M, target, v, a.sync + 1, a.wait_cycles, abort);
             FUSED_MARK(L, 10);
             if (has_unit) {
                 const int grp = tid >> 3, u8 = tid & 7;

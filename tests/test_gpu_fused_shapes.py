@@ -64,3 +64,21 @@ def test_step_kernel_choice():
         assert mq.decode_step_kernels(1, 2048, 6144, 24) == "layers"
     finally:
         mq.set_decode_path("i8")
+
+
+@pytest.mark.parametrize("H,I", [(1024, 512), (1024, 1536), (2048, 1024)])
+@pytest.mark.parametrize("m", [1, 8])
+@pytest.mark.parametrize("nl", [1, 2])
+def test_layer_stack_cluster_counts(oracle, H, I, m, nl):
+    """One, two and three clusters (intermediate 512, 1024, 1536: one to three contributions per
+    accumulator word) and stacks whose final h sits in the second and third accumulator."""
+    layers, hl, lm, hlm, fn, hfn = build(H, I, 6000 + H + I + m)
+    layers, hl = layers[:nl], hl[:nl]
+    assert mq.decode_step_kernels(m, H, I, nl) == "fused"
+    h0 = mq.synth_bf16((m, H), 6100 + m + nl, 0.0, 1.0)
+    ids, _, h = (t.clone() for t in mq.DecodeStep(layers, fn, lm, m)(h0))
+    torch.cuda.synchronize()
+    assert mq.device_error() == 0
+    rids, _, rh = oracle.decode_step(u16(h0), hl, hfn, hlm)
+    assert max_rel_row_err(f32(h), rh) < 1e-4
+    assert np.array_equal(ids.cpu().numpy(), rids)
