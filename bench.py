@@ -15,7 +15,8 @@ memory (marlin_q4_tp_decode_step): strong scaling.
 least one second has been timed, each repeat bracketed by a barrier and a synchronize, the max over
 ranks per repeat, the median over repeats.  `e2e` repeats the measurement through the public API
 with the step's embeddings copied from pinned host memory and the token ids read back to the host
-every step.  `roofline` covers the step's dominant part, the MLP layers as they run inside the step
+every step (`marlin_q4.HostDecodeStep`: the two copies and the step replayed as one CUDA graph, then
+a synchronisation).  `roofline` covers the step's dominant part, the MLP layers as they run inside the step
 (at N = 1 one persistent kernel for all layers, at N > 1 two kernels per layer; per-layer time =
 (t(24 layers) - t(1 layer)) / 23, both CUDA-graph replays of the same public call; per rank at
 N > 1).  `extras.step_per_layer_kernels` times the N = 1 step on the per-layer kernels as well.  At N > 1 `parity` compares the sharded step's ids and h
@@ -239,7 +240,6 @@ def run_ours(args):
 
     step = make_step(layers, B)
     graph = capture(torch, lambda: step(h0))
-    out_ids = step.ids
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -278,22 +278,19 @@ def run_ours(args):
     h_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
     h_host.copy_(h0.cpu())
     ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    # marlin_q4.HostDecodeStep: the copy in, the step and the copy out as one graph per token
+    host_step = mq.HostDecodeStep(step, h_host, ids_host)
     for _ in range(3):
-        h0.copy_(h_host, non_blocking=True)
-        graph.replay()
-        ids_host.copy_(out_ids, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        host_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        h0.copy_(h_host, non_blocking=True)
-        graph.replay()
-        ids_host.copy_(out_ids, non_blocking=True)
-        torch.cuda.current_stream().synchronize()  # the host reads the token every step
+        host_step()  # H2D of the embeddings, the step, D2H of the ids, then the host waits for them
     e1.record()
     e1.synchronize()
     e2e_ms = max_over_ranks(torch, dist, [e0.elapsed_time(e1) / args.steps], dev)[0]
+    host_step.close()
     ids_run, h_run = step.ids.clone(), step.h.clone()
     del graph
     close(step)

@@ -286,6 +286,50 @@ class DecodeStep:
         return self.ids, self.best, self.h
 
 
+class HostDecodeStep:
+    """A decode step fed from, and read back into, pinned host buffers, for a serving loop whose
+    embeddings come from and whose tokens go to the host: the copy of the embedding rows to the
+    device, the step (a DecodeStep, or a tensor-parallel step with the same call) and the copy of
+    its ids back are captured once as one CUDA graph, so each token costs one graph launch and one
+    synchronisation instead of three stream operations and a synchronisation.
+
+    h_host: pinned bf16 [m, hidden], refilled by the caller before each call; ids_host: pinned int32
+    [m], valid when the call returns.  Both stay bound to the graph until close()."""
+
+    def __init__(self, step, h_host: torch.Tensor, ids_host: torch.Tensor):
+        m, hidden = step.m, step.hidden
+        if not (h_host.is_pinned() and ids_host.is_pinned()):
+            raise ValueError("h_host and ids_host must be pinned host tensors")
+        if h_host.dtype != torch.bfloat16 or tuple(h_host.shape) != (m, hidden):
+            raise ValueError(f"h_host must be bf16 [{m}, {hidden}]")
+        if ids_host.dtype != torch.int32 or ids_host.numel() != m:
+            raise ValueError(f"ids_host must be int32 [{m}]")
+        self.step, self.h_host, self.ids_host = step, h_host, ids_host
+        self.h0 = torch.empty((m, hidden), dtype=torch.bfloat16, device=step.ids.device)
+        side = torch.cuda.Stream(device=self.h0.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # one eager run first (library set-up outside the capture)
+            self._body()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        torch.cuda.current_stream().synchronize()
+
+    def _body(self):
+        self.h0.copy_(self.h_host, non_blocking=True)
+        self.step(self.h0)
+        self.ids_host.copy_(self.step.ids, non_blocking=True)
+
+    def __call__(self) -> torch.Tensor:
+        self.graph.replay()
+        torch.cuda.current_stream().synchronize()
+        return self.ids_host
+
+    def close(self):
+        self.graph = None
+
+
 class GreedyLoop:
     """run_decode_loop's greedy path (src/core/engine.cpp:79-94) on the device: per token, the
     embedding rows of the current ids from the tied Q4 table (embed_q4), one DecodeStep, and its ids

@@ -102,3 +102,13 @@ def test_python_front_end_refuses_cpu_tensors():
     import marlin_q4
     with pytest.raises(ValueError):
         marlin_q4.quantize_weight(torch.zeros(8, 64, dtype=torch.bfloat16))
+
+
+def test_host_decode_step_refuses_unpinned_buffers():
+    import types
+
+    import torch
+    import marlin_q4
+    fake = types.SimpleNamespace(m=2, hidden=64, ids=torch.zeros(2, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        marlin_q4.HostDecodeStep(fake, torch.zeros(2, 64, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.int32))

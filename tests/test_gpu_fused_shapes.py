@@ -82,3 +82,25 @@ def test_layer_stack_cluster_counts(oracle, H, I, m, nl):
     rids, _, rh = oracle.decode_step(u16(h0), hl, hfn, hlm)
     assert max_rel_row_err(f32(h), rh) < 1e-4
     assert np.array_equal(ids.cpu().numpy(), rids)
+
+
+def test_host_decode_step_matches_device_step():
+    """HostDecodeStep (copy in, step, copy out as one graph) returns the ids of DecodeStep for each
+    refill of its host buffer."""
+    H, m = 1024, 2
+    layers, hl, lm, hlm, fn, hfn = build(H, 4 * H, 7000)
+    h_host = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
+    ids_host = torch.empty(m, dtype=torch.int32).pin_memory()
+    hs = mq.HostDecodeStep(mq.DecodeStep(layers, fn, lm, m), h_host, ids_host)
+    ref = mq.DecodeStep(layers, fn, lm, m)
+    try:
+        for seed in (7100, 7101, 7102):
+            h0 = mq.synth_bf16((m, H), seed, 0.0, 1.0)
+            h_host.copy_(h0.cpu())
+            ids = hs().clone()
+            rids, _, _ = ref(h0)
+            torch.cuda.synchronize()
+            assert torch.equal(ids, rids.cpu())
+        assert mq.device_error() == 0
+    finally:
+        hs.close()
