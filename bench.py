@@ -492,8 +492,8 @@ def run_ours(args):
         "clocks": ck,
         "e2e": {"value": round(B / (e2e_ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * 4,
-                "path": "public API (CUDA graph of marlin_q4_decode_step / TP step) with pinned host embeddings in "
-                        "and token ids out every step, host sync per token"},
+                "path": "public API marlin_q4.HostDecodeStep (pinned host embeddings in, the step, token ids out, "
+                        "replayed as one CUDA graph) every step, host sync per token"},
         "gpu_launches": launches,
         "roofline": roof,
         "parity": parity,
