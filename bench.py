@@ -15,8 +15,9 @@ memory (marlin_q4_tp_decode_step): strong scaling.
 least one second has been timed, each repeat bracketed by a barrier and a synchronize, the max over
 ranks per repeat, the median over repeats.  `e2e` repeats the measurement through the public API
 with the step's embeddings copied from pinned host memory and the token ids read back to the host
-every step (`marlin_q4.HostDecodeStep`: the two copies and the step replayed as one CUDA graph, then
-a synchronisation).  `roofline` covers the step's dominant part, the MLP layers as they run inside the step
+every step (on one GPU through `marlin_q4.HostDecodeStep`: the two copies and the step replayed as
+one CUDA graph, then a synchronisation; at N > 1 the copies run as stream operations around the
+step's graph).  `roofline` covers the step's dominant part, the MLP layers as they run inside the step
 (at N = 1 one persistent kernel for all layers, at N > 1 two kernels per layer; per-layer time =
 (t(24 layers) - t(1 layer)) / 23, both CUDA-graph replays of the same public call; per rank at
 N > 1).  `extras.step_per_layer_kernels` times the N = 1 step on the per-layer kernels as well.  At N > 1 `parity` compares the sharded step's ids and h
@@ -278,8 +279,16 @@ def run_ours(args):
     h_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
     h_host.copy_(h0.cpu())
     ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
-    # marlin_q4.HostDecodeStep: the copy in, the step and the copy out as one graph per token
-    host_step = mq.HostDecodeStep(step, h_host, ids_host)
+    if world == 1:
+        # marlin_q4.HostDecodeStep: the copy in, the step and the copy out as one graph per token
+        host_step = mq.HostDecodeStep(step, h_host, ids_host)
+    else:
+        # tensor-parallel step: the copies as stream operations around the step's graph
+        def host_step():
+            h0.copy_(h_host, non_blocking=True)
+            graph.replay()
+            ids_host.copy_(step.ids, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
     for _ in range(3):
         host_step()
     barrier()
@@ -290,7 +299,8 @@ def run_ours(args):
     e1.record()
     e1.synchronize()
     e2e_ms = max_over_ranks(torch, dist, [e0.elapsed_time(e1) / args.steps], dev)[0]
-    host_step.close()
+    if world == 1:
+        host_step.close()
     ids_run, h_run = step.ids.clone(), step.h.clone()
     del graph
     close(step)
@@ -492,8 +502,10 @@ def run_ours(args):
         "clocks": ck,
         "e2e": {"value": round(B / (e2e_ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * 4,
-                "path": "public API marlin_q4.HostDecodeStep (pinned host embeddings in, the step, token ids out, "
-                        "replayed as one CUDA graph) every step, host sync per token"},
+                "path": ("public API marlin_q4.HostDecodeStep (pinned host embeddings in, the step, token ids out, "
+                         "replayed as one CUDA graph) every step, host sync per token" if world == 1 else
+                         "public API (CUDA graph of the TP step) with pinned host embeddings in and token ids out "
+                         "every step as stream copies, host sync per token")},
         "gpu_launches": launches,
         "roofline": roof,
         "parity": parity,
