@@ -291,7 +291,8 @@ class HostDecodeStep:
     embeddings come from and whose tokens go to the host: the copy of the embedding rows to the
     device, the step (a DecodeStep, or a tensor-parallel step with the same call) and the copy of
     its ids back are captured once as one CUDA graph, so each token costs one graph launch and one
-    synchronisation instead of three stream operations and a synchronisation.
+    synchronisation instead of three stream operations and a synchronisation.  The reference's decode
+    loop reads every token on the host the same way (`token.item()`, src/core/engine.cpp:80).
 
     h_host: pinned bf16 [m, hidden], refilled by the caller before each call; ids_host: pinned int32
     [m], valid when the call returns.  Both stay bound to the graph until close()."""
