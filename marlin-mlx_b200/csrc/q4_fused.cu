@@ -167,8 +167,8 @@ __device__ __forceinline__ ulonglong2 ld_relaxed_v2(const unsigned long long* p)
 
 // Eight accumulator words of each of rows 0..M-1 (at p + m * stride), waited for until each holds
 // `target` contributions (bounded; gives up on a timeout or an abort), as binary32.  The rows go in
-// batches of up to four: every pending row's words of a batch are requested before any of them is
-// checked, so a batch costs one round trip to L2 (8 rows: two, not eight).  The loads are relaxed;
+// batches of FUSED_POLL_ROWS: every pending row's words of a batch are requested before any of them
+// is checked, so a batch costs one round trip to L2 (8 rows: four, not eight).  The loads are relaxed;
 // the fence after them gives the words acquire order (and with them the adders' earlier reads of
 // the accumulator this CTA clears next).
 template <int MS>
