@@ -295,7 +295,8 @@ class HostDecodeStep:
     loop reads every token on the host the same way (`token.item()`, src/core/engine.cpp:80).
 
     h_host: pinned bf16 [m, hidden], refilled by the caller before each call; ids_host: pinned int32
-    [m], valid when the call returns.  Both stay bound to the graph until close()."""
+    [m], valid when the call returns.  Both stay bound to the graph until close().  The constructor
+    runs the step once, eagerly, on what h_host holds at that time (before the capture)."""
 
     def __init__(self, step, h_host: torch.Tensor, ids_host: torch.Tensor):
         m, hidden = step.m, step.hidden
