@@ -12,6 +12,7 @@
 #include "q4_misc.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 
@@ -19,9 +20,10 @@ namespace marlin {
 namespace {
 
 thread_local int t_last_cuda_error = 0;
-bool g_pdl = true;
-int g_step_kernels = MARLIN_Q4_STEP_FUSED;
-unsigned long long g_peer_wait_cycles = kPeerWaitDefaultCycles;
+// process-wide settings: set from any thread, read when a call is issued
+std::atomic<bool> g_pdl{true};
+std::atomic<int> g_step_kernels{MARLIN_Q4_STEP_FUSED};
+std::atomic<unsigned long long> g_peer_wait_cycles{kPeerWaitDefaultCycles};
 
 int cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return MARLIN_Q4_OK;

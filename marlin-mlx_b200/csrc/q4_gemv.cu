@@ -37,6 +37,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 
 namespace marlin {
 namespace {
@@ -757,7 +758,7 @@ uint32_t plan_unit(UnitArgs& a, int NT, int nmat, bool swz, int64_t M, bool norm
 
 }  // namespace
 
-int g_decode_path = kPathI8;
+std::atomic<int> g_decode_path{kPathI8};  // process-wide, set from any thread
 
 int decode_path() { return g_decode_path; }
 
