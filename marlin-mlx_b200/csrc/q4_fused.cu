@@ -900,7 +900,9 @@ cudaError_t fused_launch(const FusedArgs& a, int grid, uint32_t smem, bool pdl, 
 }
 
 // Whether `grid` CTAs in clusters of 8 can all be resident at once on the current device (the layer
-// waits need every CTA running).  Cached per device and activation width.
+// waits need every CTA running).  Cached per device and activation width: plan_fused fills shared
+// memory to within one ring stage of the limit at every hidden size, one CTA per SM, so the count
+// does not depend on the exact size.
 bool fused_coresident(int ntn, int grid, uint32_t smem) {
     static std::mutex mu;
     static int cache[64][3];  // [device][ntn index]: 0 unknown, else max active clusters + 1
